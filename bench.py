@@ -1,0 +1,414 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 Q8_0 hot path (one JSON line on rank 0).
+
+Headline metric: Q8_0 GEMV GB/s.  One step = the seven MiniCPM4 projection
+GEMVs (q/k/v/o 2048->2048/256/256/2048, gate/up 2048->6144, down 6144->2048;
+BASELINE config 2 shapes at M=1) for each of 28 layers: 196 launches over
+1,403,781,120 bytes of distinct Q8_0 weights (larger than the 126 MB L2, so no
+flush is needed between steps).  Algorithmic bytes per GEMV = N*K*34/32 +
+4*K + 4*N.  `value` replays a CUDA graph of the step with inputs resident in
+HBM; `e2e` goes through the C ABI with pinned host buffers: one H2D of every
+step input, the graph, one D2H of every output, all inside the timed region.
+
+--impl reference times the CPU restatement of ggml's Q8_0 mat-mul (the
+oracle; ggml itself is not buildable here) on the host cores on a bounded
+sample of the same workload.
+
+Multi-GPU (torchrun): each rank runs the same step on its own GPU (independent
+work, no collective on the data path); time is the max over ranks and value
+is the total bytes of all ranks / that time (weak scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "voxcpm-cpp_b200"), os.path.join(ROOT, "oracle")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+HIDDEN, NH, NKV, HD, FFN, LAYERS = 2048, 16, 2, 128, 6144, 28
+SHAPES = [  # (name, K, N, input slot)
+    ("q", HIDDEN, NH * HD, "a"), ("k", HIDDEN, NKV * HD, "a"), ("v", HIDDEN, NKV * HD, "a"),
+    ("o", NH * HD, HIDDEN, "o"), ("gate", HIDDEN, FFN, "a"), ("up", HIDDEN, FFN, "a"), ("down", FFN, HIDDEN, "d")]
+IN_LEN = {"a": HIDDEN, "o": NH * HD, "d": FFN}
+IN_OFF = {"a": 0, "o": HIDDEN, "d": HIDDEN + NH * HD}
+IN_PER_LAYER = HIDDEN + NH * HD + FFN
+OUT_PER_LAYER = sum(s[2] for s in SHAPES)
+# dram bytes per launch of the config-1 GEMV (N=6144, K=2048) from the ncu
+# capture summarised in profiles/gemv_q8_0_config1.md; None until captured.
+NCU_TRAFFIC_CONFIG1 = None
+
+
+def q8_bytes(K, N):
+    return N * K // 32 * 34
+
+
+def alg_bytes(K, N, M=1):
+    return q8_bytes(K, N) + 4 * K * M + 4 * N * M
+
+
+STEP_BYTES = LAYERS * sum(alg_bytes(K, N) for _, K, N, _ in SHAPES)
+
+
+def synth_q8_0(rng, N, K):
+    """GGUF Q8_0 bytes of a synthetic [N, K] weight: int8 quants uniform in
+    [-127, 127] and fp16 scales around those of N(0, 0.02) weights."""
+    nb = K // 32
+    blk = np.empty((N, nb, 34), np.uint8)
+    d = (0.02 * (2.1 + 0.3 * rng.standard_normal((N, nb))) / 127.0).astype(np.float16)
+    blk[:, :, 0:2] = d.view(np.uint8).reshape(N, nb, 2)
+    blk[:, :, 2:] = rng.integers(-127, 128, size=(N, nb, 32), dtype=np.int8).view(np.uint8)
+    return blk.reshape(N, nb * 34)
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling during the timed region (read-only queries)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.t:
+                self.t.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_baseline(seconds=12.0, layers=2):
+    """The oracle's Q8_0 mat-mul (ggml-CPU semantics: activation quantized to
+    Q8_0, int8 block dots, OpenMP over rows) on all host cores, over the
+    projection set of `layers` layers, repeated for ~`seconds`."""
+    import oracle as O
+    rng = np.random.default_rng(1)
+    ws = [(K, N, synth_q8_0(rng, N, K)) for _ in range(layers) for _, K, N, _ in SHAPES]
+    xs = {K: rng.standard_normal((1, K)).astype(np.float32) for K in (HIDDEN, FFN)}
+    threads = os.cpu_count() or 1
+    L = O.lib()
+    ys = {N: np.zeros((1, N), np.float32) for _, _, N, _ in SHAPES}
+    # warm-up pass
+    for K, N, W in ws:
+        L.vo_matmul(O.TYPE_Q8_0, W.ctypes.data, K, N, xs[K].ctypes.data, 1, ys[N].ctypes.data, O.QRULE_X86, threads)
+    done, nbytes, t0 = 0, 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        for K, N, W in ws:
+            L.vo_matmul(O.TYPE_Q8_0, W.ctypes.data, K, N, xs[K].ctypes.data, 1, ys[N].ctypes.data, O.QRULE_X86,
+                        threads)
+            nbytes += alg_bytes(K, N)
+        done += 1
+    dt = time.perf_counter() - t0
+    return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{done} passes over the 7 projection GEMVs of {layers} layers "
+                      f"({layers * 7} Q8_0 weights, {sum(q8_bytes(K, N) for K, N, _ in ws) / 1e6:.1f} MB), "
+                      f"{dt:.1f} s; CPU restatement of ggml's Q8_0 path (ggml itself not buildable here)"}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def config_block(n):
+    return {"workload": "BASELINE config 2 projection set at M=1, Q8_0, 28 MiniCPM4 layers per step",
+            "shapes": {s[0]: [s[1], s[2]] for s in SHAPES}, "layers": LAYERS, "M": 1,
+            "bytes_per_step": STEP_BYTES, "l2": "inputs larger than L2 (1.40 GB distinct weights per step)",
+            "parallelism": f"independent replicas x{n}"}
+
+
+# ------------------------------------------------------------- reference
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    steps_t = []
+    base = None
+    for _ in range(max(1, args.steps if args.steps <= 3 else 3)):
+        base = cpu_baseline(seconds=min(20.0, 6.0 + 2.0 * args.steps))
+        steps_t.append(base["value"])
+    v = float(np.median(steps_t))
+    line = {"impl": "reference", "metric": "Q8_0 GEMV GB/s", "value": v, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": config_block(world),
+            "cpu_baseline": dict(base, value=v),
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------- B200
+def run_b200(args, rank, world, local_rank):
+    import torch
+    import vcpm_b200 as vb
+
+    torch.cuda.set_device(local_rank)
+    ctx = vb.Context(local_rank)
+    rng = np.random.default_rng(1234 + rank)
+
+    # weights: 28 layers x 7 projections, registered (uploaded + repacked)
+    host_layers = []
+    weights = []
+    for l in range(LAYERS):
+        hl = {}
+        for name, K, N, _ in SHAPES:
+            hb = synth_q8_0(rng, N, K)
+            hl[name] = hb
+            weights.append((name, K, N, ctx.weight(vb.TYPE_Q8_0, K, N, hb)))
+        host_layers.append(hl)
+    X = torch.randn(LAYERS * IN_PER_LAYER, dtype=torch.float32, device="cuda")
+    Y = torch.zeros(LAYERS * OUT_PER_LAYER, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+
+    def enqueue_step():
+        xo, yo = X.data_ptr(), Y.data_ptr()
+        i = 0
+        for l in range(LAYERS):
+            off = 0
+            for name, K, N, slot in SHAPES:
+                w = weights[i][3]
+                ctx.matmul(w, xo + 4 * (l * IN_PER_LAYER + IN_OFF[slot]), 1,
+                           yo + 4 * (l * OUT_PER_LAYER + off))
+                off += N
+                i += 1
+
+    ctx.graph_begin()
+    enqueue_step()
+    g = ctx.graph_end()
+
+    # config-1 shape alone: the 56 gate/up weights [2048 -> 6144]
+    c1 = [(w, K, N) for (name, K, N, w) in weights if name in ("gate", "up")]
+    ctx.graph_begin()
+    for w, K, N in c1:
+        ctx.matmul(w, X.data_ptr(), 1, Y.data_ptr())
+    g1 = ctx.graph_end()
+
+    ev0, ev1 = ctx.event(), ctx.event()
+
+    def timed(fn, k):
+        ctx.record(ev0)
+        for _ in range(k):
+            fn()
+        ctx.record(ev1)
+        return ctx.elapsed_ms(ev0, ev1)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    for _ in range(args.warmup):
+        ctx.graph_launch(g)
+    ctx.sync()
+    barrier()
+    ctx.sync()
+    vis = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip().isdigit()]
+    clocks = ClockSampler(int(vis[local_rank]) if local_rank < len(vis) else local_rank)
+    clocks.start()
+    ms = timed(lambda: ctx.graph_launch(g), args.steps)
+    ctx.sync()
+    barrier()
+    ck = clocks.stop()
+
+    # config-1 per-launch timing (same kernel, one shape)
+    for _ in range(3):
+        ctx.graph_launch(g1)
+    ms1 = timed(lambda: ctx.graph_launch(g1), max(5, args.steps // 4))
+    per_launch_ms = ms1 / (max(5, args.steps // 4) * len(c1))
+    c1_gbs = alg_bytes(2048, 6144) / (per_launch_ms * 1e-3) / 1e9
+
+    # e2e through the C ABI: pinned host inputs -> graph -> pinned host outputs
+    hx = torch.randn(LAYERS * IN_PER_LAYER, dtype=torch.float32).pin_memory()
+    hy = torch.zeros(LAYERS * OUT_PER_LAYER, dtype=torch.float32).pin_memory()
+    h2d, d2h = hx.numel() * 4, hy.numel() * 4
+
+    def e2e_step():
+        ctx.memcpy_h2d(X, hx, h2d)
+        ctx.graph_launch(g)
+        ctx.memcpy_d2h(hy, Y, d2h)
+
+    for _ in range(max(3, args.warmup // 2)):
+        e2e_step()
+    ctx.sync()
+    barrier()
+    ms_e2e = timed(e2e_step, args.steps)
+    ctx.sync()
+
+    # max over ranks
+    t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms, ms_e2e = float(t[0]), float(t[1])
+
+    value = world * STEP_BYTES * args.steps / (ms * 1e-3) / 1e9
+    e2e_value = world * STEP_BYTES * args.steps / (ms_e2e * 1e-3) / 1e9
+    peak, peak_kind = load_peaks()
+    per_gpu = value / world
+
+    decode = None
+    if not args.no_decode and world == 1:
+        decode = decode_bench(ctx, host_layers, args)
+
+    base = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
+
+    if rank == 0:
+        line = {
+            "metric": "Q8_0 GEMV GB/s", "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic (uniform int8 quants, fp16 scales of N(0,0.02) "
+                                                         "weights; activations N(0,1))",
+            "config": config_block(world),
+            "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
+                         "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+                         "kernel": "vb::gemv_q8_kernel<1,2,4>", "traffic": NCU_TRAFFIC_CONFIG1,
+                         "traffic_unit": "bytes per config-1 launch",
+                         "achieved_config1": c1_gbs, "config1_us_per_launch": per_launch_ms * 1e3,
+                         "config1_alg_bytes": alg_bytes(2048, 6144)},
+            "cpu_baseline": base,
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": ms_e2e / args.steps, "path": "vb_memcpy_h2d + vb_graph_launch + vb_memcpy_d2h"},
+            "clocks": ck,
+            "gpu_launches": args.steps * LAYERS * len(SHAPES),
+        }
+        if decode:
+            line["decode"] = decode
+        print(json.dumps(line), flush=True)
+    ctx.graph_destroy(g)
+    ctx.graph_destroy(g1)
+    for *_, w in weights:
+        w.release()
+    ctx.close()
+    return 0
+
+
+def decode_bench(ctx, host_layers, args):
+    """Secondary metric: MiniCPM4 28-layer decode tokens/s (
+    256-token prefill, then single-token steps against a bf16 KV cache of 512
+    slots) through vb_lm_forward, using the same synthetic Q8_0 weights."""
+    import torch
+    import vcpm_b200 as vb
+    rng = np.random.default_rng(7)
+    layers = []
+    for hl in host_layers:
+        L = dict(hl)
+        L["attn_norm"] = (1.0 + 0.02 * rng.standard_normal(HIDDEN)).astype(np.float32)
+        L["ffn_norm"] = (1.0 + 0.02 * rng.standard_normal(HIDDEN)).astype(np.float32)
+        layers.append(L)
+    fn = (1.0 + 0.02 * rng.standard_normal(HIDDEN)).astype(np.float32)
+    cfg = vb.LMConfig(HIDDEN, NH, NKV, HD, FFN, LAYERS, 1e-5, 10000.0, 0, 0.0, vb.TYPE_Q8_0)
+    lm = vb.LM(ctx, cfg, layers, fn)
+    kv = vb.KV(ctx, lm, 1, 512)
+    P, D = 256, args.decode_steps
+    x = (torch.randn(P + D, HIDDEN, device="cuda") * 0.5).to(torch.bfloat16).float()
+    out = torch.zeros(P + D, HIDDEN, device="cuda")
+    torch.cuda.synchronize()
+    ev0, ev1 = ctx.event(), ctx.event()
+    ctx.record(ev0)
+    lm.forward(kv, [0], [0], P, x[:P], out[:P])
+    ctx.record(ev1)
+    prefill_ms = ctx.elapsed_ms(ev0, ev1)
+    # decode: a few untimed steps, then the timed ones
+    warm = 4
+    for i in range(warm):
+        lm.forward(kv, [0], [P + i], 1, x[P + i:P + i + 1], out[P + i:P + i + 1])
+    ctx.sync()
+    ctx.record(ev0)
+    for i in range(warm, D):
+        lm.forward(kv, [0], [P + i], 1, x[P + i:P + i + 1], out[P + i:P + i + 1])
+    ctx.record(ev1)
+    ms = ctx.elapsed_ms(ev0, ev1)
+    n = D - warm
+    kv.close()
+    lm.close()
+    return {"metric": "LM decode tokens/s (28-layer MiniCPM4, Q8_0, batch 1)", "tokens_per_s": n / (ms * 1e-3),
+            "ms_per_token": ms / n, "prefill_ms_256": prefill_ms, "kv_positions": [P, P + D],
+            "weight_bytes_per_token": 1_403_781_120}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--decode-steps", type=int, default=64)
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if world > 1:
+        import datetime
+        import torch
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local_rank))
+    try:
+        return run_b200(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,285 @@
+/*
+ * vcpm_b200.h -- C ABI of the B200 (sm_100a) quantized-weight hot path of
+ * VoxCPM-C.
+ *
+ * This library replaces, for the Q8_0/F16 mat-muls and the attention glue
+ * between them, the ggml dispatch of the reference runtime
+ * (src/ggml_backend.c, src/ggml_backend.h:33-59) and the weight offload of
+ * src/model_loader.c (vcpm_model_offload, src/model_loader.h:169).  The C11
+ * host code and include/voxcpm.h of the reference stay unchanged; a
+ * replacement src/ggml_backend.c routes matching graph nodes here.
+ *
+ * Conventions
+ *   - Plain C types only; device buffers are passed as plain pointers that
+ *     the caller obtained from vb_malloc (or any cudaMalloc'd memory of the
+ *     context's device).
+ *   - Return codes mirror vcpm_status (include/voxcpm.h:14-23): 0 OK,
+ *     1 INVALID_ARG, 5 BACKEND, 6 OOM, 7 NOT_IMPLEMENTED.  Nothing aborts;
+ *     vb_last_error() holds the message of the last failure.
+ *   - One vb_ctx = one device + one CUDA stream, used by one host thread at a
+ *     time; multi-GPU hosts create one context per device.  All work is
+ *     enqueued asynchronously on the context stream; vb_sync() waits.
+ *   - Weight shapes use ggml order: a weight of ggml shape [K, N] is N rows
+ *     of K elements (src/minicpm4.c:5-8).  Activations are row-major [M][K]
+ *     (one token per row) and mat-mul results [M][N], both fp32.
+ */
+#ifndef VCPM_B200_H
+#define VCPM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (include/voxcpm.h:14-23). */
+enum {
+    VB_OK = 0,
+    VB_ERR_INVALID_ARG = 1,
+    VB_ERR_BACKEND = 5,
+    VB_ERR_OOM = 6,
+    VB_ERR_NOT_IMPLEMENTED = 7
+};
+
+/* Weight types: ggml type ids (GGML_TYPE_F32/F16/Q8_0). */
+enum { VB_TYPE_F32 = 0, VB_TYPE_F16 = 1, VB_TYPE_Q8_0 = 8 };
+
+/* Q8_0 activation rounding rule.  VB_QRULE_X86 is ggml-CPU's x86 SIMD rule
+ * (id = 127/amax, round half to even), the default; VB_QRULE_REF is ggml's
+ * reference rule (id = 1/d, round half away from zero). */
+enum { VB_QRULE_X86 = 0, VB_QRULE_REF = 1 };
+
+/* Output flags. */
+#define VB_OUT_BF16 1u   /* round results F32->BF16->F32 (src/minicpm4.c:39-42) */
+
+typedef struct vb_ctx vb_ctx;
+typedef struct vb_weight_s *vb_weight;
+
+/* ------------------------------------------------------------------ */
+/* Context: replaces vcpm_backend_init / vcpm_backend_free            */
+/* (src/ggml_backend.h:33-37).                                        */
+/* ------------------------------------------------------------------ */
+int vb_device_count(int *n);
+int vb_create(int device, vb_ctx **out);
+void vb_destroy(vb_ctx *ctx);
+const char *vb_last_error(const vb_ctx *ctx);
+/* Waits for all work on the context stream (the synchronous return of
+ * vcpm_backend_compute_graph, src/ggml_backend.h:58-59). */
+int vb_sync(vb_ctx *ctx);
+/* Use an external cudaStream_t (passed as void*); NULL restores the
+ * context's own stream. */
+int vb_set_stream(vb_ctx *ctx, void *cuda_stream);
+void *vb_get_stream(vb_ctx *ctx);
+/* Q8_0 activation rule for every later call on this context. */
+int vb_set_qrule(vb_ctx *ctx, int rule);
+
+/* CUDA-graph capture of a fixed sequence of calls on the context stream:
+ * the device-side counterpart of the reference's persistent CFM graph
+ * (src/gen_step.c:482-580), which builds a graph once and replays it.
+ * Between begin and end only launches are recorded (no allocation, no
+ * synchronisation); replay re-runs them on the same buffers. */
+typedef struct vb_graph_s *vb_graph;
+int vb_graph_begin(vb_ctx *ctx);
+int vb_graph_end(vb_ctx *ctx, vb_graph *out);
+int vb_graph_launch(vb_ctx *ctx, vb_graph g);
+void vb_graph_destroy(vb_graph g);
+
+/* CUDA events on the context stream, for timing replays from hosts that
+ * do not link cudart: record, then elapsed milliseconds between two. */
+typedef struct vb_event_s *vb_event;
+int vb_event_create(vb_ctx *ctx, vb_event *out);
+int vb_event_record(vb_ctx *ctx, vb_event e);
+int vb_event_elapsed_ms(vb_event start, vb_event stop, float *ms);
+void vb_event_destroy(vb_event e);
+
+/* Device / pinned-host memory for hosts that do not link cudart. */
+int vb_malloc(vb_ctx *ctx, size_t bytes, void **dptr);
+int vb_free(vb_ctx *ctx, void *dptr);
+int vb_host_alloc(vb_ctx *ctx, size_t bytes, void **hptr);
+int vb_host_free(vb_ctx *ctx, void *hptr);
+int vb_memcpy_h2d(vb_ctx *ctx, void *dst, const void *src, size_t bytes);
+int vb_memcpy_d2h(vb_ctx *ctx, void *dst, const void *src, size_t bytes);
+int vb_memcpy_d2d(vb_ctx *ctx, void *dst, const void *src, size_t bytes);
+int vb_memset(vb_ctx *ctx, void *dst, int value, size_t bytes);
+
+/* ------------------------------------------------------------------ */
+/* Weights: replaces vcpm_model_offload (src/model_loader.h:169,      */
+/* src/model_loader.c:615-700).  The GGUF bytes (34-byte Q8_0 blocks,  */
+/* fp16 or fp32 rows) are uploaded and repacked once; the host buffer */
+/* stays owned by the caller, the device copy by the context.         */
+/* ------------------------------------------------------------------ */
+int vb_weight_register(vb_ctx *ctx, int type, int64_t K, int64_t N,
+                       const void *host, size_t nbytes, vb_weight *out);
+int vb_weight_release(vb_ctx *ctx, vb_weight w);
+int vb_weight_info(vb_weight w, int *type, int64_t *K, int64_t *N,
+                   size_t *device_bytes);
+
+/* ------------------------------------------------------------------ */
+/* Ops on device pointers                                             */
+/* ------------------------------------------------------------------ */
+
+/* ggml_mul_mat(W, x) on a registered Q8_0/F16/F32 weight
+ * (src/projections.h:24-29 and every call site of src/minicpm4.c,
+ * src/locdit.c, src/gen_step.c): y[m][n] = sum_k W[n][k] x[m][k] with
+ * ggml-CPU operand conversion (Q8_0: x quantized to Q8_0 per row; F16: x
+ * rounded to fp16).  flags: VB_OUT_BF16.  Optional bias (F32 [N], device,
+ * added before rounding, dit_add_bias_2d src/locdit.c:192-207). */
+int vb_matmul(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, float *y,
+              unsigned flags);
+int vb_matmul_bias(vb_ctx *ctx, vb_weight w, const float *x, int64_t M,
+                   const float *bias, float *y, unsigned flags);
+
+/* Q8_0 quantization of M rows of K floats into GGUF blocks (34 bytes per
+ * 32 values) -- the activation conversion inside every Q8_0 ggml_mul_mat. */
+int vb_quantize_q8_0(vb_ctx *ctx, const float *x, int64_t K, int64_t M,
+                     void *blocks, int rule);
+/* Q8_0 block dequantization (src/model_loader.c:317-331,
+ * src/gen_prompt.c:106-125), n values. */
+int vb_dequantize_q8_0(vb_ctx *ctx, const void *blocks, int64_t n, float *y);
+
+/* vcpm_rms_norm (src/minicpm4.c:132-152): with w != NULL and VB_OUT_BF16,
+ * y = bf16(bf16(rms_norm(x)) * w); with w == NULL and flags == 0 the plain
+ * ggml_rms_norm.  rows of n floats. */
+int vb_rms_norm(vb_ctx *ctx, const float *x, const float *w, float *y,
+                int64_t n, int64_t rows, float eps, unsigned flags);
+/* In-place F32->BF16->F32 (minicpm_bf16_round). */
+int vb_bf16_round(vb_ctx *ctx, float *x, int64_t n);
+/* y = bf16(a + scale*b) (block residual, src/minicpm4.c:496-528); scale 1
+ * skips the multiply as the reference does. */
+int vb_residual_add(vb_ctx *ctx, const float *a, const float *b, float scale,
+                    float *y, int64_t n, unsigned flags);
+/* SwiGLU middle of vcpm_mlp (src/minicpm4.c:441-456):
+ * y = bf16(bf16(silu(bf16(g))) * bf16(u)) with VB_OUT_BF16, else silu(g)*u. */
+int vb_swiglu(vb_ctx *ctx, const float *g, const float *u, float *y,
+              int64_t n, unsigned flags);
+/* NEOX rope_ext with the LongRoPE short factors when head_dim == 128
+ * (vcpm_rope, src/minicpm4.c:165-223), in place on x[T][n_heads][head_dim];
+ * pos: device int32 [T]; VB_OUT_BF16 rounds the result. */
+int vb_rope_neox(vb_ctx *ctx, float *x, int head_dim, int n_heads, int T,
+                 const int32_t *pos, float theta, unsigned flags);
+/* vcpm_fsq_quantize (src/fsq.c:16-29): round(tanh(x)*s)/s, in place. */
+int vb_fsq_quantize(vb_ctx *ctx, float *x, int64_t n, float quant_scale);
+
+/* Grouped-query attention over a BF16 K/V store (gqa_group_attn and the
+ * per-token loop of vcpm_attention, src/minicpm4.c:232-248,338-412).
+ * q: fp32 [T][n_heads][head_dim]; k, v: bf16 [n_kv_heads][n_rows][head_dim];
+ * token t attends to rows row_start[t] .. row_start[t]+kv_len[t]-1
+ * (row_start, kv_len: device int32 [T]); out: fp32 [T][n_heads*head_dim].
+ * Scores are scaled by 1/sqrt(head_dim) and soft-maxed in fp32. */
+int vb_attention(vb_ctx *ctx, const float *q, const uint16_t *k,
+                 const uint16_t *v, int n_rows, int T, int n_heads,
+                 int n_kv_heads, int head_dim, const int32_t *row_start,
+                 const int32_t *kv_len, float *out);
+/* KV-cache append (src/minicpm4.c:299-320): writes bf16(k), bf16(v) of T
+ * tokens (fp32 [T][n_kv_heads][head_dim]) into rows dst_row[t] of the
+ * bf16 stores [n_kv_heads][n_rows][head_dim]. */
+int vb_kv_write(vb_ctx *ctx, const float *k, const float *v, uint16_t *kc,
+                uint16_t *vc, int n_rows, int T, int n_kv_heads, int head_dim,
+                const int32_t *dst_row);
+
+/* ------------------------------------------------------------------ */
+/* Transformer stacks (MiniCPM4 TSLM / RALM / LocDiT blocks / LocEnc) */
+/* vcpm_minicpm4_block / vcpm_minicpm4_forward (src/minicpm4.c:467-572)*/
+/* ------------------------------------------------------------------ */
+typedef struct {
+    int hidden, n_heads, n_kv_heads, head_dim, ffn, n_layers;
+    float eps;
+    float rope_theta;
+    int no_rope;         /* RALM: 1 (src/gen_prompt.c:162) */
+    float scale_depth;   /* residual scale = scale_depth/sqrt(n_layers) if > 0 */
+    int wtype;           /* VB_TYPE_Q8_0 / VB_TYPE_F16 / VB_TYPE_F32 */
+} vb_lm_config;
+
+/* Host pointers in GGUF storage; norms are F32 [hidden]. */
+typedef struct {
+    const void *q, *k, *v, *o, *gate, *up, *down;
+    const float *attn_norm, *ffn_norm;
+} vb_layer_host;
+
+typedef struct vb_lm vb_lm;
+typedef struct vb_kv vb_kv;
+
+int vb_lm_create(vb_ctx *ctx, const vb_lm_config *cfg,
+                 const vb_layer_host *layers, const float *final_norm,
+                 vb_lm **out);
+void vb_lm_destroy(vb_ctx *ctx, vb_lm *lm);
+size_t vb_lm_weight_bytes(const vb_lm *lm);
+
+/* BF16 KV cache for n_seqs independent sequences of `capacity` positions
+ * (vcpm_kv_cache_init, src/minicpm4.c:93-122; bf16 is exact because the
+ * reference rounds K/V to bf16 before caching, src/minicpm4.c:221-222). */
+int vb_kv_create(vb_ctx *ctx, const vb_lm *lm, int n_seqs, int capacity,
+                 vb_kv **out);
+void vb_kv_destroy(vb_ctx *ctx, vb_kv *kv);
+int vb_kv_reset(vb_kv *kv, int seq);
+int vb_kv_used(const vb_kv *kv, int seq);
+
+/* Causal forward of T tokens for each of n sequences (rows of x are
+ * [n][T][hidden], device fp32).  seq: host int32 [n] cache slots; pos: host
+ * int32 [n] RoPE position of each sequence's first token (the reference's
+ * `pos`, src/minicpm4.c:536-572).  K/V are appended at each sequence's
+ * n_used.  out: [n][T][hidden] after the final norm.
+ * `final_norm` NULL keeps the final-norm output; hidden states are bf16. */
+int vb_lm_forward(vb_ctx *ctx, vb_lm *lm, vb_kv *kv, int n, const int32_t *seq,
+                  const int32_t *pos, int T, const float *x, float *out);
+/* Bidirectional forward (no_causal = 1, no cache; LocDiT/LocEnc blocks,
+ * src/locdit.c:321-370, src/locenc.c:89-113) of n independent segments of
+ * T tokens, RoPE positions 0..T-1 in each; no final norm. h in place. */
+int vb_lm_forward_noncausal(vb_ctx *ctx, vb_lm *lm, int n, int T, float *h);
+
+/* ------------------------------------------------------------------ */
+/* LocDiT estimator and the CFM loop                                   */
+/* (src/locdit.c:140-400, src/gen_step.c:472-652, src/cfm_solver.c)   */
+/* ------------------------------------------------------------------ */
+typedef struct {
+    int hidden, n_layers, n_heads, n_kv_heads, ffn, head_dim;
+    int feat_dim, patch;
+    float eps;
+    int wtype;
+} vb_dit_config;
+
+typedef struct {
+    const void *in_proj, *cond_proj, *out_proj;
+    const float *in_bias, *cond_bias, *out_bias;
+    const void *t_w1, *t_w2, *dt_w1, *dt_w2;
+    const float *t_b1, *t_b2, *dt_b1, *dt_b2;
+    const float *norm;
+    const vb_layer_host *layers;
+} vb_dit_host;
+
+typedef struct vb_dit vb_dit;
+
+int vb_dit_create(vb_ctx *ctx, const vb_dit_config *cfg, const vb_dit_host *w,
+                  vb_dit **out);
+void vb_dit_destroy(vb_ctx *ctx, vb_dit *dit);
+size_t vb_dit_weight_bytes(const vb_dit *dit);
+
+/* vcpm_locdit_forward for n items: x, cond [n][patch][feat] (device);
+ * t, dt: host float [n]; mu: device [n][2*hidden] or NULL; has_mu: host
+ * int [n] (0 = unconditional branch, zero mu tokens) or NULL (all 1 when mu
+ * is given).  out: device [n][patch][feat]. */
+int vb_dit_forward(vb_ctx *ctx, vb_dit *dit, int n, const float *x,
+                   const float *cond, const float *t, const float *dt,
+                   const float *mu, const int *has_mu, float *out);
+
+/* The Euler CFM solve of vcpm_gen_step (src/gen_step.c:472-652) for n
+ * utterances at once: sway t-schedule with the CFG-Zero* skipped steps,
+ * cond+uncond evaluated as one batch, CFG-Zero* blend and bf16 Euler update
+ * on the device.  mu: device [n][2*hidden] (NULL = no guidance);
+ * cond, x: device [n][patch][feat]; x holds the noise on entry and the
+ * patch on return. */
+int vb_cfm_solve(vb_ctx *ctx, vb_dit *dit, int n, const float *mu,
+                 const float *cond, float *x, int n_steps, float cfg_value);
+
+/* Host helpers restated from the reference for its callers. */
+float vb_cfm_sway_t_bf16(int step, int n_steps);   /* src/cfm_solver.c:27-37 */
+int vb_cfm_zero_star_steps(int n_steps);           /* src/gen_step.c:50-54 */
+void vb_cfm_noise(uint64_t seed, int ar_step, float *x, int n); /* src/gen_step.c:409-431 */
+int vb_round_cache_capacity(int required, int model_max); /* src/gen_init.c:115-127 */
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VCPM_B200_H */

@@ -1,0 +1,86 @@
+"""Seeded synthetic weights and inputs shared by the parity tests.
+
+Weights are N(0, 0.02) (norms N(1, 0.02)), drawn with the oracle's
+SplitMix64/Box-Muller generator and stored in GGUF layout: Q8_0 blocks
+quantized with ggml's weight rule (tools/quantize.c:292), F16 rows, or F32.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+import oracle as O
+
+_seed = [1000]
+
+
+def next_seed():
+    _seed[0] += 1
+    return _seed[0]
+
+
+def normal(n, std=1.0, mean=0.0, seed=None):
+    return O.fill_normal(seed if seed is not None else next_seed(), mean, std, int(np.prod(n))).reshape(n)
+
+
+def weight(wtype, N, K, std=0.02):
+    """GGUF storage of a random [N, K] weight."""
+    return O.make_weight(wtype, normal((N, K), std), O.QRULE_REF)
+
+
+def layer(wtype, hidden, n_heads, n_kv, head_dim, ffn):
+    qd, kd = n_heads * head_dim, n_kv * head_dim
+    return {
+        "q": weight(wtype, qd, hidden), "k": weight(wtype, kd, hidden), "v": weight(wtype, kd, hidden),
+        "o": weight(wtype, hidden, qd), "gate": weight(wtype, ffn, hidden), "up": weight(wtype, ffn, hidden),
+        "down": weight(wtype, hidden, ffn),
+        "attn_norm": normal(hidden, 0.02, 1.0), "ffn_norm": normal(hidden, 0.02, 1.0),
+    }
+
+
+def oracle_layer(wtype, L):
+    return O.Layer(wtype, L["q"], L["k"], L["v"], L["o"], L["gate"], L["up"], L["down"], L["attn_norm"],
+                   L["ffn_norm"])
+
+
+def dit_tensors(wtype, hidden, feat):
+    return {
+        "in_proj": weight(wtype, hidden, feat), "cond_proj": weight(wtype, hidden, feat),
+        "out_proj": weight(wtype, feat, hidden),
+        "in_bias": normal(hidden, 0.02), "cond_bias": normal(hidden, 0.02), "out_bias": normal(feat, 0.02),
+        "t_w1": weight(wtype, hidden, hidden), "t_w2": weight(wtype, hidden, hidden),
+        "dt_w1": weight(wtype, hidden, hidden), "dt_w2": weight(wtype, hidden, hidden),
+        "t_b1": normal(hidden, 0.02), "t_b2": normal(hidden, 0.02),
+        "dt_b1": normal(hidden, 0.02), "dt_b2": normal(hidden, 0.02),
+        "norm": normal(hidden, 0.02, 1.0),
+    }
+
+
+# ------------------------------------------------------------- tolerances
+def rel_l2(y, r):
+    y = np.asarray(y, np.float64).ravel()
+    r = np.asarray(r, np.float64).ravel()
+    return float(np.linalg.norm(y - r) / max(np.linalg.norm(r), 1e-30))
+
+
+def assert_matmul_close(y, r, tol=1e-3):
+    """Pre-rounding fp32 mat-mul outputs: |y - r| <= tol * max(|r|, rms(r))
+    elementwise (only the fp32 accumulation order differs)."""
+    y = np.asarray(y, np.float64)
+    r = np.asarray(r, np.float64)
+    rms = float(np.sqrt(np.mean(r * r))) + 1e-30
+    err = np.abs(y - r) / np.maximum(np.abs(r), rms)
+    assert float(err.max()) <= tol, f"max rel err {err.max():.3e} > {tol}"
+
+
+def assert_layer_close(y, r, tol=1e-3):
+    """bf16-rounded layer outputs: relative L2 <= tol and every element within
+    one bf16 ulp of its own magnitude plus tol * rms (a rounding flip when the
+    pre-round value straddles a bf16 boundary)."""
+    y = np.asarray(y, np.float64)
+    r = np.asarray(r, np.float64)
+    rl = rel_l2(y, r)
+    assert rl <= tol, f"relative L2 {rl:.3e} > {tol}"
+    rms = float(np.sqrt(np.mean(r * r))) + 1e-30
+    bound = np.abs(r) * 2.0 ** -7 + tol * rms
+    worst = float((np.abs(y - r) - bound).max())
+    assert worst <= 0, f"element beyond one bf16 ulp: excess {worst:.3e}"

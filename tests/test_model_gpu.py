@@ -1,0 +1,213 @@
+"""GPU parity of the transformer stacks, LocDiT and the CFM loop against the
+CPU oracle, on reduced sizes that the oracle finishes in seconds.
+
+Gate: layer outputs (bf16 hidden states) within relative L2 1e-3 and every
+element within one bf16 ulp (+1e-3 rms) of the oracle: the fp32 mat-mul
+accumulation order differs, so a pre-round value that straddles a bf16
+boundary may round the other way."""
+import numpy as np
+import pytest
+
+import oracle as O
+import synth as S
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+import vcpm_b200 as vb  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    c = vb.Context(0)
+    yield c
+    c.close()
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+SMALL = dict(hidden=512, n_heads=4, n_kv=2, head_dim=128, ffn=1024, n_layers=2)
+
+
+def build_lm(ctx, wtype, no_rope=0, with_norm=True, **kw):
+    c = dict(SMALL, **kw)
+    layers = [S.layer(wtype, c["hidden"], c["n_heads"], c["n_kv"], c["head_dim"], c["ffn"])
+              for _ in range(c["n_layers"])]
+    fn = S.normal(c["hidden"], 0.02, 1.0) if with_norm else None
+    vcfg = vb.LMConfig(c["hidden"], c["n_heads"], c["n_kv"], c["head_dim"], c["ffn"], c["n_layers"], 1e-5, 10000.0,
+                       no_rope, 0.0, wtype)
+    ocfg = O.LMConfig(c["hidden"], c["n_heads"], c["n_kv"], c["head_dim"], c["ffn"], c["n_layers"], 1e-5, 10000.0,
+                      no_rope, 0.0)
+    lm = vb.LM(ctx, vcfg, layers, fn)
+    olayers = [S.oracle_layer(wtype, L) for L in layers]
+    return c, lm, ocfg, olayers, fn
+
+
+@pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_F16])
+@pytest.mark.parametrize("no_rope", [0, 1])
+def test_causal_prefill_then_decode(ctx, wtype, no_rope):
+    c, lm, ocfg, olayers, fn = build_lm(ctx, wtype, no_rope)
+    H = c["hidden"]
+    kv = vb.KV(ctx, lm, 1, 64)
+    ocache = O.KVCache(c["n_layers"], 64, c["n_kv"], c["head_dim"])
+    T = 7
+    x = O.bf16_round(S.normal((T, H)))
+    out = torch.zeros((T, H), dtype=torch.float32, device="cuda")
+    xd = dev(x)
+    torch.cuda.synchronize()
+    lm.forward(kv, [0], [0], T, xd, out)
+    ctx.sync()
+    ref = O.lm_forward(ocfg, olayers, fn, ocache, x, T, 0)
+    S.assert_layer_close(host(out), ref)
+    pos = T
+    for step in range(3):
+        x1 = O.bf16_round(S.normal((1, H)))
+        o1 = torch.zeros((1, H), dtype=torch.float32, device="cuda")
+        xd1 = dev(x1)
+        torch.cuda.synchronize()
+        lm.forward(kv, [0], [pos], 1, xd1, o1)
+        ctx.sync()
+        r1 = O.lm_forward(ocfg, olayers, fn, ocache, x1, 1, pos)
+        S.assert_layer_close(host(o1), r1)
+        pos += 1
+    assert kv.used(0) == T + 3 == ocache.n_used(0)
+    kv.close()
+    lm.close()
+
+
+def test_batched_decode_matches_per_sequence(ctx):
+    wtype = O.TYPE_Q8_0
+    c, lm, ocfg, olayers, fn = build_lm(ctx, wtype)
+    H = c["hidden"]
+    kv = vb.KV(ctx, lm, 3, 128)
+    lens = [5, 9, 70]          # the 70-token prompt spans two attention chunks
+    caches = [O.KVCache(c["n_layers"], 128, c["n_kv"], c["head_dim"]) for _ in lens]
+    for s, L in enumerate(lens):
+        x = O.bf16_round(S.normal((L, H)))
+        out = torch.zeros((L, H), dtype=torch.float32, device="cuda")
+        xd = dev(x)
+        torch.cuda.synchronize()
+        lm.forward(kv, [s], [0], L, xd, out)
+        ctx.sync()
+        S.assert_layer_close(host(out), O.lm_forward(ocfg, olayers, fn, caches[s], x, L, 0))
+    # one batched decode step over the three sequences (slots given out of order)
+    order = [2, 0, 1]
+    xb = O.bf16_round(S.normal((3, H)))
+    ob = torch.zeros((3, H), dtype=torch.float32, device="cuda")
+    xbd = dev(xb)
+    torch.cuda.synchronize()
+    lm.forward(kv, order, [lens[s] for s in order], 1, xbd, ob)
+    ctx.sync()
+    got = host(ob)
+    for i, s in enumerate(order):
+        ref = O.lm_forward(ocfg, olayers, fn, caches[s], xb[i:i + 1], 1, lens[s])
+        S.assert_layer_close(got[i:i + 1], ref)
+    for s, L in enumerate(lens):
+        assert kv.used(s) == L + 1
+    kv.close()
+    lm.close()
+
+
+def test_kv_capacity_overflow_is_an_error(ctx):
+    c, lm, *_ = build_lm(ctx, O.TYPE_Q8_0, n_layers=1)
+    kv = vb.KV(ctx, lm, 1, 8)
+    x = torch.zeros((9, c["hidden"]), dtype=torch.float32, device="cuda")
+    with pytest.raises(vb.VBError) as e:
+        lm.forward(kv, [0], [0], 9, x, x)
+    assert e.value.code == vb.VB_ERR_INVALID_ARG
+    assert kv.used(0) == 0
+    kv.close()
+    lm.close()
+
+
+def test_noncausal_segments(ctx):
+    c, lm, ocfg, olayers, _ = build_lm(ctx, O.TYPE_Q8_0, with_norm=False)
+    H, T, n = c["hidden"], 11, 3
+    h = O.bf16_round(S.normal((n, T, H)))
+    hd = dev(h)
+    torch.cuda.synchronize()
+    lm.forward_noncausal(n, T, hd)
+    ctx.sync()
+    got = host(hd)
+    for i in range(n):
+        ref = h[i].copy()
+        for L in olayers:
+            ref = O.block(ocfg, L, ref, T, 0, 1)
+        S.assert_layer_close(got[i], ref)
+    lm.close()
+
+
+# ----------------------------------------------------------------- LocDiT
+DIT = dict(hidden=512, n_layers=2, n_heads=4, n_kv=2, ffn=1024, head_dim=128, feat=64, patch=4)
+
+
+def build_dit(ctx, wtype):
+    d = DIT
+    t = S.dit_tensors(wtype, d["hidden"], d["feat"])
+    layers = [S.layer(wtype, d["hidden"], d["n_heads"], d["n_kv"], d["head_dim"], d["ffn"])
+              for _ in range(d["n_layers"])]
+    vcfg = vb.DiTConfig(d["hidden"], d["n_layers"], d["n_heads"], d["n_kv"], d["ffn"], d["head_dim"], d["feat"],
+                        d["patch"], 1e-5, wtype)
+    ocfg = O.DiTConfig(d["hidden"], d["n_layers"], d["n_heads"], d["n_kv"], d["ffn"], d["head_dim"], d["feat"],
+                       d["patch"], 1e-5)
+    gpu = vb.DiT(ctx, vcfg, t, layers)
+    ora = O.DiT(ocfg, wtype, t, [S.oracle_layer(wtype, L) for L in layers])
+    return gpu, ora
+
+
+@pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_F16])
+def test_dit_forward_cond_and_uncond(ctx, wtype):
+    gpu, ora = build_dit(ctx, wtype)
+    d = DIT
+    n = 3
+    x = O.bf16_round(S.normal((n, d["patch"], d["feat"])))
+    cond = O.bf16_round(S.normal((n, d["patch"], d["feat"])))
+    mu = S.normal((n, 2 * d["hidden"]))
+    ts = [O.cfm_sway_t(s, 10) for s in (1, 4, 9)]
+    out = torch.zeros((n, d["patch"], d["feat"]), dtype=torch.float32, device="cuda")
+    xd, cd, md = dev(x), dev(cond), dev(mu)
+    has = [1, 0, 1]
+    torch.cuda.synchronize()
+    gpu.forward(n, xd, cd, ts, [0.0] * n, md, out, has_mu=has)
+    ctx.sync()
+    got = host(out)
+    for i in range(n):
+        ref = ora.forward(x[i], cond[i], ts[i], 0.0, mu[i] if has[i] else None)
+        S.assert_layer_close(got[i], ref)
+    gpu.close()
+
+
+def test_cfm_solve_vs_oracle(ctx):
+    gpu, ora = build_dit(ctx, O.TYPE_Q8_0)
+    d = DIT
+    n = 2
+    mu = S.normal((n, 2 * d["hidden"]))
+    cond = O.bf16_round(S.normal((n, d["patch"], d["feat"])))
+    x0 = np.stack([O.cfm_noise(42, i, d["patch"] * d["feat"]).reshape(d["patch"], d["feat"]) for i in range(n)])
+    xd, cd, md = dev(x0), dev(cond), dev(mu)
+    torch.cuda.synchronize()
+    gpu.cfm_solve(n, md, cd, xd, 10, 2.0)
+    ctx.sync()
+    got = host(xd)
+    for i in range(n):
+        ref = ora.cfm_solve(mu[i], cond[i], x0[i], 10, 2.0)
+        assert S.rel_l2(got[i], ref) <= 1e-2, S.rel_l2(got[i], ref)
+    # no-guidance path (cfg = 1): one DiT evaluation per step
+    xd2 = dev(x0)
+    torch.cuda.synchronize()
+    gpu.cfm_solve(n, md, cd, xd2, 10, 1.0)
+    ctx.sync()
+    got2 = host(xd2)
+    for i in range(n):
+        ref = ora.cfm_solve(mu[i], cond[i], x0[i], 10, 1.0)
+        assert S.rel_l2(got2[i], ref) <= 1e-2
+    gpu.close()

@@ -1,0 +1,54 @@
+// vb_kernels.cuh -- launchers shared between the translation units.
+#pragma once
+
+#include "vb_common.cuh"
+
+namespace vb {
+
+int init_kernels(vb_ctx *ctx);
+
+// weights (vb_quant.cu)
+int weight_upload(vb_ctx *ctx, int type, int64_t K, int64_t N, const void *host, size_t nbytes, vb_weight *out);
+void weight_free(vb_ctx *ctx, vb_weight w);
+
+// Output mapping of a mat-mul: logical row m of the [M][N] result lands in
+// row  (m / seg) * seg_stride + seg_off + (m % seg)  of y (leading dim ldy).
+// With seg = M, seg_stride = 0, seg_off = 0, ldy = N it is the plain layout.
+struct MatmulOut {
+    float *y = nullptr;
+    const float *bias = nullptr;   // [N] or null
+    unsigned flags = 0;            // VB_OUT_BF16
+    int64_t ldy = 0;
+    int64_t seg = 0, seg_stride = 0, seg_off = 0;
+};
+
+// Input mapping: logical row m reads x row (m % x_mod) (x_mod = M: plain),
+// leading dimension ldx.
+int launch_matmul(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx, int64_t x_mod,
+                  const MatmulOut &out);
+
+int launch_quantize_q8_0(vb_ctx *ctx, const float *x, int64_t K, int64_t M, void *blocks, int rule);
+int launch_dequantize_q8_0(vb_ctx *ctx, const void *blocks, int64_t n, float *y);
+
+// elementwise (vb_elem.cu)
+int launch_rms_norm(vb_ctx *ctx, const float *x, const float *w, float *y, int64_t n, int64_t rows, float eps,
+                    unsigned flags, int64_t ldx = 0, int64_t ldy = 0);
+int launch_bf16_round(vb_ctx *ctx, float *x, int64_t n);
+int launch_residual(vb_ctx *ctx, const float *a, const float *b, float scale, float *y, int64_t n, unsigned flags);
+int launch_swiglu(vb_ctx *ctx, const float *g, const float *u, float *y, int64_t n, unsigned flags);
+int launch_fsq(vb_ctx *ctx, float *x, int64_t n, float s);
+// In-place NEOX rotation of x (row t at x + t*ldx, n_heads x head_dim),
+// positions pos[t]; table cs [max_pos][head_dim].
+int launch_rope(vb_ctx *ctx, float *x, int64_t ldx, int head_dim, int n_heads, int T, const int32_t *pos,
+                const float *cs, unsigned flags);
+int launch_kv_write(vb_ctx *ctx, const float *k, const float *v, int64_t ldkv, uint16_t *kc, uint16_t *vc,
+                    int n_rows, int T, int n_kv, int head_dim, const int32_t *dst_row);
+int launch_fill(vb_ctx *ctx, float *x, float v, int64_t n);
+
+// attention (vb_attn.cu)
+int launch_attention(vb_ctx *ctx, const float *q, int64_t ldq, const uint16_t *k, const uint16_t *v, int n_rows,
+                     int T, int n_heads, int n_kv, int head_dim, const int32_t *row_start, const int32_t *kv_len,
+                     int max_kv_len, float *out, int64_t ldo);
+size_t attention_scratch_bytes(int T, int n_heads, int head_dim, int max_kv_len);
+
+}  // namespace vb

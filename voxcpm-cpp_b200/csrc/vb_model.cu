@@ -1,0 +1,693 @@
+// vb_model.cu -- transformer stacks, LocDiT and the CFM loop on the device.
+//
+// Host orchestration mirrors the reference graph builders op for op:
+//   vcpm_minicpm4_block / _forward   src/minicpm4.c:467-572
+//   vcpm_attention                   src/minicpm4.c:250-428
+//   vcpm_mlp                         src/minicpm4.c:432-463
+//   vcpm_locdit_forward              src/locdit.c:216-400
+//   CFM Euler loop + CFG-Zero*       src/gen_step.c:472-652, src/cfm_solver.c:27-93
+// Weights are registered once (repacked), q/k/v and gate/up are fused row-wise
+// into one mat-mul each (every output is the same per-row dot product, so
+// values are unchanged).  The KV cache is bf16 [layer][n_kv][seq*cap][hd].
+#include "vb_common.cuh"
+#include "vb_kernels.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+namespace vb {
+
+static size_t row_bytes(int type, int64_t K) {
+    return type == VB_TYPE_Q8_0 ? (size_t)(K / QK) * Q8_BYTES : (size_t)K * (type == VB_TYPE_F16 ? 2u : 4u);
+}
+
+struct LayerDev {
+    vb_weight qkv = nullptr, o = nullptr, gu = nullptr, down = nullptr;
+    float *attn_norm = nullptr, *ffn_norm = nullptr;
+};
+
+// ----------------------------------------------------------- small kernels
+// y = bf16(silu(x)) on bf16-valued x (time MLP, src/locdit.c:152-153).
+__global__ void silu_bf16_kernel(float *x, int64_t n) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) x[i] = bf16r(silu_f(bf16r(x[i])));
+}
+
+// Fused-layout SwiGLU: row m of gu holds [gate(ffn) | up(ffn)].
+__global__ void swiglu_rows_kernel(const float *gu, float *y, int64_t rows, int64_t ffn) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * ffn) return;
+    const int64_t m = i / ffn, j = i % ffn;
+    const float g = bf16r(gu[m * 2 * ffn + j]);
+    const float u = bf16r(gu[m * 2 * ffn + ffn + j]);
+    y[i] = bf16r(__fmul_rn(bf16r(silu_f(g)), u));
+}
+
+// dst row r <- src row (r / seg) * seg_stride + seg_off + r % seg.
+__global__ void gather_rows_kernel(const float *src, float *dst, int64_t rows, int64_t width, int64_t seg,
+                                   int64_t seg_stride, int64_t seg_off) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * width) return;
+    const int64_t r = i / width, c = i % width;
+    dst[i] = src[((r / seg) * seg_stride + seg_off + r % seg) * width + c];
+}
+
+// DiT sequence head: rows 0,1 <- mu halves (or zeros), row 2 <- bf16(tf + dtf).
+__global__ void dit_head_kernel(float *seq, int64_t T, int64_t H, const float *mu, const int *has_mu,
+                                const float *tf, const float *dtf, int t_shared) {
+    const int64_t i = blockIdx.x;
+    float *s = seq + i * T * H;
+    const float *tfi = tf + (t_shared ? 0 : i * H);
+    const float *dfi = dtf + (t_shared ? 0 : i * H);
+    const bool m = mu && has_mu[i];
+    for (int64_t j = threadIdx.x; j < 2 * H; j += blockDim.x) s[j] = m ? mu[i * 2 * H + j] : 0.0f;
+    for (int64_t j = threadIdx.x; j < H; j += blockDim.x) s[2 * H + j] = bf16r(__fadd_rn(tfi[j], dfi[j]));
+}
+
+// One CTA per utterance: CFG-Zero* blend (src/cfm_solver.c:65-93) and the
+// bf16 Euler update x = bf16(x + bf16(dt*v)) (src/gen_step.c:626-629).
+// The dot products sum bf16 values in double; such sums are exact, so the
+// result does not depend on the reduction order.
+__global__ void cfm_update_kernel(float *x, const float *vel, int n, int len, int use_cfg, float cfg_value,
+                                  float step_size) {
+    const int i = blockIdx.x;
+    const float *vc = vel + (int64_t)i * len;
+    const float *vu = vel + (int64_t)(n + i) * len;
+    float *xi = x + (int64_t)i * len;
+    __shared__ double red[2][32];
+    __shared__ float st_s;
+    if (use_cfg) {
+        double dot = 0.0, sq = 0.0;
+        for (int j = threadIdx.x; j < len; j += blockDim.x) {
+            const float p = bf16r(vc[j]), q = bf16r(vu[j]);
+            dot += (double)bf16r(__fmul_rn(p, q));
+            sq += (double)bf16r(__fmul_rn(q, q));
+        }
+        dot = warp_sum_d(dot);
+        sq = warp_sum_d(sq);
+        if ((threadIdx.x & 31) == 0) { red[0][threadIdx.x >> 5] = dot; red[1][threadIdx.x >> 5] = sq; }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double a = 0.0, b = 0.0;
+            for (int w = 0; w < (int)(blockDim.x >> 5); w++) { a += red[0][w]; b += red[1][w]; }
+            const float dot_b = bf16r(__double2float_rn(a));
+            const float norm_b = bf16r(__fadd_rn(__double2float_rn(b), 1.0e-8f));
+            st_s = bf16r(__fdiv_rn(dot_b, norm_b));
+        }
+        __syncthreads();
+    }
+    const float st = use_cfg ? st_s : 0.0f;
+    const float cfg_b = bf16r(cfg_value);
+    for (int j = threadIdx.x; j < len; j += blockDim.x) {
+        float v;
+        if (use_cfg) {
+            const float p = bf16r(vc[j]), q = bf16r(vu[j]);
+            const float qs = bf16r(__fmul_rn(q, st));
+            const float delta = bf16r(__fsub_rn(p, qs));
+            const float guide = bf16r(__fmul_rn(cfg_b, delta));
+            v = bf16r(__fadd_rn(qs, guide));
+        } else {
+            v = vc[j];
+        }
+        const float d = bf16r(__fmul_rn(step_size, v));
+        xi[j] = bf16r(__fadd_rn(xi[j], d));
+    }
+}
+
+int init_model_kernels(vb_ctx *) { return VB_OK; }
+
+// -------------------------------------------------------------- workspace
+struct Carve {
+    uint8_t *p;
+    size_t off = 0;
+    explicit Carve(void *base) : p((uint8_t *)base) {}
+    template <class T>
+    T *take(size_t n) {
+        off = (off + 255) & ~(size_t)255;
+        T *r = (T *)(p + off);
+        off += n * sizeof(T);
+        return r;
+    }
+};
+
+static size_t align256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+}  // namespace vb
+
+using namespace vb;
+
+struct vb_lm {
+    vb_lm_config cfg;
+    std::vector<LayerDev> layers;
+    float *final_norm = nullptr;
+    size_t weight_bytes = 0;
+};
+
+struct vb_kv {
+    int n_seqs = 0, capacity = 0, n_layers = 0, n_kv = 0, head_dim = 0;
+    uint16_t *k = nullptr, *v = nullptr;   // [layer][n_kv][n_seqs*capacity][head_dim]
+    std::vector<int> n_used;
+    size_t layer_elems() const { return (size_t)n_kv * n_seqs * capacity * head_dim; }
+};
+
+static int upload_f32(vb_ctx *ctx, const float *h, size_t n, float **d) {
+    if (!h) { *d = nullptr; return VB_OK; }
+    VB_CHECK(ctx, cudaMalloc(d, n * 4));
+    VB_CHECK(ctx, cudaMemcpy(*d, h, n * 4, cudaMemcpyHostToDevice));
+    return VB_OK;
+}
+
+// Concatenate the rows of several GGUF weights that share K into one buffer.
+static int register_concat(vb_ctx *ctx, int type, int64_t K, std::initializer_list<std::pair<const void *, int64_t>> parts,
+                           vb_weight *out) {
+    const size_t rb = row_bytes(type, K);
+    int64_t N = 0;
+    for (auto &p : parts) N += p.second;
+    std::vector<uint8_t> buf((size_t)N * rb);
+    size_t off = 0;
+    for (auto &p : parts) {
+        if (!p.first) return set_error(ctx, VB_ERR_INVALID_ARG, "missing layer weight");
+        memcpy(buf.data() + off, p.first, (size_t)p.second * rb);
+        off += (size_t)p.second * rb;
+    }
+    return weight_upload(ctx, type, K, N, buf.data(), buf.size(), out);
+}
+
+static void lm_free(vb_ctx *ctx, vb_lm *lm) {
+    if (!lm) return;
+    for (auto &L : lm->layers) {
+        weight_free(ctx, L.qkv);
+        weight_free(ctx, L.o);
+        weight_free(ctx, L.gu);
+        weight_free(ctx, L.down);
+        cudaFree(L.attn_norm);
+        cudaFree(L.ffn_norm);
+    }
+    cudaFree(lm->final_norm);
+    delete lm;
+}
+
+extern "C" int vb_lm_create(vb_ctx *ctx, const vb_lm_config *cfg, const vb_layer_host *layers,
+                            const float *final_norm, vb_lm **out) {
+    if (!ctx || !cfg || !layers || !out) return VB_ERR_INVALID_ARG;
+    *out = nullptr;
+    const vb_lm_config &c = *cfg;
+    if (c.hidden <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.n_heads % c.n_kv_heads || c.head_dim <= 0 ||
+        c.head_dim % 2 || c.ffn <= 0 || c.n_layers <= 0)
+        return set_error(ctx, VB_ERR_INVALID_ARG, "vb_lm_create: bad configuration");
+    VB_CHECK(ctx, cudaSetDevice(ctx->device));
+    vb_lm *lm = new vb_lm();
+    lm->cfg = c;
+    lm->layers.resize(c.n_layers);
+    const int64_t H = c.hidden, QD = (int64_t)c.n_heads * c.head_dim, KD = (int64_t)c.n_kv_heads * c.head_dim;
+    int rc = VB_OK;
+    for (int l = 0; l < c.n_layers && rc == VB_OK; l++) {
+        const vb_layer_host &w = layers[l];
+        LayerDev &L = lm->layers[l];
+        rc = register_concat(ctx, c.wtype, H, {{w.q, QD}, {w.k, KD}, {w.v, KD}}, &L.qkv);
+        if (!rc) rc = register_concat(ctx, c.wtype, QD, {{w.o, H}}, &L.o);
+        if (!rc) rc = register_concat(ctx, c.wtype, H, {{w.gate, c.ffn}, {w.up, c.ffn}}, &L.gu);
+        if (!rc) rc = register_concat(ctx, c.wtype, c.ffn, {{w.down, H}}, &L.down);
+        if (!rc) rc = upload_f32(ctx, w.attn_norm, H, &L.attn_norm);
+        if (!rc) rc = upload_f32(ctx, w.ffn_norm, H, &L.ffn_norm);
+        if (!rc) lm->weight_bytes += L.qkv->device_bytes + L.o->device_bytes + L.gu->device_bytes + L.down->device_bytes;
+    }
+    if (!rc && final_norm) rc = upload_f32(ctx, final_norm, H, &lm->final_norm);
+    if (rc) {
+        lm_free(ctx, lm);
+        return rc;
+    }
+    *out = lm;
+    return VB_OK;
+}
+
+extern "C" void vb_lm_destroy(vb_ctx *ctx, vb_lm *lm) { lm_free(ctx, lm); }
+extern "C" size_t vb_lm_weight_bytes(const vb_lm *lm) { return lm ? lm->weight_bytes : 0; }
+
+extern "C" int vb_kv_create(vb_ctx *ctx, const vb_lm *lm, int n_seqs, int capacity, vb_kv **out) {
+    if (!ctx || !lm || !out || n_seqs <= 0 || capacity <= 0) return VB_ERR_INVALID_ARG;
+    *out = nullptr;
+    vb_kv *kv = new vb_kv();
+    kv->n_seqs = n_seqs;
+    kv->capacity = capacity;
+    kv->n_layers = lm->cfg.n_layers;
+    kv->n_kv = lm->cfg.n_kv_heads;
+    kv->head_dim = lm->cfg.head_dim;
+    kv->n_used.assign(n_seqs, 0);
+    const size_t bytes = kv->layer_elems() * kv->n_layers * 2u;
+    if (fault_injected("alloc") || cudaMalloc(&kv->k, bytes) != cudaSuccess || cudaMalloc(&kv->v, bytes) != cudaSuccess) {
+        cudaFree(kv->k);
+        delete kv;
+        return set_error(ctx, VB_ERR_OOM, "KV cache allocation of 2 x %zu bytes failed", bytes);
+    }
+    cudaMemsetAsync(kv->k, 0, bytes, ctx->stream);
+    cudaMemsetAsync(kv->v, 0, bytes, ctx->stream);
+    *out = kv;
+    return VB_OK;
+}
+
+extern "C" void vb_kv_destroy(vb_ctx *ctx, vb_kv *kv) {
+    if (!kv) return;
+    if (ctx) cudaStreamSynchronize(ctx->stream);
+    cudaFree(kv->k);
+    cudaFree(kv->v);
+    delete kv;
+}
+
+extern "C" int vb_kv_reset(vb_kv *kv, int seq) {
+    if (!kv || seq < -1 || seq >= kv->n_seqs) return VB_ERR_INVALID_ARG;
+    if (seq < 0) std::fill(kv->n_used.begin(), kv->n_used.end(), 0);
+    else kv->n_used[seq] = 0;
+    return VB_OK;
+}
+
+extern "C" int vb_kv_used(const vb_kv *kv, int seq) {
+    if (!kv || seq < 0 || seq >= kv->n_seqs) return -1;
+    return kv->n_used[seq];
+}
+
+namespace vb {
+
+// Per-call token tables (device int32): rope position, KV destination row,
+// first visible row and visible length of every token.
+struct TokenTables {
+    int32_t *pos, *dst, *start, *len;
+    int max_len;
+};
+
+// The layer loop shared by causal and bidirectional stacks.  h: [M][H]
+// residual stream (in place).  K/V go to (kc, vc) rows tt.dst.
+static int run_layers(vb_ctx *ctx, vb_lm *lm, int M, float *h, const TokenTables &tt, uint16_t *kc_base,
+                      uint16_t *vc_base, size_t kv_layer_elems, int kv_rows, Carve &cv) {
+    const vb_lm_config &c = lm->cfg;
+    const int64_t H = c.hidden, QD = (int64_t)c.n_heads * c.head_dim, KD = (int64_t)c.n_kv_heads * c.head_dim;
+    const int64_t QKV = QD + 2 * KD;
+    float *xn = cv.take<float>((size_t)M * H);
+    float *qkv = cv.take<float>((size_t)M * QKV);
+    float *att = cv.take<float>((size_t)M * QD);
+    float *a = cv.take<float>((size_t)M * H);
+    float *gu = cv.take<float>((size_t)M * 2 * c.ffn);
+    float *act = cv.take<float>((size_t)M * c.ffn);
+    float scale = 1.0f;
+    if (c.scale_depth > 0.0f && c.n_layers > 0) scale = c.scale_depth / sqrtf((float)c.n_layers);
+    const float *cs = nullptr;
+    if (!c.no_rope) {
+        const RopeTable *rt = rope_table(ctx, c.head_dim, c.rope_theta, c.head_dim == 128, tt.max_len + 1);
+        if (!rt) return VB_ERR_OOM;
+        cs = rt->d_cs;
+    }
+    int rc;
+    for (int l = 0; l < c.n_layers; l++) {
+        LayerDev &L = lm->layers[l];
+        uint16_t *kc = kc_base + (size_t)l * kv_layer_elems;
+        uint16_t *vc = vc_base + (size_t)l * kv_layer_elems;
+        if ((rc = launch_rms_norm(ctx, h, L.attn_norm, xn, H, M, c.eps, VB_OUT_BF16))) return rc;
+        MatmulOut o;
+        o.y = qkv;
+        o.flags = VB_OUT_BF16;
+        if ((rc = launch_matmul(ctx, L.qkv, xn, M, 0, 0, o))) return rc;
+        if (!c.no_rope) {
+            if ((rc = launch_rope(ctx, qkv, QKV, c.head_dim, c.n_heads, M, tt.pos, cs, VB_OUT_BF16))) return rc;
+            if ((rc = launch_rope(ctx, qkv + QD, QKV, c.head_dim, c.n_kv_heads, M, tt.pos, cs, VB_OUT_BF16))) return rc;
+        }
+        if ((rc = launch_kv_write(ctx, qkv + QD, qkv + QD + KD, QKV, kc, vc, kv_rows, M, c.n_kv_heads, c.head_dim,
+                                  tt.dst)))
+            return rc;
+        if ((rc = launch_attention(ctx, qkv, QKV, kc, vc, kv_rows, M, c.n_heads, c.n_kv_heads, c.head_dim, tt.start,
+                                   tt.len, tt.max_len, att, QD)))
+            return rc;
+        o.y = a;
+        if ((rc = launch_matmul(ctx, L.o, att, M, 0, 0, o))) return rc;
+        if ((rc = launch_residual(ctx, h, a, scale, h, (int64_t)M * H, VB_OUT_BF16))) return rc;
+        if ((rc = launch_rms_norm(ctx, h, L.ffn_norm, xn, H, M, c.eps, VB_OUT_BF16))) return rc;
+        o.y = gu;
+        if ((rc = launch_matmul(ctx, L.gu, xn, M, 0, 0, o))) return rc;
+        int64_t ne = (int64_t)M * c.ffn;
+        swiglu_rows_kernel<<<(unsigned)((ne + 255) / 256), 256, 0, ctx->stream>>>(gu, act, M, c.ffn);
+        VB_LAUNCH_CHECK(ctx, "swiglu_rows");
+        o.y = a;
+        if ((rc = launch_matmul(ctx, L.down, act, M, 0, 0, o))) return rc;
+        if ((rc = launch_residual(ctx, h, a, scale, h, (int64_t)M * H, VB_OUT_BF16))) return rc;
+    }
+    return VB_OK;
+}
+
+static size_t layer_ws_bytes(const vb_lm_config &c, int M) {
+    const int64_t H = c.hidden, QD = (int64_t)c.n_heads * c.head_dim, KD = (int64_t)c.n_kv_heads * c.head_dim;
+    size_t b = 0;
+    b += align256((size_t)M * H * 4) * 2;
+    b += align256((size_t)M * (QD + 2 * KD) * 4);
+    b += align256((size_t)M * QD * 4);
+    b += align256((size_t)M * 2 * c.ffn * 4);
+    b += align256((size_t)M * c.ffn * 4);
+    return b + 4096;
+}
+
+static int upload_tables(vb_ctx *ctx, Carve &cv, int M, const std::vector<int32_t> &host4, TokenTables &tt) {
+    int32_t *d = cv.take<int32_t>((size_t)4 * M);
+    VB_CHECK(ctx, cudaMemcpyAsync(d, host4.data(), (size_t)4 * M * 4, cudaMemcpyHostToDevice, ctx->stream));
+    tt.pos = d;
+    tt.dst = d + M;
+    tt.start = d + 2 * M;
+    tt.len = d + 3 * M;
+    return VB_OK;
+}
+
+}  // namespace vb
+
+extern "C" int vb_lm_forward(vb_ctx *ctx, vb_lm *lm, vb_kv *kv, int n, const int32_t *seq, const int32_t *pos, int T,
+                             const float *x, float *out) {
+    if (!ctx || !lm || !kv || n <= 0 || !seq || !pos || T <= 0 || !x || !out) return VB_ERR_INVALID_ARG;
+    const vb_lm_config &c = lm->cfg;
+    if (kv->n_layers != c.n_layers || kv->n_kv != c.n_kv_heads || kv->head_dim != c.head_dim)
+        return set_error(ctx, VB_ERR_INVALID_ARG, "vb_lm_forward: KV cache shape does not match the stack");
+    const int M = n * T;
+    std::vector<int32_t> tab((size_t)4 * M);
+    int max_len = 1;
+    for (int i = 0; i < n; i++) {
+        const int s = seq[i];
+        if (s < 0 || s >= kv->n_seqs) return set_error(ctx, VB_ERR_INVALID_ARG, "vb_lm_forward: bad sequence slot");
+        for (int j = 0; j < i; j++)
+            if (seq[j] == s) return set_error(ctx, VB_ERR_INVALID_ARG, "vb_lm_forward: duplicate sequence slot");
+        const int used = kv->n_used[s];
+        if (used + T > kv->capacity)
+            return set_error(ctx, VB_ERR_INVALID_ARG, "vb_lm_forward: KV cache full (%d + %d > %d)", used, T,
+                             kv->capacity);
+        for (int t = 0; t < T; t++) {
+            const int m = i * T + t;
+            tab[m] = pos[i] + t;
+            tab[M + m] = s * kv->capacity + used + t;
+            tab[2 * M + m] = s * kv->capacity;
+            tab[3 * M + m] = used + t + 1;
+        }
+        max_len = std::max(max_len, used + T);
+        if (!c.no_rope) max_len = std::max(max_len, pos[i] + T);
+    }
+    const int64_t H = c.hidden;
+    int rc = ws_reserve(ctx, layer_ws_bytes(c, M) + align256((size_t)M * H * 4) + align256((size_t)16 * M) + 4096);
+    if (rc) return rc;
+    Carve cv(ctx->ws.ptr);
+    TokenTables tt;
+    if ((rc = upload_tables(ctx, cv, M, tab, tt))) return rc;
+    tt.max_len = max_len;
+    float *h = cv.take<float>((size_t)M * H);
+    VB_CHECK(ctx, cudaMemcpyAsync(h, x, (size_t)M * H * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+    // attention visible lengths never exceed used+T; max_len only sizes grids
+    int kv_max = 1;
+    for (int i = 0; i < n; i++) kv_max = std::max(kv_max, kv->n_used[seq[i]] + T);
+    TokenTables tl = tt;
+    tl.max_len = kv_max;
+    if (!c.no_rope) {
+        // rope table must cover every position used
+        if (!rope_table(ctx, c.head_dim, c.rope_theta, c.head_dim == 128, max_len + 1)) return VB_ERR_OOM;
+    }
+    rc = run_layers(ctx, lm, M, h, tl, kv->k, kv->v, kv->layer_elems(), kv->n_seqs * kv->capacity, cv);
+    if (rc) return rc;
+    if (lm->final_norm) rc = launch_rms_norm(ctx, h, lm->final_norm, out, H, M, c.eps, VB_OUT_BF16);
+    else VB_CHECK(ctx, cudaMemcpyAsync(out, h, (size_t)M * H * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+    if (rc) return rc;
+    for (int i = 0; i < n; i++) kv->n_used[seq[i]] += T;
+    return VB_OK;
+}
+
+extern "C" int vb_lm_forward_noncausal(vb_ctx *ctx, vb_lm *lm, int n, int T, float *h) {
+    if (!ctx || !lm || n <= 0 || T <= 0 || !h) return VB_ERR_INVALID_ARG;
+    const vb_lm_config &c = lm->cfg;
+    const int M = n * T;
+    std::vector<int32_t> tab((size_t)4 * M);
+    for (int m = 0; m < M; m++) {
+        tab[m] = m % T;
+        tab[M + m] = m;
+        tab[2 * M + m] = (m / T) * T;
+        tab[3 * M + m] = T;
+    }
+    const size_t kv_elems = (size_t)c.n_kv_heads * M * c.head_dim;
+    int rc = ws_reserve(ctx, layer_ws_bytes(c, M) + 2 * align256(kv_elems * 2) + align256((size_t)16 * M) + 4096);
+    if (rc) return rc;
+    Carve cv(ctx->ws.ptr);
+    TokenTables tt;
+    if ((rc = upload_tables(ctx, cv, M, tab, tt))) return rc;
+    tt.max_len = T;
+    uint16_t *kc = cv.take<uint16_t>(kv_elems);
+    uint16_t *vc = cv.take<uint16_t>(kv_elems);
+    return run_layers(ctx, lm, M, h, tt, kc, vc, 0, M, cv);
+}
+
+// ================================================================== LocDiT
+struct vb_dit {
+    vb_dit_config cfg;
+    vb_weight in_proj = nullptr, cond_proj = nullptr, out_proj = nullptr;
+    vb_weight t_w1 = nullptr, t_w2 = nullptr, dt_w1 = nullptr, dt_w2 = nullptr;
+    float *in_bias = nullptr, *cond_bias = nullptr, *out_bias = nullptr;
+    float *t_b1 = nullptr, *t_b2 = nullptr, *dt_b1 = nullptr, *dt_b2 = nullptr, *norm = nullptr;
+    vb_lm *blocks = nullptr;
+    size_t weight_bytes = 0;
+};
+
+static void dit_free(vb_ctx *ctx, vb_dit *d) {
+    if (!d) return;
+    for (vb_weight w : {d->in_proj, d->cond_proj, d->out_proj, d->t_w1, d->t_w2, d->dt_w1, d->dt_w2})
+        weight_free(ctx, w);
+    for (float *p : {d->in_bias, d->cond_bias, d->out_bias, d->t_b1, d->t_b2, d->dt_b1, d->dt_b2, d->norm}) cudaFree(p);
+    lm_free(ctx, d->blocks);
+    delete d;
+}
+
+extern "C" int vb_dit_create(vb_ctx *ctx, const vb_dit_config *cfg, const vb_dit_host *w, vb_dit **out) {
+    if (!ctx || !cfg || !w || !out) return VB_ERR_INVALID_ARG;
+    *out = nullptr;
+    const vb_dit_config &c = *cfg;
+    if (c.hidden <= 0 || c.patch <= 0 || c.feat_dim <= 0 || c.n_layers <= 0)
+        return set_error(ctx, VB_ERR_INVALID_ARG, "vb_dit_create: bad configuration");
+    vb_dit *d = new vb_dit();
+    d->cfg = c;
+    const int64_t H = c.hidden, F = c.feat_dim;
+    int rc = VB_OK;
+    auto reg = [&](const void *host, int64_t K, int64_t N, vb_weight *dst) {
+        if (rc) return;
+        if (!host) { rc = set_error(ctx, VB_ERR_INVALID_ARG, "vb_dit_create: missing weight"); return; }
+        rc = weight_upload(ctx, c.wtype, K, N, host, (size_t)N * row_bytes(c.wtype, K), dst);
+        if (!rc) d->weight_bytes += (*dst)->device_bytes;
+    };
+    reg(w->in_proj, F, H, &d->in_proj);
+    reg(w->cond_proj, F, H, &d->cond_proj);
+    reg(w->out_proj, H, F, &d->out_proj);
+    reg(w->t_w1, H, H, &d->t_w1);
+    reg(w->t_w2, H, H, &d->t_w2);
+    reg(w->dt_w1, H, H, &d->dt_w1);
+    reg(w->dt_w2, H, H, &d->dt_w2);
+    if (!rc) rc = upload_f32(ctx, w->in_bias, H, &d->in_bias);
+    if (!rc) rc = upload_f32(ctx, w->cond_bias, H, &d->cond_bias);
+    if (!rc) rc = upload_f32(ctx, w->out_bias, F, &d->out_bias);
+    if (!rc) rc = upload_f32(ctx, w->t_b1, H, &d->t_b1);
+    if (!rc) rc = upload_f32(ctx, w->t_b2, H, &d->t_b2);
+    if (!rc) rc = upload_f32(ctx, w->dt_b1, H, &d->dt_b1);
+    if (!rc) rc = upload_f32(ctx, w->dt_b2, H, &d->dt_b2);
+    if (!rc) rc = upload_f32(ctx, w->norm, H, &d->norm);
+    if (!rc) {
+        vb_lm_config lc;
+        lc.hidden = c.hidden;
+        lc.n_heads = c.n_heads;
+        lc.n_kv_heads = c.n_kv_heads;
+        lc.head_dim = c.head_dim;
+        lc.ffn = c.ffn;
+        lc.n_layers = c.n_layers;
+        lc.eps = c.eps;
+        lc.rope_theta = 10000.0f;   // src/locdit.c:355
+        lc.no_rope = 0;
+        lc.scale_depth = 0.0f;
+        lc.wtype = c.wtype;
+        rc = vb_lm_create(ctx, &lc, w->layers, nullptr, &d->blocks);
+        if (!rc) d->weight_bytes += d->blocks->weight_bytes;
+    }
+    if (rc) {
+        dit_free(ctx, d);
+        return rc;
+    }
+    *out = d;
+    return VB_OK;
+}
+
+extern "C" void vb_dit_destroy(vb_ctx *ctx, vb_dit *d) { dit_free(ctx, d); }
+extern "C" size_t vb_dit_weight_bytes(const vb_dit *d) { return d ? d->weight_bytes : 0; }
+
+namespace vb {
+
+// dit_sinusoidal_t_embed (src/locdit.c:163-188), on the host with libm so
+// the values equal the reference's: [sin(half) | cos(half)], each bf16.
+static void dit_time_sin(float t, int dim, float *out) {
+    const int half = dim / 2;
+    const float log_max_period = logf(10000.0f);
+    const float denom = (half > 1) ? (float)(half - 1) : 1.0f;
+    const float scaled_t = ::vb_host_bf16(t * 1000.0f);
+    for (int i = 0; i < half; i++) {
+        const float exponent = ::vb_host_bf16(::vb_host_bf16((float)i) * (-log_max_period / denom));
+        const float freq = ::vb_host_bf16(expf(exponent));
+        const float angle = ::vb_host_bf16(freq * scaled_t);
+        out[i] = ::vb_host_bf16(sinf(angle));
+        out[half + i] = ::vb_host_bf16(cosf(angle));
+    }
+}
+
+// The LocDiT forward of n items.  x_mod: item rows of x/cond wrap modulo
+// x_mod items (the CFG batch reads the same patch for both branches).
+// t_shared: every item uses t[0], dt[0].
+static int dit_forward_impl(vb_ctx *ctx, vb_dit *d, int n, const float *x, const float *cond, int x_mod,
+                            const float *t, const float *dt, int t_shared, const float *mu, const int *has_mu_dev,
+                            float *out) {
+    const vb_dit_config &c = d->cfg;
+    const int64_t H = c.hidden, P = c.patch, F = c.feat_dim, T = 3 + 2 * P;
+    const int nt = t_shared ? 1 : n;
+    const vb_lm_config &lc = d->blocks->cfg;
+    const int M = (int)(n * T);
+    // workspace: blocks need their own carve region after ours
+    size_t mine = align256((size_t)M * H * 4) + 4 * align256((size_t)nt * H * 4) + align256((size_t)n * P * H * 4) +
+                  align256((size_t)n * 4) + 4096;
+    size_t need = mine + layer_ws_bytes(lc, M) + 2 * align256((size_t)lc.n_kv_heads * M * lc.head_dim * 2) +
+                  align256((size_t)16 * M) + 4096;
+    int rc = ws_reserve(ctx, need);
+    if (rc) return rc;
+    Carve cv(ctx->ws.ptr);
+    float *seq = cv.take<float>((size_t)M * H);
+    float *tsin = cv.take<float>((size_t)nt * H);
+    float *h1 = cv.take<float>((size_t)nt * H);
+    float *tf = cv.take<float>((size_t)nt * H);
+    float *dtf = cv.take<float>((size_t)nt * H);
+    float *xn = cv.take<float>((size_t)n * P * H);
+    int *hm = cv.take<int>((size_t)n);
+
+    // time embeddings: host sinusoid, device time MLPs
+    std::vector<float> ts((size_t)nt * H), dts((size_t)nt * H);
+    for (int i = 0; i < nt; i++) {
+        dit_time_sin(t[i], (int)H, ts.data() + (size_t)i * H);
+        dit_time_sin(dt[i], (int)H, dts.data() + (size_t)i * H);
+    }
+    MatmulOut o;
+    o.flags = VB_OUT_BF16;
+    auto time_mlp = [&](const std::vector<float> &sinv, vb_weight w1, const float *b1, vb_weight w2, const float *b2,
+                        float *dst) -> int {
+        VB_CHECK(ctx, cudaMemcpyAsync(tsin, sinv.data(), (size_t)nt * H * 4, cudaMemcpyHostToDevice, ctx->stream));
+        MatmulOut m1;
+        m1.y = h1;
+        m1.bias = b1;
+        m1.flags = VB_OUT_BF16;
+        int r = launch_matmul(ctx, w1, tsin, nt, 0, 0, m1);
+        if (r) return r;
+        silu_bf16_kernel<<<(unsigned)((nt * H + 255) / 256), 256, 0, ctx->stream>>>(h1, nt * H);
+        VB_LAUNCH_CHECK(ctx, "silu_bf16");
+        MatmulOut m2;
+        m2.y = dst;
+        m2.bias = b2;
+        m2.flags = VB_OUT_BF16;
+        return launch_matmul(ctx, w2, h1, nt, 0, 0, m2);
+    };
+    if ((rc = time_mlp(ts, d->t_w1, d->t_b1, d->t_w2, d->t_b2, tf))) return rc;
+    if ((rc = time_mlp(dts, d->dt_w1, d->dt_b1, d->dt_w2, d->dt_b2, dtf))) return rc;
+
+    // x tokens -> rows 3+P.., cond tokens -> rows 3.. of every item
+    MatmulOut ox;
+    ox.y = seq;
+    ox.flags = VB_OUT_BF16;
+    ox.ldy = H;
+    ox.seg = P;
+    ox.seg_stride = T;
+    ox.bias = d->in_bias;
+    ox.seg_off = 3 + P;
+    if ((rc = launch_matmul(ctx, d->in_proj, x, (int64_t)n * P, F, (int64_t)x_mod * P, ox))) return rc;
+    ox.bias = d->cond_bias;
+    ox.seg_off = 3;
+    if ((rc = launch_matmul(ctx, d->cond_proj, cond, (int64_t)n * P, F, (int64_t)x_mod * P, ox))) return rc;
+    // mu / zero tokens and the time token
+    if (mu) {
+        if (!has_mu_dev) {
+            std::vector<int> ones(n, 1);
+            VB_CHECK(ctx, cudaMemcpyAsync(hm, ones.data(), (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream));
+            has_mu_dev = hm;
+        }
+    }
+    dit_head_kernel<<<n, 256, 0, ctx->stream>>>(seq, T, H, mu, has_mu_dev, tf, dtf, t_shared);
+    VB_LAUNCH_CHECK(ctx, "dit_head");
+
+    // the blocks carve the workspace after our region
+    Carve inner((uint8_t *)ctx->ws.ptr + align256(cv.off));
+    {
+        const int M2 = M;
+        std::vector<int32_t> tab((size_t)4 * M2);
+        for (int m = 0; m < M2; m++) {
+            tab[m] = (int)(m % T);
+            tab[M2 + m] = m;
+            tab[2 * M2 + m] = (int)((m / T) * T);
+            tab[3 * M2 + m] = (int)T;
+        }
+        TokenTables tt;
+        if ((rc = upload_tables(ctx, inner, M2, tab, tt))) return rc;
+        tt.max_len = (int)T;
+        const size_t kv_elems = (size_t)lc.n_kv_heads * M2 * lc.head_dim;
+        uint16_t *kc = inner.take<uint16_t>(kv_elems);
+        uint16_t *vc = inner.take<uint16_t>(kv_elems);
+        if ((rc = run_layers(ctx, d->blocks, M2, seq, tt, kc, vc, 0, M2, inner))) return rc;
+    }
+    // slice the x tokens, final norm, out_proj
+    int64_t rows = (int64_t)n * P;
+    gather_rows_kernel<<<(unsigned)((rows * H + 255) / 256), 256, 0, ctx->stream>>>(seq, xn, rows, H, P, T, 3 + P);
+    VB_LAUNCH_CHECK(ctx, "gather_rows");
+    if ((rc = launch_rms_norm(ctx, xn, d->norm, xn, H, rows, c.eps, VB_OUT_BF16))) return rc;
+    MatmulOut oo;
+    oo.y = out;
+    oo.bias = d->out_bias;
+    oo.flags = VB_OUT_BF16;
+    return launch_matmul(ctx, d->out_proj, xn, rows, 0, 0, oo);
+}
+
+}  // namespace vb
+
+extern "C" int vb_dit_forward(vb_ctx *ctx, vb_dit *d, int n, const float *x, const float *cond, const float *t,
+                              const float *dt, const float *mu, const int *has_mu, float *out) {
+    if (!ctx || !d || n <= 0 || !x || !cond || !t || !dt || !out) return VB_ERR_INVALID_ARG;
+    int *hm_dev = nullptr;
+    if (mu && has_mu) {
+        VB_CHECK(ctx, cudaMalloc(&hm_dev, (size_t)n * 4));
+        cudaMemcpyAsync(hm_dev, has_mu, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream);
+    }
+    int rc = dit_forward_impl(ctx, d, n, x, cond, n, t, dt, 0, mu, hm_dev, out);
+    if (hm_dev) {
+        cudaStreamSynchronize(ctx->stream);
+        cudaFree(hm_dev);
+    }
+    return rc;
+}
+
+extern "C" int vb_cfm_solve(vb_ctx *ctx, vb_dit *d, int n, const float *mu, const float *cond, float *x, int n_steps,
+                            float cfg_value) {
+    if (!ctx || !d || n <= 0 || !cond || !x || n_steps <= 0) return VB_ERR_INVALID_ARG;
+    const vb_dit_config &c = d->cfg;
+    const int len = c.patch * c.feat_dim;
+    const int use_cfg = (cfg_value != 1.0f && mu != nullptr);
+    const int items = use_cfg ? 2 * n : n;
+    const int zero_star = vb_cfm_zero_star_steps(n_steps);
+    // velocity buffer and the has_mu table live in the attention arena's
+    // neighbour: a dedicated allocation sized once per call shape.
+    float *vel = nullptr;
+    int *hm = nullptr;
+    VB_CHECK(ctx, cudaMallocAsync(&vel, (size_t)items * len * 4, ctx->stream));
+    VB_CHECK(ctx, cudaMallocAsync(&hm, (size_t)items * 4, ctx->stream));
+    std::vector<int> hmh(items, 0);
+    for (int i = 0; i < n; i++) hmh[i] = 1;
+    int rc = VB_OK;
+    if (cudaMemcpyAsync(hm, hmh.data(), (size_t)items * 4, cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess)
+        rc = set_error(ctx, VB_ERR_BACKEND, "cfm: upload failed");
+    for (int step = zero_star; step < n_steps && rc == VB_OK; step++) {
+        const float t = vb_cfm_sway_t_bf16(step, n_steps);
+        const float nt = vb_cfm_sway_t_bf16(step + 1, n_steps);
+            const float step_size = ::vb_host_bf16(-(t - nt));
+        const float zero = 0.0f;
+        rc = dit_forward_impl(ctx, d, items, x, cond, n, &t, &zero, 1, mu, hm, vel);
+        if (rc) break;
+        cfm_update_kernel<<<n, 256, 0, ctx->stream>>>(x, vel, n, len, use_cfg, cfg_value, step_size);
+        rc = check_launch(ctx, "cfm_update");
+    }
+    cudaFreeAsync(vel, ctx->stream);
+    cudaFreeAsync(hm, ctx->stream);
+    return rc;
+}

@@ -1,0 +1,373 @@
+"""ctypes binding of libvcpm_b200.so (include/vcpm_b200.h).
+
+This is the Python face of the C ABI that a host runtime binds: tests and
+bench.py drive the B200 kernels through exactly these entry points.  It never
+falls back to anything: if the library is missing or no sm_100 device is
+present, creating a context raises.
+
+Device buffers are plain integers (device addresses), typically
+`torch.Tensor.data_ptr()` of CUDA tensors on the context's device.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libvcpm_b200.so")
+
+VB_OK, VB_ERR_INVALID_ARG, VB_ERR_BACKEND, VB_ERR_OOM, VB_ERR_NOT_IMPLEMENTED = 0, 1, 5, 6, 7
+TYPE_F32, TYPE_F16, TYPE_Q8_0 = 0, 1, 8
+QRULE_X86, QRULE_REF = 0, 1
+OUT_BF16 = 1
+
+_lib = None
+
+
+class VBError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"vcpm_b200 error {code}: {msg}")
+        self.code = code
+
+
+class LMConfig(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("hidden", "n_heads", "n_kv_heads", "head_dim", "ffn", "n_layers")] + [
+        ("eps", C.c_float), ("rope_theta", C.c_float), ("no_rope", C.c_int), ("scale_depth", C.c_float),
+        ("wtype", C.c_int)]
+
+
+class LayerHost(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("q", "k", "v", "o", "gate", "up", "down", "attn_norm", "ffn_norm")]
+
+
+class DiTConfig(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("hidden", "n_layers", "n_heads", "n_kv_heads", "ffn", "head_dim",
+                                       "feat_dim", "patch")] + [("eps", C.c_float), ("wtype", C.c_int)]
+
+
+class DiTHost(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "in_proj", "cond_proj", "out_proj", "in_bias", "cond_bias", "out_bias",
+        "t_w1", "t_w2", "dt_w1", "dt_w2", "t_b1", "t_b2", "dt_b1", "dt_b2", "norm", "layers")]
+
+
+# exported name -> (restype, argtypes)
+_P, _I, _I64, _F, _SZ, _U = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t, C.c_uint
+SIGNATURES = {
+    "vb_device_count": (_I, [C.POINTER(C.c_int)]),
+    "vb_create": (_I, [_I, C.POINTER(_P)]),
+    "vb_destroy": (None, [_P]),
+    "vb_last_error": (C.c_char_p, [_P]),
+    "vb_sync": (_I, [_P]),
+    "vb_set_stream": (_I, [_P, _P]),
+    "vb_get_stream": (_P, [_P]),
+    "vb_set_qrule": (_I, [_P, _I]),
+    "vb_graph_begin": (_I, [_P]),
+    "vb_graph_end": (_I, [_P, C.POINTER(_P)]),
+    "vb_graph_launch": (_I, [_P, _P]),
+    "vb_graph_destroy": (None, [_P]),
+    "vb_event_create": (_I, [_P, C.POINTER(_P)]),
+    "vb_event_record": (_I, [_P, _P]),
+    "vb_event_elapsed_ms": (_I, [_P, _P, C.POINTER(C.c_float)]),
+    "vb_event_destroy": (None, [_P]),
+    "vb_malloc": (_I, [_P, _SZ, C.POINTER(_P)]),
+    "vb_free": (_I, [_P, _P]),
+    "vb_host_alloc": (_I, [_P, _SZ, C.POINTER(_P)]),
+    "vb_host_free": (_I, [_P, _P]),
+    "vb_memcpy_h2d": (_I, [_P, _P, _P, _SZ]),
+    "vb_memcpy_d2h": (_I, [_P, _P, _P, _SZ]),
+    "vb_memcpy_d2d": (_I, [_P, _P, _P, _SZ]),
+    "vb_memset": (_I, [_P, _P, _I, _SZ]),
+    "vb_weight_register": (_I, [_P, _I, _I64, _I64, _P, _SZ, C.POINTER(_P)]),
+    "vb_weight_release": (_I, [_P, _P]),
+    "vb_weight_info": (_I, [_P, C.POINTER(_I), C.POINTER(_I64), C.POINTER(_I64), C.POINTER(_SZ)]),
+    "vb_matmul": (_I, [_P, _P, _P, _I64, _P, _U]),
+    "vb_matmul_bias": (_I, [_P, _P, _P, _I64, _P, _P, _U]),
+    "vb_quantize_q8_0": (_I, [_P, _P, _I64, _I64, _P, _I]),
+    "vb_dequantize_q8_0": (_I, [_P, _P, _I64, _P]),
+    "vb_rms_norm": (_I, [_P, _P, _P, _P, _I64, _I64, _F, _U]),
+    "vb_bf16_round": (_I, [_P, _P, _I64]),
+    "vb_residual_add": (_I, [_P, _P, _P, _F, _P, _I64, _U]),
+    "vb_swiglu": (_I, [_P, _P, _P, _P, _I64, _U]),
+    "vb_rope_neox": (_I, [_P, _P, _I, _I, _I, _P, _F, _U]),
+    "vb_fsq_quantize": (_I, [_P, _P, _I64, _F]),
+    "vb_attention": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P]),
+    "vb_kv_write": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
+    "vb_lm_create": (_I, [_P, _P, _P, _P, C.POINTER(_P)]),
+    "vb_lm_destroy": (None, [_P, _P]),
+    "vb_lm_weight_bytes": (_SZ, [_P]),
+    "vb_kv_create": (_I, [_P, _P, _I, _I, C.POINTER(_P)]),
+    "vb_kv_destroy": (None, [_P, _P]),
+    "vb_kv_reset": (_I, [_P, _I]),
+    "vb_kv_used": (_I, [_P, _I]),
+    "vb_lm_forward": (_I, [_P, _P, _P, _I, _P, _P, _I, _P, _P]),
+    "vb_lm_forward_noncausal": (_I, [_P, _P, _I, _I, _P]),
+    "vb_dit_create": (_I, [_P, _P, _P, C.POINTER(_P)]),
+    "vb_dit_destroy": (None, [_P, _P]),
+    "vb_dit_weight_bytes": (_SZ, [_P]),
+    "vb_dit_forward": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _P, _P]),
+    "vb_cfm_solve": (_I, [_P, _P, _I, _P, _P, _P, _I, _F]),
+    "vb_cfm_sway_t_bf16": (_F, [_I, _I]),
+    "vb_cfm_zero_star_steps": (_I, [_I]),
+    "vb_cfm_noise": (None, [C.c_uint64, _I, _P, _I]),
+    "vb_round_cache_capacity": (_I, [_I, _I]),
+}
+
+
+def lib():
+    """Loads the library (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(f"{LIB_PATH} is missing: run voxcpm-cpp_b200/build.py (or __graft_entry__.build())")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def device_count() -> int:
+    n = C.c_int(0)
+    lib().vb_device_count(C.byref(n))
+    return n.value
+
+
+def _addr(a):
+    """Device address of a torch tensor / int / None; host address of numpy."""
+    if a is None:
+        return None
+    if isinstance(a, int):
+        return a
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    if hasattr(a, "ctypes"):
+        return a.ctypes.data
+    raise TypeError(type(a))
+
+
+class Context:
+    """One device + one stream (vb_ctx)."""
+
+    def __init__(self, device: int = 0):
+        self.h = C.c_void_p()
+        rc = lib().vb_create(device, C.byref(self.h))
+        if rc != VB_OK:
+            raise VBError(rc, f"vb_create(device={device}) failed (no sm_100 device?)")
+        self.device = device
+        self.L = lib()
+
+    def close(self):
+        if self.h:
+            self.L.vb_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def check(self, rc):
+        if rc != VB_OK:
+            raise VBError(rc, self.last_error())
+        return rc
+
+    def last_error(self) -> str:
+        return (self.L.vb_last_error(self.h) or b"").decode()
+
+    def sync(self):
+        self.check(self.L.vb_sync(self.h))
+
+    def stream(self) -> int:
+        return self.L.vb_get_stream(self.h)
+
+    def set_stream(self, s):
+        self.check(self.L.vb_set_stream(self.h, s))
+
+    def set_qrule(self, rule):
+        self.check(self.L.vb_set_qrule(self.h, rule))
+
+    # ------------------------------------------------------------- graphs
+    def graph_begin(self):
+        self.check(self.L.vb_graph_begin(self.h))
+
+    def graph_end(self):
+        g = C.c_void_p()
+        self.check(self.L.vb_graph_end(self.h, C.byref(g)))
+        return g
+
+    def graph_launch(self, g):
+        self.check(self.L.vb_graph_launch(self.h, g))
+
+    def graph_destroy(self, g):
+        self.L.vb_graph_destroy(g)
+
+    def event(self):
+        e = C.c_void_p()
+        self.check(self.L.vb_event_create(self.h, C.byref(e)))
+        return e
+
+    def record(self, e):
+        self.check(self.L.vb_event_record(self.h, e))
+
+    def elapsed_ms(self, a, b):
+        ms = C.c_float(0)
+        self.check(self.L.vb_event_elapsed_ms(a, b, C.byref(ms)))
+        return ms.value
+
+    def memcpy_h2d(self, dst, src, nbytes):
+        self.check(self.L.vb_memcpy_h2d(self.h, _addr(dst), _addr(src), nbytes))
+
+    def memcpy_d2h(self, dst, src, nbytes):
+        self.check(self.L.vb_memcpy_d2h(self.h, _addr(dst), _addr(src), nbytes))
+
+    # ------------------------------------------------------------ weights
+    def weight(self, wtype, K, N, host_array):
+        """Registers a GGUF-layout weight (numpy uint8/uint16/float32)."""
+        w = C.c_void_p()
+        self.check(self.L.vb_weight_register(self.h, wtype, K, N, host_array.ctypes.data, host_array.nbytes,
+                                             C.byref(w)))
+        return Weight(self, w, wtype, K, N)
+
+    # ---------------------------------------------------------------- ops
+    def matmul(self, w, x, M, y, flags=0, bias=None):
+        self.check(self.L.vb_matmul_bias(self.h, w.h, _addr(x), M, _addr(bias), _addr(y), flags))
+
+    def quantize_q8_0(self, x, K, M, blocks, rule=QRULE_X86):
+        self.check(self.L.vb_quantize_q8_0(self.h, _addr(x), K, M, _addr(blocks), rule))
+
+    def dequantize_q8_0(self, blocks, n, y):
+        self.check(self.L.vb_dequantize_q8_0(self.h, _addr(blocks), n, _addr(y)))
+
+    def rms_norm(self, x, w, y, n, rows, eps, flags=0):
+        self.check(self.L.vb_rms_norm(self.h, _addr(x), _addr(w), _addr(y), n, rows, eps, flags))
+
+    def bf16_round(self, x, n):
+        self.check(self.L.vb_bf16_round(self.h, _addr(x), n))
+
+    def residual_add(self, a, b, scale, y, n, flags=OUT_BF16):
+        self.check(self.L.vb_residual_add(self.h, _addr(a), _addr(b), scale, _addr(y), n, flags))
+
+    def swiglu(self, g, u, y, n, flags=OUT_BF16):
+        self.check(self.L.vb_swiglu(self.h, _addr(g), _addr(u), _addr(y), n, flags))
+
+    def rope_neox(self, x, head_dim, n_heads, T, pos, theta, flags=OUT_BF16):
+        self.check(self.L.vb_rope_neox(self.h, _addr(x), head_dim, n_heads, T, _addr(pos), theta, flags))
+
+    def fsq_quantize(self, x, n, s):
+        self.check(self.L.vb_fsq_quantize(self.h, _addr(x), n, s))
+
+    def attention(self, q, k, v, n_rows, T, n_heads, n_kv, head_dim, row_start, kv_len, out):
+        self.check(self.L.vb_attention(self.h, _addr(q), _addr(k), _addr(v), n_rows, T, n_heads, n_kv, head_dim,
+                                       _addr(row_start), _addr(kv_len), _addr(out)))
+
+    def kv_write(self, k, v, kc, vc, n_rows, T, n_kv, head_dim, dst_row):
+        self.check(self.L.vb_kv_write(self.h, _addr(k), _addr(v), _addr(kc), _addr(vc), n_rows, T, n_kv, head_dim,
+                                      _addr(dst_row)))
+
+
+class Weight:
+    def __init__(self, ctx, h, wtype, K, N):
+        self.ctx, self.h, self.wtype, self.K, self.N = ctx, h, wtype, K, N
+
+    def device_bytes(self):
+        sz = C.c_size_t(0)
+        self.ctx.check(self.ctx.L.vb_weight_info(self.h, None, None, None, C.byref(sz)))
+        return sz.value
+
+    def release(self):
+        if self.h:
+            self.ctx.L.vb_weight_release(self.ctx.h, self.h)
+            self.h = None
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+class LM:
+    """A transformer stack (vb_lm) built from numpy GGUF-layout weights."""
+
+    def __init__(self, ctx: Context, cfg: LMConfig, layers: list[dict], final_norm=None):
+        self.ctx, self.cfg = ctx, cfg
+        self._keep = layers
+        arr = (LayerHost * cfg.n_layers)()
+        for i, L in enumerate(layers):
+            arr[i] = LayerHost(*[_ptr(L[k]) for k in ("q", "k", "v", "o", "gate", "up", "down", "attn_norm",
+                                                      "ffn_norm")])
+        self._fn = final_norm
+        self.h = C.c_void_p()
+        ctx.check(ctx.L.vb_lm_create(ctx.h, C.byref(cfg), arr, _ptr(final_norm), C.byref(self.h)))
+
+    def weight_bytes(self):
+        return self.ctx.L.vb_lm_weight_bytes(self.h)
+
+    def forward(self, kv, seq, pos, T, x, out):
+        n = len(seq)
+        s = (C.c_int32 * n)(*seq)
+        p = (C.c_int32 * n)(*pos)
+        self.ctx.check(self.ctx.L.vb_lm_forward(self.ctx.h, self.h, kv.h, n, s, p, T, _addr(x), _addr(out)))
+
+    def forward_noncausal(self, n, T, h):
+        self.ctx.check(self.ctx.L.vb_lm_forward_noncausal(self.ctx.h, self.h, n, T, _addr(h)))
+
+    def close(self):
+        if self.h:
+            self.ctx.L.vb_lm_destroy(self.ctx.h, self.h)
+            self.h = C.c_void_p()
+
+
+class KV:
+    def __init__(self, ctx: Context, lm: LM, n_seqs, capacity):
+        self.ctx = ctx
+        self.h = C.c_void_p()
+        ctx.check(ctx.L.vb_kv_create(ctx.h, lm.h, n_seqs, capacity, C.byref(self.h)))
+
+    def used(self, seq=0):
+        return self.ctx.L.vb_kv_used(self.h, seq)
+
+    def reset(self, seq=-1):
+        self.ctx.check(self.ctx.L.vb_kv_reset(self.h, seq))
+
+    def close(self):
+        if self.h:
+            self.ctx.L.vb_kv_destroy(self.ctx.h, self.h)
+            self.h = C.c_void_p()
+
+
+class DiT:
+    def __init__(self, ctx: Context, cfg: DiTConfig, t: dict, layers: list[dict]):
+        self.ctx, self.cfg = ctx, cfg
+        self._keep = (t, layers)
+        self._arr = (LayerHost * cfg.n_layers)()
+        for i, L in enumerate(layers):
+            self._arr[i] = LayerHost(*[_ptr(L[k]) for k in ("q", "k", "v", "o", "gate", "up", "down", "attn_norm",
+                                                            "ffn_norm")])
+        g = lambda k: _ptr(t.get(k))  # noqa: E731
+        host = DiTHost(g("in_proj"), g("cond_proj"), g("out_proj"), g("in_bias"), g("cond_bias"), g("out_bias"),
+                       g("t_w1"), g("t_w2"), g("dt_w1"), g("dt_w2"), g("t_b1"), g("t_b2"), g("dt_b1"), g("dt_b2"),
+                       g("norm"), C.cast(self._arr, C.c_void_p))
+        self.h = C.c_void_p()
+        ctx.check(ctx.L.vb_dit_create(ctx.h, C.byref(cfg), C.byref(host), C.byref(self.h)))
+
+    def weight_bytes(self):
+        return self.ctx.L.vb_dit_weight_bytes(self.h)
+
+    def forward(self, n, x, cond, t, dt, mu, out, has_mu=None):
+        ta = (C.c_float * n)(*t)
+        da = (C.c_float * n)(*dt)
+        hm = (C.c_int * n)(*has_mu) if has_mu is not None else None
+        self.ctx.check(self.ctx.L.vb_dit_forward(self.ctx.h, self.h, n, _addr(x), _addr(cond), ta, da, _addr(mu),
+                                                 hm, _addr(out)))
+
+    def cfm_solve(self, n, mu, cond, x, n_steps, cfg_value):
+        self.ctx.check(self.ctx.L.vb_cfm_solve(self.ctx.h, self.h, n, _addr(mu), _addr(cond), _addr(x), n_steps,
+                                               cfg_value))
+
+    def close(self):
+        if self.h:
+            self.ctx.L.vb_dit_destroy(self.ctx.h, self.h)
+            self.h = C.c_void_p()
