@@ -9,6 +9,7 @@ contiguous numpy arrays.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
 import os
 import subprocess
@@ -24,11 +25,16 @@ QRULE_X86, QRULE_REF = 0, 1
 _lib = None
 
 
+LIB_F32ACC_PATH = os.path.join(HERE, "liboracle_f32acc.so")
+_f32acc = None
+
+
 def build(force: bool = False) -> str:
-    """Compile liboracle.so with the committed Makefile."""
-    if force or not os.path.exists(LIB_PATH) or (
-        os.path.getmtime(LIB_PATH) < os.path.getmtime(os.path.join(HERE, "vcpm_oracle.c"))
-    ):
+    """Compile liboracle.so (and its fp32-accumulation twin) with the
+    committed Makefile."""
+    src = os.path.getmtime(os.path.join(HERE, "vcpm_oracle.c"))
+    stale = any(not os.path.exists(p) or os.path.getmtime(p) < src for p in (LIB_PATH, LIB_F32ACC_PATH))
+    if force or stale:
         subprocess.check_call(["make", "-s", "-B" if force else "all", "-C", HERE])
     return LIB_PATH
 
@@ -40,6 +46,22 @@ def lib():
         _lib = C.CDLL(LIB_PATH)
         _declare(_lib)
     return _lib
+
+
+@contextlib.contextmanager
+def f32_accumulation():
+    """Within the block every oracle call uses the fp32-accumulation build
+    (same restatement, ggml's accumulation precision)."""
+    global _lib, _f32acc
+    base = lib()
+    if _f32acc is None:
+        _f32acc = C.CDLL(LIB_F32ACC_PATH)
+        _declare(_f32acc)
+    _lib = _f32acc
+    try:
+        yield
+    finally:
+        _lib = base
 
 
 class LayerWeights(C.Structure):

@@ -18,6 +18,17 @@
 #include <omp.h>
 #endif
 
+/* Accumulator of every dot product (mat-mul blocks, attention scores and
+ * value sums).  The default (double) is the most exact restatement; the
+ * Makefile also builds liboracle_f32acc.so with VO_ACC=float, which sums in
+ * fp32 as ggml-CPU's SIMD lanes do.  Both are the same algorithm up to
+ * accumulation order; the distance between their outputs measures how far
+ * two legitimate orders drift apart through bf16 casts and Q8_0 activation
+ * rounding, and the parity tests calibrate stacked-layer gates with it. */
+#ifndef VO_ACC
+#define VO_ACC double
+#endif
+
 /* ------------------------------------------------------------------------ */
 /* scalar conversions                                                        */
 /* ------------------------------------------------------------------------ */
@@ -165,7 +176,7 @@ size_t vo_row_bytes(int type, int64_t K) {
  * double (ggml accumulates in fp32 lanes; the difference is accumulation
  * order only). */
 static float dot_q8_0(const vo_block_q8_0 *w, const vo_block_q8_0 *x, int64_t nb) {
-    double acc = 0.0;
+    VO_ACC acc = 0.0;
     for (int64_t b = 0; b < nb; b++) {
         int32_t s = 0;
         for (int j = 0; j < VO_QK8_0; j++) s += (int32_t)w[b].qs[j] * (int32_t)x[b].qs[j];
@@ -176,13 +187,13 @@ static float dot_q8_0(const vo_block_q8_0 *w, const vo_block_q8_0 *x, int64_t nb
 }
 
 static float dot_f16(const uint16_t *w, const uint16_t *x, int64_t K) {
-    double acc = 0.0;
+    VO_ACC acc = 0.0;
     for (int64_t k = 0; k < K; k++) acc += (double)(g_f16_table[w[k]] * g_f16_table[x[k]]);
     return (float)acc;
 }
 
 static float dot_f32(const float *w, const float *x, int64_t K) {
-    double acc = 0.0;
+    VO_ACC acc = 0.0;
     for (int64_t k = 0; k < K; k++) acc += (double)(w[k] * x[k]);
     return (float)acc;
 }
@@ -402,14 +413,14 @@ int vo_attention(const vo_lm_config *cfg, const vo_layer_weights *w,
                 const float *qv = q + (size_t)ti * QD + (size_t)h * HD;
                 for (int l = 0; l < L; l++) {
                     const float *kv = ks + (size_t)l * KD + (size_t)g * HD;
-                    double acc = 0.0;
+                    VO_ACC acc = 0.0;
                     for (int d = 0; d < HD; d++) acc += (double)(kv[d] * qv[d]);
                     sc[l] = (float)acc * kq_scale;
                 }
                 softmax_inplace(sc, L);
                 float *ov = att + (size_t)ti * QD + (size_t)h * HD;
                 for (int d = 0; d < HD; d++) {
-                    double acc = 0.0;
+                    VO_ACC acc = 0.0;
                     for (int l = 0; l < L; l++) acc += (double)(vs[(size_t)l * KD + (size_t)g * HD + d] * sc[l]);
                     ov[d] = (float)acc;
                 }

@@ -72,6 +72,33 @@ def assert_matmul_close(y, r, tol=1e-3):
     assert float(err.max()) <= tol, f"max rel err {err.max():.3e} > {tol}"
 
 
+def cos_sim(y, r):
+    y = np.asarray(y, np.float64).ravel()
+    r = np.asarray(r, np.float64).ravel()
+    return float(y @ r / max(np.linalg.norm(y) * np.linalg.norm(r), 1e-300))
+
+
+def assert_envelope(y, r, r_f32, floor=1.5e-2, factor=3.0):
+    """Gate for outputs of stacked layers (several blocks, LocDiT, CFM).
+
+    Through bf16 casts and Q8_0 activation rounding, a last-bit difference in
+    one fp32 accumulation can flip a rounding and spread; two legitimate
+    accumulation orders of the same algorithm therefore drift apart.  `r` is
+    the oracle with double accumulation, `r_f32` the same oracle with fp32
+    accumulation (ggml's precision); the device result must lie within
+    `factor` times their distance (at least `floor`) of `r`, and keep the
+    reference's own fixture gate cos >= 0.9999.  The default floor (1.5e-2)
+    comes from the oracle itself: its two builds differ by up to 9.0e-3 on a
+    2-layer Q8_0 LocDiT output when one flip cascades, and by exactly 0 when
+    none does, so one sample of their distance can understate the spread.
+    Stage-by-stage exactness is checked separately (test_stages_gpu.py)."""
+    s = rel_l2(r_f32, r)
+    e = rel_l2(y, r)
+    c = cos_sim(y, r)
+    assert c >= 0.9999, f"cos {c:.6f} < 0.9999"
+    assert e <= max(floor, factor * s), f"relative L2 {e:.3e} > max({floor}, {factor} x {s:.3e})"
+
+
 def assert_layer_close(y, r, tol=1e-3):
     """bf16-rounded layer outputs: relative L2 <= tol and every element within
     one bf16 ulp of its own magnitude plus tol * rms (a rounding flip when the

@@ -1,10 +1,15 @@
 """GPU parity of the transformer stacks, LocDiT and the CFM loop against the
 CPU oracle, on reduced sizes that the oracle finishes in seconds.
 
-Gate: layer outputs (bf16 hidden states) within relative L2 1e-3 and every
-element within one bf16 ulp (+1e-3 rms) of the oracle: the fp32 mat-mul
-accumulation order differs, so a pre-round value that straddles a bf16
-boundary may round the other way."""
+Stacked outputs use synth.assert_envelope: the device must stay within a
+small multiple of the distance between the oracle's double- and
+fp32-accumulation builds (two legitimate accumulation orders of the same
+algorithm, which drift apart through bf16 casts and Q8_0 activation
+rounding), with a floor of 3e-3 (one block) or 1.5e-2 (several), and
+cos >= 0.9999 (the reference's fixture gate).  The exact op order of every
+stage is pinned separately by test_stages_gpu.py."""
+import contextlib
+
 import numpy as np
 import pytest
 
@@ -35,6 +40,10 @@ def host(t):
     return t.cpu().numpy()
 
 
+def variant(f32):
+    return O.f32_accumulation() if f32 else contextlib.nullcontext()
+
+
 SMALL = dict(hidden=512, n_heads=4, n_kv=2, head_dim=128, ffn=1024, n_layers=2)
 
 
@@ -52,34 +61,57 @@ def build_lm(ctx, wtype, no_rope=0, with_norm=True, **kw):
     return c, lm, ocfg, olayers, fn
 
 
+def oracle_steps(c, ocfg, olayers, fn, steps, cap, f32):
+    """Runs (x, T, pos) steps on a fresh oracle cache; returns the outputs."""
+    cache = O.KVCache(c["n_layers"], cap, c["n_kv"], c["head_dim"])
+    with variant(f32):
+        return [O.lm_forward(ocfg, olayers, fn, cache, x, T, pos) for x, T, pos in steps], cache
+
+
 @pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_F16])
 @pytest.mark.parametrize("no_rope", [0, 1])
 def test_causal_prefill_then_decode(ctx, wtype, no_rope):
     c, lm, ocfg, olayers, fn = build_lm(ctx, wtype, no_rope)
     H = c["hidden"]
     kv = vb.KV(ctx, lm, 1, 64)
-    ocache = O.KVCache(c["n_layers"], 64, c["n_kv"], c["head_dim"])
     T = 7
+    steps = [(O.bf16_round(S.normal((T, H))), T, 0)]
+    steps += [(O.bf16_round(S.normal((1, H))), 1, T + i) for i in range(3)]
+    got = []
+    for x, t, pos in steps:
+        out = torch.zeros((t, H), dtype=torch.float32, device="cuda")
+        xd = dev(x)
+        torch.cuda.synchronize()
+        lm.forward(kv, [0], [pos], t, xd, out)
+        ctx.sync()
+        got.append(host(out))
+    ref, ocache = oracle_steps(c, ocfg, olayers, fn, steps, 64, False)
+    ref32, _ = oracle_steps(c, ocfg, olayers, fn, steps, 64, True)
+    for g, r, r32 in zip(got, ref, ref32):
+        S.assert_envelope(g, r, r32)
+    assert kv.used(0) == T + 3 == ocache.n_used(0)
+    kv.close()
+    lm.close()
+
+
+@pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_F16])
+def test_single_block_prefill(ctx, wtype):
+    """One causal block (the unit the reference's vcpm_minicpm4_block builds)."""
+    c, lm, ocfg, olayers, fn = build_lm(ctx, wtype, n_layers=1, with_norm=False)
+    H, T = c["hidden"], 16
+    kv = vb.KV(ctx, lm, 1, 32)
     x = O.bf16_round(S.normal((T, H)))
     out = torch.zeros((T, H), dtype=torch.float32, device="cuda")
     xd = dev(x)
     torch.cuda.synchronize()
     lm.forward(kv, [0], [0], T, xd, out)
     ctx.sync()
-    ref = O.lm_forward(ocfg, olayers, fn, ocache, x, T, 0)
-    S.assert_layer_close(host(out), ref)
-    pos = T
-    for step in range(3):
-        x1 = O.bf16_round(S.normal((1, H)))
-        o1 = torch.zeros((1, H), dtype=torch.float32, device="cuda")
-        xd1 = dev(x1)
-        torch.cuda.synchronize()
-        lm.forward(kv, [0], [pos], 1, xd1, o1)
-        ctx.sync()
-        r1 = O.lm_forward(ocfg, olayers, fn, ocache, x1, 1, pos)
-        S.assert_layer_close(host(o1), r1)
-        pos += 1
-    assert kv.used(0) == T + 3 == ocache.n_used(0)
+    refs = []
+    for f32 in (False, True):
+        cache = O.KVCache(1, 32, c["n_kv"], c["head_dim"])
+        with variant(f32):
+            refs.append(O.block(ocfg, olayers[0], x, T, 0, 0, cache))
+    S.assert_envelope(host(out), refs[0], refs[1], floor=3e-3)
     kv.close()
     lm.close()
 
@@ -90,18 +122,15 @@ def test_batched_decode_matches_per_sequence(ctx):
     H = c["hidden"]
     kv = vb.KV(ctx, lm, 3, 128)
     lens = [5, 9, 70]          # the 70-token prompt spans two attention chunks
-    caches = [O.KVCache(c["n_layers"], 128, c["n_kv"], c["head_dim"]) for _ in lens]
+    prompts = [O.bf16_round(S.normal((L, H))) for L in lens]
+    order = [2, 0, 1]          # slots given out of order
+    xb = O.bf16_round(S.normal((3, H)))
     for s, L in enumerate(lens):
-        x = O.bf16_round(S.normal((L, H)))
         out = torch.zeros((L, H), dtype=torch.float32, device="cuda")
-        xd = dev(x)
+        xd = dev(prompts[s])
         torch.cuda.synchronize()
         lm.forward(kv, [s], [0], L, xd, out)
         ctx.sync()
-        S.assert_layer_close(host(out), O.lm_forward(ocfg, olayers, fn, caches[s], x, L, 0))
-    # one batched decode step over the three sequences (slots given out of order)
-    order = [2, 0, 1]
-    xb = O.bf16_round(S.normal((3, H)))
     ob = torch.zeros((3, H), dtype=torch.float32, device="cuda")
     xbd = dev(xb)
     torch.cuda.synchronize()
@@ -109,8 +138,10 @@ def test_batched_decode_matches_per_sequence(ctx):
     ctx.sync()
     got = host(ob)
     for i, s in enumerate(order):
-        ref = O.lm_forward(ocfg, olayers, fn, caches[s], xb[i:i + 1], 1, lens[s])
-        S.assert_layer_close(got[i:i + 1], ref)
+        steps = [(prompts[s], lens[s], 0), (xb[i:i + 1], 1, lens[s])]
+        r, _ = oracle_steps(c, ocfg, olayers, fn, steps, 128, False)
+        r32, _ = oracle_steps(c, ocfg, olayers, fn, steps, 128, True)
+        S.assert_envelope(got[i:i + 1], r[1], r32[1])
     for s, L in enumerate(lens):
         assert kv.used(s) == L + 1
     kv.close()
@@ -139,10 +170,14 @@ def test_noncausal_segments(ctx):
     ctx.sync()
     got = host(hd)
     for i in range(n):
-        ref = h[i].copy()
-        for L in olayers:
-            ref = O.block(ocfg, L, ref, T, 0, 1)
-        S.assert_layer_close(got[i], ref)
+        refs = []
+        for f32 in (False, True):
+            ref = h[i].copy()
+            with variant(f32):
+                for L in olayers:
+                    ref = O.block(ocfg, L, ref, T, 0, 1)
+            refs.append(ref)
+        S.assert_envelope(got[i], refs[0], refs[1])
     lm.close()
 
 
@@ -181,12 +216,16 @@ def test_dit_forward_cond_and_uncond(ctx, wtype):
     ctx.sync()
     got = host(out)
     for i in range(n):
-        ref = ora.forward(x[i], cond[i], ts[i], 0.0, mu[i] if has[i] else None)
-        S.assert_layer_close(got[i], ref)
+        m = mu[i] if has[i] else None
+        ref = ora.forward(x[i], cond[i], ts[i], 0.0, m)
+        with O.f32_accumulation():
+            ref32 = ora.forward(x[i], cond[i], ts[i], 0.0, m)
+        S.assert_envelope(got[i], ref, ref32)
     gpu.close()
 
 
-def test_cfm_solve_vs_oracle(ctx):
+@pytest.mark.parametrize("cfg_value", [2.0, 1.0])
+def test_cfm_solve_vs_oracle(ctx, cfg_value):
     gpu, ora = build_dit(ctx, O.TYPE_Q8_0)
     d = DIT
     n = 2
@@ -195,19 +234,12 @@ def test_cfm_solve_vs_oracle(ctx):
     x0 = np.stack([O.cfm_noise(42, i, d["patch"] * d["feat"]).reshape(d["patch"], d["feat"]) for i in range(n)])
     xd, cd, md = dev(x0), dev(cond), dev(mu)
     torch.cuda.synchronize()
-    gpu.cfm_solve(n, md, cd, xd, 10, 2.0)
+    gpu.cfm_solve(n, md, cd, xd, 10, cfg_value)
     ctx.sync()
     got = host(xd)
     for i in range(n):
-        ref = ora.cfm_solve(mu[i], cond[i], x0[i], 10, 2.0)
-        assert S.rel_l2(got[i], ref) <= 1e-2, S.rel_l2(got[i], ref)
-    # no-guidance path (cfg = 1): one DiT evaluation per step
-    xd2 = dev(x0)
-    torch.cuda.synchronize()
-    gpu.cfm_solve(n, md, cd, xd2, 10, 1.0)
-    ctx.sync()
-    got2 = host(xd2)
-    for i in range(n):
-        ref = ora.cfm_solve(mu[i], cond[i], x0[i], 10, 1.0)
-        assert S.rel_l2(got2[i], ref) <= 1e-2
+        ref = ora.cfm_solve(mu[i], cond[i], x0[i], 10, cfg_value)
+        with O.f32_accumulation():
+            ref32 = ora.cfm_solve(mu[i], cond[i], x0[i], 10, cfg_value)
+        S.assert_envelope(got[i], ref, ref32)
     gpu.close()

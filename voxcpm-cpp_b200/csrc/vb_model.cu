@@ -117,6 +117,39 @@ __global__ void cfm_update_kernel(float *x, const float *vel, int n, int len, in
 
 int init_model_kernels(vb_ctx *) { return VB_OK; }
 
+// ------------------------------------------------------------ stage dumps
+// With VB_DUMP_DIR set, every stage of the stacks writes
+// <dir>/dump_<label>.bin in the reference's debug-dump format (3 x int32
+// header ne0, ne1, ne2, then fp32 data; src/debug_dump.h:18-43).  Debug
+// only: it synchronises the stream, and is skipped inside graph capture.
+static thread_local const char *g_dump_prefix = "";
+
+static void dump(vb_ctx *ctx, const char *label, const float *d, int64_t ne0, int64_t ne1) {
+    const char *dir = getenv("VB_DUMP_DIR");
+    if (!dir || !dir[0] || !d) return;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(ctx->stream, &cs);
+    if (cs != cudaStreamCaptureStatusNone) return;
+    std::vector<float> h((size_t)(ne0 * ne1));
+    if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) return;
+    if (cudaMemcpy(h.data(), d, h.size() * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return;
+    char path[1024];
+    snprintf(path, sizeof(path), "%s/dump_%s%s.bin", dir, g_dump_prefix, label);
+    FILE *f = fopen(path, "wb");
+    if (!f) return;
+    int32_t hdr[3] = {(int32_t)ne0, (int32_t)ne1, 1};
+    fwrite(hdr, 4, 3, f);
+    fwrite(h.data(), 4, h.size(), f);
+    fclose(f);
+}
+
+static void dumpf(vb_ctx *ctx, const float *d, int64_t ne0, int64_t ne1, const char *fmt, int l) {
+    if (!getenv("VB_DUMP_DIR")) return;
+    char label[128];
+    snprintf(label, sizeof(label), fmt, l);
+    dump(ctx, label, d, ne0, ne1);
+}
+
 // -------------------------------------------------------------- workspace
 struct Carve {
     uint8_t *p;
@@ -302,33 +335,45 @@ static int run_layers(vb_ctx *ctx, vb_lm *lm, int M, float *h, const TokenTables
         LayerDev &L = lm->layers[l];
         uint16_t *kc = kc_base + (size_t)l * kv_layer_elems;
         uint16_t *vc = vc_base + (size_t)l * kv_layer_elems;
+        dumpf(ctx, h, H, M, "L%d.in", l);
         if ((rc = launch_rms_norm(ctx, h, L.attn_norm, xn, H, M, c.eps, VB_OUT_BF16))) return rc;
+        dumpf(ctx, xn, H, M, "L%d.attn_norm", l);
         MatmulOut o;
         o.y = qkv;
         o.flags = VB_OUT_BF16;
         if ((rc = launch_matmul(ctx, L.qkv, xn, M, 0, 0, o))) return rc;
+        dumpf(ctx, qkv, QKV, M, "L%d.qkv", l);
         if (!c.no_rope) {
             if ((rc = launch_rope(ctx, qkv, QKV, c.head_dim, c.n_heads, M, tt.pos, cs, VB_OUT_BF16))) return rc;
             if ((rc = launch_rope(ctx, qkv + QD, QKV, c.head_dim, c.n_kv_heads, M, tt.pos, cs, VB_OUT_BF16))) return rc;
         }
+        dumpf(ctx, qkv, QKV, M, "L%d.qkv_rope", l);
         if ((rc = launch_kv_write(ctx, qkv + QD, qkv + QD + KD, QKV, kc, vc, kv_rows, M, c.n_kv_heads, c.head_dim,
                                   tt.dst)))
             return rc;
         if ((rc = launch_attention(ctx, qkv, QKV, kc, vc, kv_rows, M, c.n_heads, c.n_kv_heads, c.head_dim, tt.start,
                                    tt.len, tt.max_len, att, QD)))
             return rc;
+        dumpf(ctx, att, QD, M, "L%d.att", l);
         o.y = a;
         if ((rc = launch_matmul(ctx, L.o, att, M, 0, 0, o))) return rc;
+        dumpf(ctx, a, H, M, "L%d.o", l);
         if ((rc = launch_residual(ctx, h, a, scale, h, (int64_t)M * H, VB_OUT_BF16))) return rc;
+        dumpf(ctx, h, H, M, "L%d.h_attn", l);
         if ((rc = launch_rms_norm(ctx, h, L.ffn_norm, xn, H, M, c.eps, VB_OUT_BF16))) return rc;
+        dumpf(ctx, xn, H, M, "L%d.ffn_norm", l);
         o.y = gu;
         if ((rc = launch_matmul(ctx, L.gu, xn, M, 0, 0, o))) return rc;
+        dumpf(ctx, gu, 2 * c.ffn, M, "L%d.gu", l);
         int64_t ne = (int64_t)M * c.ffn;
         swiglu_rows_kernel<<<(unsigned)((ne + 255) / 256), 256, 0, ctx->stream>>>(gu, act, M, c.ffn);
         VB_LAUNCH_CHECK(ctx, "swiglu_rows");
+        dumpf(ctx, act, c.ffn, M, "L%d.act", l);
         o.y = a;
         if ((rc = launch_matmul(ctx, L.down, act, M, 0, 0, o))) return rc;
+        dumpf(ctx, a, H, M, "L%d.down", l);
         if ((rc = launch_residual(ctx, h, a, scale, h, (int64_t)M * H, VB_OUT_BF16))) return rc;
+        dumpf(ctx, h, H, M, "L%d.out", l);
     }
     return VB_OK;
 }
@@ -608,6 +653,9 @@ static int dit_forward_impl(vb_ctx *ctx, vb_dit *d, int n, const float *x, const
     }
     dit_head_kernel<<<n, 256, 0, ctx->stream>>>(seq, T, H, mu, has_mu_dev, tf, dtf, t_shared);
     VB_LAUNCH_CHECK(ctx, "dit_head");
+    dump(ctx, "dit.tf", tf, H, nt);
+    dump(ctx, "dit.dtf", dtf, H, nt);
+    dump(ctx, "dit.seq0", seq, H, M);
 
     // the blocks carve the workspace after our region
     Carve inner((uint8_t *)ctx->ws.ptr + align256(cv.off));
@@ -626,18 +674,24 @@ static int dit_forward_impl(vb_ctx *ctx, vb_dit *d, int n, const float *x, const
         const size_t kv_elems = (size_t)lc.n_kv_heads * M2 * lc.head_dim;
         uint16_t *kc = inner.take<uint16_t>(kv_elems);
         uint16_t *vc = inner.take<uint16_t>(kv_elems);
-        if ((rc = run_layers(ctx, d->blocks, M2, seq, tt, kc, vc, 0, M2, inner))) return rc;
+        g_dump_prefix = "dit.";
+        rc = run_layers(ctx, d->blocks, M2, seq, tt, kc, vc, 0, M2, inner);
+        g_dump_prefix = "";
+        if (rc) return rc;
     }
     // slice the x tokens, final norm, out_proj
     int64_t rows = (int64_t)n * P;
     gather_rows_kernel<<<(unsigned)((rows * H + 255) / 256), 256, 0, ctx->stream>>>(seq, xn, rows, H, P, T, 3 + P);
     VB_LAUNCH_CHECK(ctx, "gather_rows");
     if ((rc = launch_rms_norm(ctx, xn, d->norm, xn, H, rows, c.eps, VB_OUT_BF16))) return rc;
+    dump(ctx, "dit.xn", xn, H, rows);
     MatmulOut oo;
     oo.y = out;
     oo.bias = d->out_bias;
     oo.flags = VB_OUT_BF16;
-    return launch_matmul(ctx, d->out_proj, xn, rows, 0, 0, oo);
+    rc = launch_matmul(ctx, d->out_proj, xn, rows, 0, 0, oo);
+    dump(ctx, "dit.out", out, F, rows);
+    return rc;
 }
 
 }  // namespace vb
