@@ -88,7 +88,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except (OSError, ValueError):
@@ -128,7 +128,7 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------ CPU baseline
-def cpu_baseline(seconds=12.0, layers=2):
+def cpu_baseline(seconds=12.0, layers=6):
     """The oracle's Q8_0 mat-mul (ggml-CPU semantics: activation quantized to
     Q8_0, int8 block dots, OpenMP over rows) on all host cores, over the
     projection set of `layers` layers, repeated for ~`seconds`."""
@@ -215,27 +215,44 @@ def run_b200(args, rank, world, local_rank):
     Y = torch.zeros(LAYERS * OUT_PER_LAYER, dtype=torch.float32, device="cuda")
     torch.cuda.synchronize()
 
-    def enqueue_step():
-        xo, yo = X.data_ptr(), Y.data_ptr()
-        i = 0
-        for l in range(LAYERS):
-            off = 0
-            for name, K, N, slot in SHAPES:
-                w = weights[i][3]
-                ctx.matmul(w, xo + 4 * (l * IN_PER_LAYER + IN_OFF[slot]), 1,
-                           yo + 4 * (l * OUT_PER_LAYER + off))
-                off += N
-                i += 1
-
+    # The step as ONE weight-streaming program: per layer the dependency
+    # groups of a decode layer, q,k,v | o | gate,up | down, each group
+    # waiting for the previous one on every SM.
+    GROUP_OF = {"q": 0, "k": 0, "v": 0, "o": 1, "gate": 2, "up": 2, "down": 3}
+    ops = []
+    xo, yo = X.data_ptr(), Y.data_ptr()
+    i = 0
+    for l in range(LAYERS):
+        off = 0
+        for name, K, N, slot in SHAPES:
+            grp = 4 * l + GROUP_OF[name]
+            ops.append(dict(w=weights[i][3], x=xo + 4 * (l * IN_PER_LAYER + IN_OFF[slot]),
+                            y=yo + 4 * (l * OUT_PER_LAYER + off), M=1, group=grp,
+                            wait_group=grp - 1))
+            off += N
+            i += 1
+    prog = vb.Program(ctx, ops)
     ctx.graph_begin()
-    enqueue_step()
+    prog.run()
     g = ctx.graph_end()
 
-    # config-1 shape alone: the 56 gate/up weights [2048 -> 6144]
-    c1 = [(w, K, N) for (name, K, N, w) in weights if name in ("gate", "up")]
+    # the same step as 196 separate launches (one vb_matmul per GEMV)
     ctx.graph_begin()
-    for w, K, N in c1:
-        ctx.matmul(w, X.data_ptr(), 1, Y.data_ptr())
+    i = 0
+    for l in range(LAYERS):
+        off = 0
+        for name, K, N, slot in SHAPES:
+            ctx.matmul(weights[i][3], xo + 4 * (l * IN_PER_LAYER + IN_OFF[slot]), 1,
+                       yo + 4 * (l * OUT_PER_LAYER + off))
+            off += N
+            i += 1
+    g_launch = ctx.graph_end()
+
+    # config-1 shape alone: the 56 gate/up weights [2048 -> 6144] in one program
+    c1 = [(w, K, N) for (name, K, N, w) in weights if name in ("gate", "up")]
+    prog1 = vb.Program(ctx, [dict(w=w, x=xo, y=yo, M=1, group=0) for w, K, N in c1])
+    ctx.graph_begin()
+    prog1.run()
     g1 = ctx.graph_end()
 
     ev0, ev1 = ctx.event(), ctx.event()
@@ -264,12 +281,25 @@ def run_b200(args, rank, world, local_rank):
     barrier()
     ck = clocks.stop()
 
-    # config-1 per-launch timing (same kernel, one shape)
+    rc, derr = prog.status()
+    if rc != 0 or derr != 0:
+        raise RuntimeError(f"streaming program reported device error {derr}: {ctx.last_error()}")
+
+    # config-1 shape: 56 distinct W[2048 -> 6144] (750 MB) in one program;
+    # per-GEMV time = run time / 56
     for _ in range(3):
         ctx.graph_launch(g1)
-    ms1 = timed(lambda: ctx.graph_launch(g1), max(5, args.steps // 4))
-    per_launch_ms = ms1 / (max(5, args.steps // 4) * len(c1))
-    c1_gbs = alg_bytes(2048, 6144) / (per_launch_ms * 1e-3) / 1e9
+    k1 = max(5, args.steps // 4)
+    ms1 = timed(lambda: ctx.graph_launch(g1), k1)
+    per_gemv_ms = ms1 / (k1 * len(c1))
+    c1_gbs = alg_bytes(2048, 6144) / (per_gemv_ms * 1e-3) / 1e9
+
+    # the same step as 196 separate launches, for comparison
+    for _ in range(3):
+        ctx.graph_launch(g_launch)
+    kl = max(5, args.steps // 4)
+    ms_l = timed(lambda: ctx.graph_launch(g_launch), kl)
+    per_launch_gbs = STEP_BYTES * kl / (ms_l * 1e-3) / 1e9
 
     # e2e through the C ABI: pinned host inputs -> graph -> pinned host outputs
     hx = torch.randn(LAYERS * IN_PER_LAYER, dtype=torch.float32).pin_memory()
@@ -314,21 +344,26 @@ def run_b200(args, rank, world, local_rank):
             "config": config_block(world),
             "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
                          "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
-                         "kernel": "vb::gemv_q8_kernel<1,2,4>", "traffic": NCU_TRAFFIC_CONFIG1,
-                         "traffic_unit": "bytes per config-1 launch",
-                         "achieved_config1": c1_gbs, "config1_us_per_launch": per_launch_ms * 1e3,
-                         "config1_alg_bytes": alg_bytes(2048, 6144)},
+                         "kernel": "vb::stream_gemv_kernel (one persistent launch per step)",
+                         "traffic": NCU_TRAFFIC_CONFIG1, "traffic_unit": "bytes per config-1 GEMV",
+                         "achieved_config1": c1_gbs, "config1_us_per_gemv": per_gemv_ms * 1e3,
+                         "config1_alg_bytes": alg_bytes(2048, 6144),
+                         "separate_launches_gbs": per_launch_gbs},
             "cpu_baseline": base,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": ms_e2e / args.steps, "path": "vb_memcpy_h2d + vb_graph_launch + vb_memcpy_d2h"},
             "clocks": ck,
-            "gpu_launches": args.steps * LAYERS * len(SHAPES),
+            "gpu_launches": args.steps,
+            "gpu_launches_note": "one stream_gemv_kernel launch (+1 memset of its 112 barrier counters) per step",
         }
         if decode:
             line["decode"] = decode
         print(json.dumps(line), flush=True)
     ctx.graph_destroy(g)
     ctx.graph_destroy(g1)
+    ctx.graph_destroy(g_launch)
+    prog.close()
+    prog1.close()
     for *_, w in weights:
         w.release()
     ctx.close()
@@ -382,7 +417,7 @@ def decode_bench(ctx, host_layers, args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--decode-steps", type=int, default=64)

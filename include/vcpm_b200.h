@@ -130,6 +130,39 @@ int vb_matmul(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, float *y,
 int vb_matmul_bias(vb_ctx *ctx, vb_weight w, const float *x, int64_t M,
                    const float *bias, float *y, unsigned flags);
 
+/* Weight-streaming GEMV programs: a fixed list of ggml_mul_mat calls with
+ * small M (the decode-time mat-muls of src/minicpm4.c:270-458, M = batch)
+ * run by ONE persistent launch that streams every weight through shared
+ * memory once (the B200 replacement for dispatching each mat-mul node of a
+ * graph separately, src/ggml_backend.c:557-599).  Ops are grouped: ops of
+ * one group run concurrently; an op with wait_group >= 0 reads its x only
+ * after every op of that earlier group has finished on all SMs.  Groups are
+ * numbered 0, 1, 2, ... in op order.  Weights are Q8_0 or F16, 1 <= M <= 8,
+ * M*K*(1 or 2 bytes) <= 16384, x rows 16-byte aligned.  Semantics per op
+ * are those of vb_matmul_bias. */
+typedef struct {
+    vb_weight w;
+    const float *x;
+    int64_t ldx;          /* 0 = K */
+    float *y;
+    int64_t ldy;          /* 0 = N */
+    const float *bias;    /* device F32 [N] or NULL */
+    unsigned flags;       /* VB_OUT_BF16 */
+    int M;
+    int group;
+    int wait_group;       /* -1: no dependency */
+} vb_gemv_op;
+
+typedef struct vb_program_s *vb_program;
+int vb_program_create(vb_ctx *ctx, int n_ops, const vb_gemv_op *ops,
+                      vb_program *out);
+/* Enqueues one run on the context stream (capturable in a vb_graph). */
+int vb_program_run(vb_ctx *ctx, vb_program p);
+/* Waits for the stream and reports a device-side error code (a bounded
+ * wait that timed out); 0 = OK. */
+int vb_program_status(vb_ctx *ctx, vb_program p, int *device_error);
+void vb_program_destroy(vb_program p);
+
 /* Q8_0 quantization of M rows of K floats into GGUF blocks (34 bytes per
  * 32 values) -- the activation conversion inside every Q8_0 ggml_mul_mat. */
 int vb_quantize_q8_0(vb_ctx *ctx, const float *x, int64_t K, int64_t M,

@@ -1,0 +1,420 @@
+// vb_stream.cu -- persistent weight-streaming GEMV programs.
+//
+// A batch-1 decode step is a chain of small dependent mat-muls (every
+// ggml_mul_mat of src/minicpm4.c:270-458 at M=1).  Launched one by one, each
+// pays launch latency, an activation prologue and a cold HBM pipeline, and
+// the step ends up far below the bandwidth roofline.  This file runs a whole
+// program of GEMVs in ONE cooperative launch with one CTA per SM:
+//
+//   warp 0 (producer)   walks the program in order and, for this CTA's slice
+//                        of every weight, issues 1-D TMA bulk copies
+//                        (cp.async.bulk, no multicast) of row chunks into a
+//                        5-stage shared-memory ring, each stage completing
+//                        an mbarrier by transaction bytes;
+//   warps 1..8          quantize the activation of each op once into shared
+//   (consumers)          memory (ggml's Q8_0 rule, bit-exact), then reduce
+//                        every row chunk from the ring with dp4a block dots
+//                        and write the outputs through the epilogue.
+//
+// Ops carry a dependency group: before reading its activation an op waits
+// until every CTA has finished the group it depends on (a grid-wide
+// counter).  The producer does not wait for dependencies -- weights do not
+// depend on activations -- so it keeps HBM busy through the barriers, up to
+// the ring depth.  Every wait is bounded: on timeout the kernel records an
+// error code, stops issuing work, drains its own bulk copies and exits.
+#include "vb_common.cuh"
+#include "vb_kernels.cuh"
+#include "vb_device.cuh"
+#include "vb_stream.cuh"
+
+namespace vb {
+
+struct StreamOp {
+    const uint8_t *w;       // Q8_0 qs int8 [N][K] or fp16 [N][K]
+    const uint16_t *sc;     // Q8_0 scales fp16 [N][K/32]
+    const float *x;
+    float *y;
+    const float *bias;
+    int64_t ldx, ldy;
+    int wtype, K, N, M;
+    unsigned flags;
+    int group, wait_group, last_in_group;
+    int rows_per_chunk, row_bytes, sc_bulk;
+};
+
+constexpr int ST_STAGES = 5;
+constexpr int ST_SLOT = 32768;                  // weight bytes per ring stage
+constexpr int ST_SC_SLOT = ST_SLOT / 16;        // Q8_0 scale bytes per stage
+constexpr int ST_CONSUMER_WARPS = 8;
+constexpr int ST_CONSUMERS = ST_CONSUMER_WARPS * 32;
+constexpr int ST_THREADS = ST_CONSUMERS + 32;
+constexpr int ST_XBYTES = 16384;                // activation operand (int8 or fp16)
+constexpr int ST_MMAX = 8;
+constexpr size_t ST_SMEM = (size_t)ST_STAGES * ST_SLOT + (size_t)ST_STAGES * ST_SC_SLOT + ST_XBYTES +
+                           (ST_XBYTES / 32) * 4 + 2 * ST_STAGES * 8 + 64;
+
+__device__ __forceinline__ void stream_store(const StreamOp &op, int m, int64_t n, float v) {
+    if (op.bias) v = __fadd_rn(v, op.bias[n]);
+    if (op.flags & VB_OUT_BF16) v = bf16r(v);
+    op.y[(int64_t)m * op.ldy + n] = v;
+}
+
+// Bounded wait on an mbarrier phase; false on timeout or abort.
+__device__ __forceinline__ bool wait_phase(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort_flag) return false;
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
+    }
+    return true;
+}
+
+__device__ __forceinline__ bool wait_grid(const unsigned *ctr, unsigned target, volatile int *abort_flag) {
+    const long long t0 = clock64();
+    while (ld_acquire_gpu(ctr) < target) {
+        if (*abort_flag) return false;
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
+        __nanosleep(64);
+    }
+    return true;
+}
+
+__device__ __forceinline__ void rows_of(int64_t N, int cta, int G, int64_t &r0, int64_t &r1) {
+    r0 = N * cta / G;
+    r1 = N * (cta + 1) / G;
+}
+
+__global__ void __launch_bounds__(ST_THREADS, 1)
+    stream_gemv_kernel(const StreamOp *__restrict__ ops, int n_ops, unsigned *bars, int *err) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    uint8_t *wslot = sm;
+    uint8_t *sslot = wslot + (size_t)ST_STAGES * ST_SLOT;
+    int8_t *xq = reinterpret_cast<int8_t *>(sslot + (size_t)ST_STAGES * ST_SC_SLOT);
+    float *xd = reinterpret_cast<float *>(xq + ST_XBYTES);
+    uint64_t *full = reinterpret_cast<uint64_t *>(xd + ST_XBYTES / 32);
+    uint64_t *empty = full + ST_STAGES;
+    __shared__ volatile int s_abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x, cta = blockIdx.x;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ST_STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], ST_CONSUMER_WARPS);
+        }
+        s_abort = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    // ------------------------------------------------------------ producer
+    if (warp == 0) {
+        if (lane != 0) return;
+        int slot = 0;
+        uint32_t phase = 0;
+        long long fills = 0;
+        for (int i = 0; i < n_ops && !s_abort; i++) {
+            const StreamOp &op = ops[i];
+            int64_t r0, r1;
+            rows_of(op.N, cta, G, r0, r1);
+            const int R = op.rows_per_chunk;
+            const int nb = op.K / QK;
+            for (int64_t r = r0; r < r1; r += R) {
+                const int nr = (int)((r1 - r) < R ? (r1 - r) : R);
+                if (!wait_phase(&empty[slot], phase ^ 1u, &s_abort)) {
+                    if (!s_abort) { atomicCAS(err, 0, STREAM_TIMEOUT_EMPTY); s_abort = 1; }
+                    break;
+                }
+                const uint32_t wb = (uint32_t)nr * (uint32_t)op.row_bytes;
+                const uint32_t sb = op.sc_bulk ? (uint32_t)nr * (uint32_t)nb * 2u : 0u;
+                mbar_arrive_expect_tx(&full[slot], wb + sb);
+                bulk_g2s(wslot + (size_t)slot * ST_SLOT, op.w + r * op.row_bytes, wb, &full[slot]);
+                if (sb) bulk_g2s(sslot + (size_t)slot * ST_SC_SLOT, op.sc + r * nb, sb, &full[slot]);
+                fills++;
+                if (++slot == ST_STAGES) { slot = 0; phase ^= 1u; }
+            }
+        }
+        // Drain: the last fill of every stage must have landed before this
+        // thread exits (normally the consumers have already seen it).
+        for (int s = 0; s < ST_STAGES; s++) {
+            const long long n_s = fills / ST_STAGES + ((fills % ST_STAGES) > s ? 1 : 0);
+            if (n_s == 0) continue;
+            const uint32_t par = (uint32_t)((n_s - 1) & 1);
+            const long long t0 = clock64();
+            while (!mbar_try_wait(&full[s], par)) {
+                if (clock64() - t0 > WAIT_LIMIT_CYCLES) { atomicCAS(err, 0, STREAM_TIMEOUT_FULL); break; }
+            }
+        }
+        return;
+    }
+
+    // ----------------------------------------------------------- consumers
+    const int ctid = threadIdx.x - 32, cw = warp - 1;
+    int slot = 0;
+    uint32_t phase = 0;
+    const float *last_x = nullptr;
+    int last_K = -1, last_M = -1, last_type = -1;
+    int64_t last_ldx = -1;
+    bool bad = false;   // this thread saw a timeout or an abort
+    // Every consumer_sync / consumer_sync_or below is executed by all
+    // consumer warps in the same order; loops end only on a uniform flag.
+    for (int i = 0; i < n_ops; i++) {
+        const StreamOp &op = ops[i];
+        if (consumer_sync_or(bad || s_abort, ST_CONSUMERS)) break;
+        if (op.wait_group >= 0) {
+            if (ctid == 0 && !wait_grid(bars + op.wait_group, (unsigned)G, &s_abort)) {
+                if (!s_abort) { atomicCAS(err, 0, STREAM_TIMEOUT_GRID); s_abort = 1; }
+                bad = true;
+            }
+            if (consumer_sync_or(bad, ST_CONSUMERS)) break;
+            last_x = nullptr;   // the activation may have been rewritten
+        }
+        const int K = op.K, M = op.M, nb = K / QK;
+        int64_t r0, r1;
+        rows_of(op.N, cta, G, r0, r1);
+        if (r1 > r0 &&
+            !(op.x == last_x && K == last_K && M == last_M && op.wtype == last_type && op.ldx == last_ldx)) {
+            if (op.wtype == VB_TYPE_Q8_0) {
+                // one thread per 32-value block, ggml's rule, bit-exact
+                for (int b = ctid; b < M * nb; b += ST_CONSUMERS) {
+                    const int m = b / nb, kb = b % nb;
+                    const float4 *src = reinterpret_cast<const float4 *>(op.x + (int64_t)m * op.ldx + kb * QK);
+                    float v[32];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const float4 f = __ldcg(src + j);
+                        v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+                    }
+                    float amax = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(v[j]));
+                    const float d = __fdiv_rn(amax, 127.0f);
+                    const uint16_t dh = f2h(d);
+                    const float id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
+                    uint32_t packed[8];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        uint32_t w4 = 0;
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const int q = __float2int_rn(__fmul_rn(v[4 * j + e], id));
+                            w4 |= ((uint32_t)(q & 0xff)) << (8 * e);
+                        }
+                        packed[j] = w4;
+                    }
+                    int4 *dst = reinterpret_cast<int4 *>(xq + (int64_t)m * K + kb * QK);
+                    dst[0] = make_int4(packed[0], packed[1], packed[2], packed[3]);
+                    dst[1] = make_int4(packed[4], packed[5], packed[6], packed[7]);
+                    xd[m * nb + kb] = h2f(dh);
+                }
+            } else {
+                uint16_t *xh = reinterpret_cast<uint16_t *>(xq);
+                for (int e = ctid; e < M * K; e += ST_CONSUMERS) {
+                    const int m = e / K, k = e % K;
+                    xh[e] = f2h(__ldcg(op.x + (int64_t)m * op.ldx + k));
+                }
+            }
+            consumer_sync(ST_CONSUMERS);
+            last_x = op.x;
+            last_K = K;
+            last_M = M;
+            last_type = op.wtype;
+            last_ldx = op.ldx;
+        }
+
+        const int R = op.rows_per_chunk;
+        for (int64_t r = r0; r < r1; r += R) {
+            const int nr = (int)((r1 - r) < R ? (r1 - r) : R);
+            if (!wait_phase(&full[slot], phase, &s_abort)) {
+                if (!s_abort) { atomicCAS(err, 0, STREAM_TIMEOUT_FULL); s_abort = 1; }
+                bad = true;
+                break;
+            }
+            const uint8_t *wt = wslot + (size_t)slot * ST_SLOT;
+            if (op.wtype == VB_TYPE_Q8_0) {
+                const uint16_t *sct = op.sc_bulk ? reinterpret_cast<const uint16_t *>(sslot + (size_t)slot * ST_SC_SLOT)
+                                                 : op.sc + r * nb;
+                for (int j = cw; j < nr; j += ST_CONSUMER_WARPS) {
+                    float acc[ST_MMAX];
+#pragma unroll
+                    for (int m = 0; m < ST_MMAX; m++) acc[m] = 0.0f;
+                    const int8_t *wr = reinterpret_cast<const int8_t *>(wt) + (int64_t)j * K;
+                    for (int c = lane; c < K / 16; c += 32) {
+                        const int4 wv = *reinterpret_cast<const int4 *>(wr + c * 16);
+                        const float sw = h2f(sct[j * nb + (c >> 1)]);
+#pragma unroll
+                        for (int m = 0; m < ST_MMAX; m++) {
+                            if (m < M) {
+                                const int4 xv = *reinterpret_cast<const int4 *>(xq + m * K + c * 16);
+                                acc[m] = fmaf((float)dot16_i8(wv, xv), __fmul_rn(sw, xd[m * nb + (c >> 1)]), acc[m]);
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int m = 0; m < ST_MMAX; m++) {
+                        if (m < M) {
+                            const float v = warp_sum(acc[m]);
+                            if (lane == 0) stream_store(op, m, r + j, v);
+                        }
+                    }
+                }
+            } else {
+                const uint16_t *xh = reinterpret_cast<const uint16_t *>(xq);
+                for (int j = cw; j < nr; j += ST_CONSUMER_WARPS) {
+                    float acc[ST_MMAX];
+#pragma unroll
+                    for (int m = 0; m < ST_MMAX; m++) acc[m] = 0.0f;
+                    const uint8_t *wr = wt + (int64_t)j * K * 2;
+                    for (int c = lane; c < K / 8; c += 32) {
+                        const int4 wv = *reinterpret_cast<const int4 *>(wr + c * 16);
+#pragma unroll
+                        for (int m = 0; m < ST_MMAX; m++) {
+                            if (m < M) {
+                                const int4 xv = *reinterpret_cast<const int4 *>(xh + m * K + c * 8);
+                                acc[m] = dot8_f16(wv, xv, acc[m]);
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int m = 0; m < ST_MMAX; m++) {
+                        if (m < M) {
+                            const float v = warp_sum(acc[m]);
+                            if (lane == 0) stream_store(op, m, r + j, v);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (++slot == ST_STAGES) { slot = 0; phase ^= 1u; }
+        }
+        if (consumer_sync_or(bad, ST_CONSUMERS)) break;
+        if (op.last_in_group && ctid == 0) {
+            __threadfence();
+            red_release_gpu(bars + op.group, 1u);
+        }
+    }
+}
+
+}  // namespace vb
+
+using namespace vb;
+
+struct vb_program_s {
+    StreamOp *d_ops = nullptr;
+    unsigned *d_bars = nullptr;
+    int *d_err = nullptr;
+    int n_ops = 0, n_groups = 0, grid = 0;
+    size_t weight_bytes = 0;
+};
+
+namespace vb {
+int init_stream(vb_ctx *ctx) {
+    VB_CHECK(ctx, cudaFuncSetAttribute(stream_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ST_SMEM));
+    return VB_OK;
+}
+}  // namespace vb
+
+extern "C" int vb_program_create(vb_ctx *ctx, int n_ops, const vb_gemv_op *ops, vb_program *out) {
+    if (!ctx || n_ops <= 0 || !ops || !out) return VB_ERR_INVALID_ARG;
+    *out = nullptr;
+    std::vector<StreamOp> h(n_ops);
+    int n_groups = 0;
+    size_t wbytes = 0;
+    for (int i = 0; i < n_ops; i++) {
+        const vb_gemv_op &o = ops[i];
+        StreamOp &s = h[i];
+        vb_weight w = o.w;
+        if (!w || !o.x || !o.y || o.M < 1 || o.M > ST_MMAX)
+            return set_error(ctx, VB_ERR_INVALID_ARG, "program op %d: null pointer or M outside 1..%d", i, ST_MMAX);
+        if (w->type != VB_TYPE_Q8_0 && w->type != VB_TYPE_F16)
+            return set_error(ctx, VB_ERR_INVALID_ARG, "program op %d: weight type must be Q8_0 or F16", i);
+        if (o.group < 0 || (i > 0 && o.group < ops[i - 1].group) || o.wait_group >= o.group)
+            return set_error(ctx, VB_ERR_INVALID_ARG, "program op %d: groups must be non-decreasing and wait on an earlier group", i);
+        if (i > 0 && o.group != ops[i - 1].group && o.group != ops[i - 1].group + 1)
+            return set_error(ctx, VB_ERR_INVALID_ARG, "program op %d: group ids must be consecutive", i);
+        const int K = (int)w->K;
+        s.wtype = w->type;
+        s.K = K;
+        s.N = (int)w->N;
+        s.M = o.M;
+        s.w = (const uint8_t *)w->data;
+        s.sc = w->scales;
+        s.x = o.x;
+        s.y = o.y;
+        s.bias = o.bias;
+        s.ldx = o.ldx ? o.ldx : K;
+        s.ldy = o.ldy ? o.ldy : w->N;
+        s.flags = o.flags;
+        s.group = o.group;
+        s.wait_group = o.wait_group;
+        s.last_in_group = (i == n_ops - 1) || (ops[i + 1].group != o.group);
+        s.row_bytes = w->type == VB_TYPE_Q8_0 ? K : 2 * K;
+        s.rows_per_chunk = ST_SLOT / s.row_bytes;
+        s.sc_bulk = (w->type == VB_TYPE_Q8_0) && (K % 256 == 0);
+        if (s.rows_per_chunk < 1 || s.row_bytes % 16)
+            return set_error(ctx, VB_ERR_INVALID_ARG, "program op %d: K=%d not supported by the streaming kernel", i, K);
+        const int xbytes = (w->type == VB_TYPE_Q8_0 ? 1 : 2) * K * o.M;
+        if (xbytes > ST_XBYTES)
+            return set_error(ctx, VB_ERR_INVALID_ARG, "program op %d: M*K operand exceeds %d bytes", i, ST_XBYTES);
+        if (((uintptr_t)o.x & 15) || (s.ldx & 3))
+            return set_error(ctx, VB_ERR_INVALID_ARG, "program op %d: x rows must be 16-byte aligned", i);
+        n_groups = o.group + 1;
+        wbytes += w->device_bytes;
+    }
+    int per_sm = 0;
+    VB_CHECK(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stream_gemv_kernel, ST_THREADS, ST_SMEM));
+    if (per_sm < 1) return set_error(ctx, VB_ERR_BACKEND, "streaming kernel does not fit on an SM");
+    vb_program p = new vb_program_s();
+    p->n_ops = n_ops;
+    p->n_groups = n_groups;
+    p->grid = ctx->sm_count;
+    p->weight_bytes = wbytes;
+    cudaError_t e = cudaMalloc(&p->d_ops, sizeof(StreamOp) * n_ops);
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_bars, sizeof(unsigned) * n_groups);
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_err, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemcpy(p->d_ops, h.data(), sizeof(StreamOp) * n_ops, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(p->d_err, 0, sizeof(int));
+    if (e != cudaSuccess) {
+        vb_program_destroy(p);
+        return check_cuda(ctx, e, "vb_program_create");
+    }
+    *out = p;
+    return VB_OK;
+}
+
+extern "C" int vb_program_run(vb_ctx *ctx, vb_program p) {
+    if (!ctx || !p) return VB_ERR_INVALID_ARG;
+    VB_CHECK(ctx, cudaMemsetAsync(p->d_bars, 0, sizeof(unsigned) * p->n_groups, ctx->stream));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p->grid);
+    cfg.blockDim = dim3(ST_THREADS);
+    cfg.dynamicSmemBytes = ST_SMEM;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    VB_CHECK(ctx, cudaLaunchKernelEx(&cfg, stream_gemv_kernel, (const StreamOp *)p->d_ops, p->n_ops, p->d_bars,
+                                     p->d_err));
+    VB_LAUNCH_CHECK(ctx, "stream_gemv");
+    return VB_OK;
+}
+
+extern "C" int vb_program_status(vb_ctx *ctx, vb_program p, int *device_error) {
+    if (!ctx || !p || !device_error) return VB_ERR_INVALID_ARG;
+    VB_CHECK(ctx, cudaStreamSynchronize(ctx->stream));
+    VB_CHECK(ctx, cudaMemcpy(device_error, p->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (*device_error) return set_error(ctx, VB_ERR_BACKEND, "streaming kernel reported error %d", *device_error);
+    return VB_OK;
+}
+
+extern "C" void vb_program_destroy(vb_program p) {
+    if (!p) return;
+    cudaFree(p->d_ops);
+    cudaFree(p->d_bars);
+    cudaFree(p->d_err);
+    delete p;
+}

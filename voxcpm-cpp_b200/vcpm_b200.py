@@ -45,6 +45,12 @@ class DiTConfig(C.Structure):
                                        "feat_dim", "patch")] + [("eps", C.c_float), ("wtype", C.c_int)]
 
 
+class GemvOp(C.Structure):
+    _fields_ = [("w", C.c_void_p), ("x", C.c_void_p), ("ldx", C.c_int64), ("y", C.c_void_p), ("ldy", C.c_int64),
+                ("bias", C.c_void_p), ("flags", C.c_uint), ("M", C.c_int), ("group", C.c_int),
+                ("wait_group", C.c_int)]
+
+
 class DiTHost(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in (
         "in_proj", "cond_proj", "out_proj", "in_bias", "cond_bias", "out_bias",
@@ -83,6 +89,10 @@ SIGNATURES = {
     "vb_weight_info": (_I, [_P, C.POINTER(_I), C.POINTER(_I64), C.POINTER(_I64), C.POINTER(_SZ)]),
     "vb_matmul": (_I, [_P, _P, _P, _I64, _P, _U]),
     "vb_matmul_bias": (_I, [_P, _P, _P, _I64, _P, _P, _U]),
+    "vb_program_create": (_I, [_P, _I, _P, C.POINTER(_P)]),
+    "vb_program_run": (_I, [_P, _P]),
+    "vb_program_status": (_I, [_P, _P, C.POINTER(_I)]),
+    "vb_program_destroy": (None, [_P]),
     "vb_quantize_q8_0": (_I, [_P, _P, _I64, _I64, _P, _I]),
     "vb_dequantize_q8_0": (_I, [_P, _P, _I64, _P]),
     "vb_rms_norm": (_I, [_P, _P, _P, _P, _I64, _I64, _F, _U]),
@@ -267,6 +277,35 @@ class Context:
     def kv_write(self, k, v, kc, vc, n_rows, T, n_kv, head_dim, dst_row):
         self.check(self.L.vb_kv_write(self.h, _addr(k), _addr(v), _addr(kc), _addr(vc), n_rows, T, n_kv, head_dim,
                                       _addr(dst_row)))
+
+
+class Program:
+    """A weight-streaming GEMV program (vb_program).  ops: list of dicts
+    with keys w (Weight), x, y (device buffers), M, group, wait_group and
+    optional ldx, ldy, bias, flags."""
+
+    def __init__(self, ctx, ops):
+        self.ctx = ctx
+        arr = (GemvOp * len(ops))()
+        for i, o in enumerate(ops):
+            arr[i] = GemvOp(o["w"].h, _addr(o["x"]), o.get("ldx", 0), _addr(o["y"]), o.get("ldy", 0),
+                            _addr(o.get("bias")), o.get("flags", 0), o.get("M", 1), o["group"],
+                            o.get("wait_group", -1))
+        self.h = C.c_void_p()
+        ctx.check(ctx.L.vb_program_create(ctx.h, len(ops), arr, C.byref(self.h)))
+
+    def run(self):
+        self.ctx.check(self.ctx.L.vb_program_run(self.ctx.h, self.h))
+
+    def status(self):
+        e = C.c_int(0)
+        rc = self.ctx.L.vb_program_status(self.ctx.h, self.h, C.byref(e))
+        return rc, e.value
+
+    def close(self):
+        if self.h:
+            self.ctx.L.vb_program_destroy(self.h)
+            self.h = C.c_void_p()
 
 
 class Weight:
