@@ -370,6 +370,39 @@ def run_b200(args, rank, world, local_rank):
     return 0
 
 
+def run_config1(args, local_rank):
+    """Profiling case: BASELINE config 1 (Q8_0 W[2048 -> 6144], M=1) as a
+    streaming program over `--copies` distinct weights (56 = 750 MB > L2),
+    run warmup + steps times.  Prints one JSON line with GB/s per GEMV."""
+    import torch
+    import vcpm_b200 as vb
+    torch.cuda.set_device(local_rank)
+    ctx = vb.Context(local_rank)
+    rng = np.random.default_rng(99)
+    ws = [ctx.weight(vb.TYPE_Q8_0, 2048, 6144, synth_q8_0(rng, 6144, 2048)) for _ in range(args.copies)]
+    x = torch.randn(2048, device="cuda")
+    y = torch.zeros(6144, device="cuda")
+    torch.cuda.synchronize()
+    prog = vb.Program(ctx, [dict(w=w, x=x, y=y, M=1, group=0) for w in ws])
+    ev0, ev1 = ctx.event(), ctx.event()
+    for _ in range(args.warmup):
+        prog.run()
+    ctx.record(ev0)
+    for _ in range(args.steps):
+        prog.run()
+    ctx.record(ev1)
+    ms = ctx.elapsed_ms(ev0, ev1)
+    rc, derr = prog.status()
+    per = ms / (args.steps * len(ws))
+    print(json.dumps({"mode": "config1", "copies": len(ws), "us_per_gemv": per * 1e3,
+                      "gbs": alg_bytes(2048, 6144) / (per * 1e-3) / 1e9, "device_error": derr}), flush=True)
+    prog.close()
+    for w in ws:
+        w.release()
+    ctx.close()
+    return 0 if rc == 0 else 1
+
+
 def decode_bench(ctx, host_layers, args):
     """Secondary metric: MiniCPM4 28-layer decode tokens/s (
     256-token prefill, then single-token steps against a bf16 KV cache of 512
@@ -423,6 +456,9 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=64)
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--mode", default="full", choices=["full", "config1"],
+                    help="config1: only the config-1 streaming program (profiling case)")
+    ap.add_argument("--copies", type=int, default=56)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -431,6 +467,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.mode == "config1":
+        return run_config1(args, local_rank)
     if world > 1:
         import datetime
         import torch
