@@ -15,7 +15,7 @@
 #include <vector>
 #include <mutex>
 
-#include "../../include/vcpm_b200.h"
+#include "vcpm_b200.h"
 
 namespace vb {
 

@@ -85,6 +85,112 @@ __device__ __forceinline__ void rows_of(int64_t N, int cta, int G, int64_t &r0, 
     r1 = N * (cta + 1) / G;
 }
 
+__device__ __forceinline__ int dot32_i8(const int4 &a0, const int4 &a1, const int4 &b0, const int4 &b1) {
+    // two independent dp4a chains, joined at the end (exact int32)
+    int s0 = __dp4a(a0.x, b0.x, 0), s1 = __dp4a(a1.x, b1.x, 0);
+    s0 = __dp4a(a0.y, b0.y, s0);
+    s1 = __dp4a(a1.y, b1.y, s1);
+    s0 = __dp4a(a0.z, b0.z, s0);
+    s1 = __dp4a(a1.z, b1.z, s1);
+    s0 = __dp4a(a0.w, b0.w, s0);
+    s1 = __dp4a(a1.w, b1.w, s1);
+    return s0 + s1;
+}
+
+// One ring chunk of a Q8_0 op: warp cw reduces rows 2cw, 2cw+1 (then +16,
+// ...); each lane owns whole 32-value blocks, so one scale pair serves 32
+// products.  y[m][n] = sum_b float(isum_b) * (d_w * d_x).  MC is the exact
+// number of activation rows, so no predicated work is issued for absent rows.
+template <int MC>
+__device__ __forceinline__ void q8_chunk(const StreamOp &op, const uint8_t *__restrict__ wt,
+                                         const uint16_t *__restrict__ sct, const int8_t *__restrict__ xq,
+                                         const float *__restrict__ xd, int nr, int cw, int lane, int64_t r) {
+    const int K = op.K, nb = K >> 5;
+    for (int j0 = 2 * cw; j0 < nr; j0 += 2 * ST_CONSUMER_WARPS) {
+        const bool two = (j0 + 1) < nr;
+        const int8_t *w0 = reinterpret_cast<const int8_t *>(wt) + (int64_t)j0 * K;
+        const int8_t *w1 = w0 + (two ? K : 0);
+        float acc0[MC], acc1[MC];
+#pragma unroll
+        for (int m = 0; m < MC; m++) { acc0[m] = 0.0f; acc1[m] = 0.0f; }
+#pragma unroll 2
+        for (int b = lane; b < nb; b += 32) {
+            const int4 a0 = *reinterpret_cast<const int4 *>(w0 + b * 32);
+            const int4 a1 = *reinterpret_cast<const int4 *>(w0 + b * 32 + 16);
+            const int4 c0 = *reinterpret_cast<const int4 *>(w1 + b * 32);
+            const int4 c1 = *reinterpret_cast<const int4 *>(w1 + b * 32 + 16);
+            const float s0 = h2f(sct[j0 * nb + b]);
+            const float s1 = h2f(sct[(j0 + (two ? 1 : 0)) * nb + b]);
+#pragma unroll
+            for (int m = 0; m < MC; m++) {
+                const int4 x0 = *reinterpret_cast<const int4 *>(xq + m * K + b * 32);
+                const int4 x1 = *reinterpret_cast<const int4 *>(xq + m * K + b * 32 + 16);
+                const float dx = xd[m * nb + b];
+                acc0[m] = fmaf((float)dot32_i8(a0, a1, x0, x1), __fmul_rn(s0, dx), acc0[m]);
+                acc1[m] = fmaf((float)dot32_i8(c0, c1, x0, x1), __fmul_rn(s1, dx), acc1[m]);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MC; m++) {
+            const float v0 = warp_sum(acc0[m]);
+            const float v1 = warp_sum(acc1[m]);
+            if (lane == 0) {
+                stream_store(op, m, r + j0, v0);
+                if (two) stream_store(op, m, r + j0 + 1, v1);
+            }
+        }
+    }
+}
+
+// One ring chunk of an F16 op: lanes own 16-value (32-byte) pieces of a row,
+// fp16 x fp16 products accumulated in fp32.
+template <int MC>
+__device__ __forceinline__ void f16_chunk(const StreamOp &op, const uint8_t *__restrict__ wt,
+                                          const uint16_t *__restrict__ xh, int nr, int cw, int lane, int64_t r) {
+    const int K = op.K, np = K >> 4;
+    for (int j0 = 2 * cw; j0 < nr; j0 += 2 * ST_CONSUMER_WARPS) {
+        const bool two = (j0 + 1) < nr;
+        const uint8_t *w0 = wt + (int64_t)j0 * K * 2;
+        const uint8_t *w1 = w0 + (two ? K * 2 : 0);
+        float acc0[MC], acc1[MC];
+#pragma unroll
+        for (int m = 0; m < MC; m++) { acc0[m] = 0.0f; acc1[m] = 0.0f; }
+#pragma unroll 2
+        for (int p = lane; p < np; p += 32) {
+            const int4 a0 = *reinterpret_cast<const int4 *>(w0 + p * 32);
+            const int4 a1 = *reinterpret_cast<const int4 *>(w0 + p * 32 + 16);
+            const int4 c0 = *reinterpret_cast<const int4 *>(w1 + p * 32);
+            const int4 c1 = *reinterpret_cast<const int4 *>(w1 + p * 32 + 16);
+#pragma unroll
+            for (int m = 0; m < MC; m++) {
+                const int4 x0 = *reinterpret_cast<const int4 *>(xh + m * K + p * 16);
+                const int4 x1 = *reinterpret_cast<const int4 *>(xh + m * K + p * 16 + 8);
+                acc0[m] = dot8_f16(a1, x1, dot8_f16(a0, x0, acc0[m]));
+                acc1[m] = dot8_f16(c1, x1, dot8_f16(c0, x0, acc1[m]));
+            }
+        }
+        if ((K & 15) && lane == 0) {   // tail of 8 values (K a multiple of 8, not 16)
+            const int4 a0 = *reinterpret_cast<const int4 *>(w0 + np * 32);
+            const int4 c0 = *reinterpret_cast<const int4 *>(w1 + np * 32);
+#pragma unroll
+            for (int m = 0; m < MC; m++) {
+                const int4 x0 = *reinterpret_cast<const int4 *>(xh + m * K + np * 16);
+                acc0[m] = dot8_f16(a0, x0, acc0[m]);
+                acc1[m] = dot8_f16(c0, x0, acc1[m]);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MC; m++) {
+            const float v0 = warp_sum(acc0[m]);
+            const float v1 = warp_sum(acc1[m]);
+            if (lane == 0) {
+                stream_store(op, m, r + j0, v0);
+                if (two) stream_store(op, m, r + j0 + 1, v1);
+            }
+        }
+    }
+}
+
 __global__ void __launch_bounds__(ST_THREADS, 1)
     stream_gemv_kernel(const StreamOp *__restrict__ ops, int n_ops, unsigned *bars, int *err) {
     extern __shared__ __align__(128) uint8_t sm[];
@@ -235,54 +341,27 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             if (op.wtype == VB_TYPE_Q8_0) {
                 const uint16_t *sct = op.sc_bulk ? reinterpret_cast<const uint16_t *>(sslot + (size_t)slot * ST_SC_SLOT)
                                                  : op.sc + r * nb;
-                for (int j = cw; j < nr; j += ST_CONSUMER_WARPS) {
-                    float acc[ST_MMAX];
-#pragma unroll
-                    for (int m = 0; m < ST_MMAX; m++) acc[m] = 0.0f;
-                    const int8_t *wr = reinterpret_cast<const int8_t *>(wt) + (int64_t)j * K;
-                    for (int c = lane; c < K / 16; c += 32) {
-                        const int4 wv = *reinterpret_cast<const int4 *>(wr + c * 16);
-                        const float sw = h2f(sct[j * nb + (c >> 1)]);
-#pragma unroll
-                        for (int m = 0; m < ST_MMAX; m++) {
-                            if (m < M) {
-                                const int4 xv = *reinterpret_cast<const int4 *>(xq + m * K + c * 16);
-                                acc[m] = fmaf((float)dot16_i8(wv, xv), __fmul_rn(sw, xd[m * nb + (c >> 1)]), acc[m]);
-                            }
-                        }
-                    }
-#pragma unroll
-                    for (int m = 0; m < ST_MMAX; m++) {
-                        if (m < M) {
-                            const float v = warp_sum(acc[m]);
-                            if (lane == 0) stream_store(op, m, r + j, v);
-                        }
-                    }
+                switch (M) {
+                    case 1: q8_chunk<1>(op, wt, sct, xq, xd, nr, cw, lane, r); break;
+                    case 2: q8_chunk<2>(op, wt, sct, xq, xd, nr, cw, lane, r); break;
+                    case 3: q8_chunk<3>(op, wt, sct, xq, xd, nr, cw, lane, r); break;
+                    case 4: q8_chunk<4>(op, wt, sct, xq, xd, nr, cw, lane, r); break;
+                    case 5: q8_chunk<5>(op, wt, sct, xq, xd, nr, cw, lane, r); break;
+                    case 6: q8_chunk<6>(op, wt, sct, xq, xd, nr, cw, lane, r); break;
+                    case 7: q8_chunk<7>(op, wt, sct, xq, xd, nr, cw, lane, r); break;
+                    default: q8_chunk<8>(op, wt, sct, xq, xd, nr, cw, lane, r); break;
                 }
             } else {
                 const uint16_t *xh = reinterpret_cast<const uint16_t *>(xq);
-                for (int j = cw; j < nr; j += ST_CONSUMER_WARPS) {
-                    float acc[ST_MMAX];
-#pragma unroll
-                    for (int m = 0; m < ST_MMAX; m++) acc[m] = 0.0f;
-                    const uint8_t *wr = wt + (int64_t)j * K * 2;
-                    for (int c = lane; c < K / 8; c += 32) {
-                        const int4 wv = *reinterpret_cast<const int4 *>(wr + c * 16);
-#pragma unroll
-                        for (int m = 0; m < ST_MMAX; m++) {
-                            if (m < M) {
-                                const int4 xv = *reinterpret_cast<const int4 *>(xh + m * K + c * 8);
-                                acc[m] = dot8_f16(wv, xv, acc[m]);
-                            }
-                        }
-                    }
-#pragma unroll
-                    for (int m = 0; m < ST_MMAX; m++) {
-                        if (m < M) {
-                            const float v = warp_sum(acc[m]);
-                            if (lane == 0) stream_store(op, m, r + j, v);
-                        }
-                    }
+                switch (M) {
+                    case 1: f16_chunk<1>(op, wt, xh, nr, cw, lane, r); break;
+                    case 2: f16_chunk<2>(op, wt, xh, nr, cw, lane, r); break;
+                    case 3: f16_chunk<3>(op, wt, xh, nr, cw, lane, r); break;
+                    case 4: f16_chunk<4>(op, wt, xh, nr, cw, lane, r); break;
+                    case 5: f16_chunk<5>(op, wt, xh, nr, cw, lane, r); break;
+                    case 6: f16_chunk<6>(op, wt, xh, nr, cw, lane, r); break;
+                    case 7: f16_chunk<7>(op, wt, xh, nr, cw, lane, r); break;
+                    default: f16_chunk<8>(op, wt, xh, nr, cw, lane, r); break;
                 }
             }
             __syncwarp();
