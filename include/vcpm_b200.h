@@ -204,6 +204,32 @@ int vb_attention(vb_ctx *ctx, const float *q, const uint16_t *k,
                  const uint16_t *v, int n_rows, int T, int n_heads,
                  int n_kv_heads, int head_dim, const int32_t *row_start,
                  const int32_t *kv_len, float *out);
+
+/* vb_attention for callers that must not allocate device memory (no
+ * counterpart in the reference; this library adds it).  Some hosts cannot
+ * let a library call cudaMalloc: an embedding runtime whose own allocator
+ * has reserved the GPU's memory up front, or a real-time audio thread that
+ * cannot afford the device-wide synchronisation an allocation may cause.
+ * vb_attention keeps its per-chunk partial results (when n_rows > 64) in a
+ * buffer it grows with cudaMalloc; this variant keeps them instead in a
+ * fixed array compiled into the library, VB_ATTENTION_NOALLOC_SCRATCH_BYTES
+ * on every GPU that loads the library, held until the process exits.
+ * Arguments and results are those of vb_attention; the caller still passes
+ * every input and output buffer.  Limit: T * n_heads * ceil(n_rows / 64) *
+ * (head_dim + 2) * 4 bytes must not exceed the array size (for example one
+ * decode token with 16 heads of 128 over up to 8192 rows fits); larger calls
+ * return VB_ERR_INVALID_ARG with the sizes in vb_last_error().  The first
+ * call on each device looks up the array's device address, so make that
+ * first call before any stream capture.  All calls on a device share the
+ * one array: calls that overlap on the GPU (two streams, two contexts of
+ * the same device) race and corrupt each other's results.  Nothing in the
+ * array needs to start at zero; each call writes every entry it reads. */
+#define VB_ATTENTION_NOALLOC_SCRATCH_BYTES (4u << 20)
+int vb_attention_noalloc(vb_ctx *ctx, const float *q, const uint16_t *k,
+                         const uint16_t *v, int n_rows, int T, int n_heads,
+                         int n_kv_heads, int head_dim,
+                         const int32_t *row_start, const int32_t *kv_len,
+                         float *out);
 /* KV-cache append (src/minicpm4.c:299-320): writes bf16(k), bf16(v) of T
  * tokens (fp32 [T][n_kv_heads][head_dim]) into rows dst_row[t] of the
  * bf16 stores [n_kv_heads][n_rows][head_dim]. */

@@ -18,6 +18,8 @@
 #include "vb_common.cuh"
 #include "vb_kernels.cuh"
 
+#include <mutex>
+
 namespace vb {
 
 constexpr int ATT_CH = 64;         // K/V rows per CTA
@@ -235,4 +237,58 @@ int launch_attention(vb_ctx *ctx, const float *q, int64_t ldq, const uint16_t *k
                                  max_kv_len, out, ldo, part);
 }
 
+// ------------------------------------------------ allocation-free variant
+// Scratch for vb_attention_noalloc: the per-chunk (max, sum, partial output)
+// records of the flash-decoding split.  It lives in the library image, so
+// every device that loads the library holds these bytes until the process
+// exits, and no call ever allocates.  Host code must not pass the symbol
+// itself to a kernel (on the host it names a stand-in, not device memory);
+// noalloc_scratch() resolves the real device address once per device.
+constexpr size_t NOALLOC_SCRATCH_BYTES = VB_ATTENTION_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) float g_attn_noalloc_scratch[NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+constexpr int NOALLOC_MAX_DEVICES = 64;
+static std::mutex g_noalloc_mu;
+static float *g_noalloc_ptr[NOALLOC_MAX_DEVICES];
+
+// Device address of the scratch array on ctx's device; the first call per
+// device looks it up (with that device current) and caches it.
+static int noalloc_scratch(vb_ctx *ctx, float **out) {
+    if (ctx->device < 0 || ctx->device >= NOALLOC_MAX_DEVICES)
+        return set_error(ctx, VB_ERR_INVALID_ARG, "attention_noalloc: device id %d out of range", ctx->device);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[ctx->device]) {
+        VB_CHECK(ctx, cudaSetDevice(ctx->device));
+        void *p = nullptr;
+        VB_CHECK(ctx, cudaGetSymbolAddress(&p, g_attn_noalloc_scratch));
+        g_noalloc_ptr[ctx->device] = (float *)p;
+    }
+    *out = g_noalloc_ptr[ctx->device];
+    return VB_OK;
+}
+
 }  // namespace vb
+
+using namespace vb;
+
+extern "C" int vb_attention_noalloc(vb_ctx *ctx, const float *q, const uint16_t *k, const uint16_t *v, int n_rows,
+                                    int T, int n_heads, int n_kv_heads, int head_dim, const int32_t *row_start,
+                                    const int32_t *kv_len, float *out) {
+    if (!ctx) return VB_ERR_INVALID_ARG;
+    if (!q || !k || !v || !row_start || !kv_len || !out || n_rows <= 0 || T < 0 || head_dim <= 0 || n_heads <= 0)
+        return set_error(ctx, VB_ERR_INVALID_ARG, "vb_attention_noalloc: bad argument");
+    // same grid as vb_attention: the chunk count comes from n_rows
+    const size_t need = attention_scratch_bytes(T, n_heads, head_dim, n_rows);
+    if (need > NOALLOC_SCRATCH_BYTES)
+        return set_error(ctx, VB_ERR_INVALID_ARG,
+                         "vb_attention_noalloc: needs %zu bytes of scratch (T=%d, heads=%d, head_dim=%d, rows=%d); "
+                         "the fixed scratch holds %zu bytes -- use vb_attention or fewer rows/tokens per call",
+                         need, T, n_heads, head_dim, n_rows, (size_t)NOALLOC_SCRATCH_BYTES);
+    float *part = nullptr;
+    if (need) {
+        int rc = noalloc_scratch(ctx, &part);
+        if (rc) return rc;
+    }
+    return launch_attention_with(ctx, q, 0, k, v, n_rows, T, n_heads, n_kv_heads, head_dim, row_start, kv_len,
+                                 n_rows, out, 0, part);
+}

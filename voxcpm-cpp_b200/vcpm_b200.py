@@ -102,6 +102,7 @@ SIGNATURES = {
     "vb_rope_neox": (_I, [_P, _P, _I, _I, _I, _P, _F, _U]),
     "vb_fsq_quantize": (_I, [_P, _P, _I64, _F]),
     "vb_attention": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P]),
+    "vb_attention_noalloc": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P]),
     "vb_kv_write": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P]),
     "vb_lm_create": (_I, [_P, _P, _P, _P, C.POINTER(_P)]),
     "vb_lm_destroy": (None, [_P, _P]),
@@ -273,6 +274,11 @@ class Context:
     def attention(self, q, k, v, n_rows, T, n_heads, n_kv, head_dim, row_start, kv_len, out):
         self.check(self.L.vb_attention(self.h, _addr(q), _addr(k), _addr(v), n_rows, T, n_heads, n_kv, head_dim,
                                        _addr(row_start), _addr(kv_len), _addr(out)))
+
+    def attention_noalloc(self, q, k, v, n_rows, T, n_heads, n_kv, head_dim, row_start, kv_len, out):
+        """vb_attention without any device allocation (fixed library scratch)."""
+        self.check(self.L.vb_attention_noalloc(self.h, _addr(q), _addr(k), _addr(v), n_rows, T, n_heads, n_kv,
+                                               head_dim, _addr(row_start), _addr(kv_len), _addr(out)))
 
     def kv_write(self, k, v, kc, vc, n_rows, T, n_kv, head_dim, dst_row):
         self.check(self.L.vb_kv_write(self.h, _addr(k), _addr(v), _addr(kc), _addr(vc), n_rows, T, n_kv, head_dim,
