@@ -191,6 +191,76 @@ __device__ __forceinline__ void f16_chunk(const StreamOp &op, const uint8_t *__r
     }
 }
 
+// Decode fast path (Q8_0, M = 1): LPR lanes own one weight row, lane s of a
+// row handles the 16-byte half-blocks s, s+LPR, ..., so every quarter-warp
+// reads 128 contiguous shared-memory bytes (no bank conflicts).  The lane's
+// slice of the quantized activation (IT half-blocks) and its scales stay in
+// registers for the whole op, so shared memory carries only the weights.
+// Each half-block contributes float(isum_16) * (d_w * d_x); a row is reduced
+// over its LPR lanes.  Returns false on a timeout or an abort.
+template <int LPR, int IT>
+__device__ __forceinline__ bool q8_m1_op(const StreamOp &op, const uint8_t *wslot, const uint8_t *sslot,
+                                         const int8_t *xq, const float *xd, uint64_t *full, uint64_t *empty,
+                                         int &slot, uint32_t &phase, int64_t r0, int64_t r1, int cw, int lane,
+                                         volatile int *abort_flag, int *err) {
+    constexpr int RPW = 32 / LPR;                       // rows per warp per pass
+    constexpr int RPP = RPW * ST_CONSUMER_WARPS;        // rows per pass of all warps
+    const int K = op.K, nb = K >> 5;
+    const int ls = lane % LPR, lr = lane / LPR;
+    int4 xr[IT];
+    float dxr[IT];
+#pragma unroll
+    for (int i = 0; i < IT; i++) {
+        const int hb = ls + LPR * i;
+        xr[i] = *reinterpret_cast<const int4 *>(xq + hb * 16);
+        dxr[i] = xd[hb >> 1];
+    }
+    float *y = op.y;
+    const float *bias = op.bias;
+    const bool b16 = op.flags & VB_OUT_BF16;
+    const int R = op.rows_per_chunk;
+    const bool sc_bulk = op.sc_bulk != 0;
+    const uint16_t *scg = op.sc;
+    for (int64_t r = r0; r < r1; r += R) {
+        const int nr = (int)((r1 - r) < R ? (r1 - r) : R);
+        if (!wait_phase(&full[slot], phase, abort_flag)) {
+            if (!*abort_flag) { atomicCAS(err, 0, STREAM_TIMEOUT_FULL); *abort_flag = 1; }
+            return false;
+        }
+        const int8_t *wt = reinterpret_cast<const int8_t *>(wslot + (size_t)slot * ST_SLOT);
+        const uint16_t *sct = sc_bulk ? reinterpret_cast<const uint16_t *>(sslot + (size_t)slot * ST_SC_SLOT)
+                                      : scg + r * nb;
+        for (int jb = cw * RPW; jb < nr; jb += RPP) {   // warp-uniform
+            const int j = jb + lr;
+            const bool valid = j < nr;
+            const int jj = valid ? j : jb;
+            const int8_t *wr = wt + (int64_t)jj * K;
+            const uint16_t *sr = sct + jj * nb;
+            float acc = 0.0f;
+#pragma unroll
+            for (int i = 0; i < IT; i++) {
+                const int hb = ls + LPR * i;
+                const int4 wv = *reinterpret_cast<const int4 *>(wr + hb * 16);
+                const float s = __fmul_rn(h2f(sr[hb >> 1]), dxr[i]);
+                acc = fmaf((float)dot16_i8(wv, xr[i]), s, acc);
+            }
+#pragma unroll
+            for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (valid && ls == 0) {
+                float v = acc;
+                const int64_t n = r + j;
+                if (bias) v = __fadd_rn(v, bias[n]);
+                if (b16) v = bf16r(v);
+                y[n] = v;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (++slot == ST_STAGES) { slot = 0; phase ^= 1u; }
+    }
+    return true;
+}
+
 __global__ void __launch_bounds__(ST_THREADS, 1)
     stream_gemv_kernel(const StreamOp *__restrict__ ops, int n_ops, unsigned *bars, int *err) {
     extern __shared__ __align__(128) uint8_t sm[];
@@ -262,63 +332,87 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     const float *last_x = nullptr;
     int last_K = -1, last_M = -1, last_type = -1;
     int64_t last_ldx = -1;
+    int waited = -1;    // highest group this CTA has already waited for
     bool bad = false;   // this thread saw a timeout or an abort
     // Every consumer_sync / consumer_sync_or below is executed by all
     // consumer warps in the same order; loops end only on a uniform flag.
     for (int i = 0; i < n_ops; i++) {
         const StreamOp &op = ops[i];
-        if (consumer_sync_or(bad || s_abort, ST_CONSUMERS)) break;
-        if (op.wait_group >= 0) {
+        if (op.wait_group > waited) {
             if (ctid == 0 && !wait_grid(bars + op.wait_group, (unsigned)G, &s_abort)) {
                 if (!s_abort) { atomicCAS(err, 0, STREAM_TIMEOUT_GRID); s_abort = 1; }
                 bad = true;
             }
-            if (consumer_sync_or(bad, ST_CONSUMERS)) break;
+            if (consumer_sync_or(bad || s_abort, ST_CONSUMERS)) break;
+            waited = op.wait_group;
             last_x = nullptr;   // the activation may have been rewritten
         }
         const int K = op.K, M = op.M, nb = K / QK;
         int64_t r0, r1;
         rows_of(op.N, cta, G, r0, r1);
+        // The previous op ended with a consumer barrier, so no warp still
+        // reads the activation buffers when they are rewritten here.
         if (r1 > r0 &&
             !(op.x == last_x && K == last_K && M == last_M && op.wtype == last_type && op.ldx == last_ldx)) {
             if (op.wtype == VB_TYPE_Q8_0) {
-                // one thread per 32-value block, ggml's rule, bit-exact
-                for (int b = ctid; b < M * nb; b += ST_CONSUMERS) {
-                    const int m = b / nb, kb = b % nb;
-                    const float4 *src = reinterpret_cast<const float4 *>(op.x + (int64_t)m * op.ldx + kb * QK);
-                    float v[32];
+                // four threads per 32-value block (8 values each), ggml's
+                // rule, bit-exact: amax over the block, d = amax/127 (fp16),
+                // q = round-half-even(x * 127/amax)
+                const int total = M * nb * 4;
+                for (int base = 0; base < total; base += ST_CONSUMERS) {
+                    const int item = base + ctid;
+                    const bool valid = item < total;
+                    const int blk = valid ? (item >> 2) : 0, part = item & 3;
+                    const int m = blk / nb, kb = blk % nb;
+                    float v[8];
+                    if (valid) {
+                        const float4 *src =
+                            reinterpret_cast<const float4 *>(op.x + (int64_t)m * op.ldx + kb * QK + part * 8);
+                        const float4 f0 = __ldcg(src), f1 = __ldcg(src + 1);
+                        v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
+                        v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        const float4 f = __ldcg(src + j);
-                        v[4 * j] = f.x; v[4 * j + 1] = f.y; v[4 * j + 2] = f.z; v[4 * j + 3] = f.w;
+                        for (int e = 0; e < 8; e++) v[e] = 0.0f;
                     }
                     float amax = 0.0f;
 #pragma unroll
-                    for (int j = 0; j < 32; j++) amax = fmaxf(amax, fabsf(v[j]));
+                    for (int e = 0; e < 8; e++) amax = fmaxf(amax, fabsf(v[e]));
+                    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+                    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
                     const float d = __fdiv_rn(amax, 127.0f);
                     const uint16_t dh = f2h(d);
                     const float id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
-                    uint32_t packed[8];
+                    uint32_t pk[2];
 #pragma unroll
-                    for (int j = 0; j < 8; j++) {
+                    for (int h = 0; h < 2; h++) {
                         uint32_t w4 = 0;
 #pragma unroll
                         for (int e = 0; e < 4; e++) {
-                            const int q = __float2int_rn(__fmul_rn(v[4 * j + e], id));
+                            const int q = __float2int_rn(__fmul_rn(v[4 * h + e], id));
                             w4 |= ((uint32_t)(q & 0xff)) << (8 * e);
                         }
-                        packed[j] = w4;
+                        pk[h] = w4;
                     }
-                    int4 *dst = reinterpret_cast<int4 *>(xq + (int64_t)m * K + kb * QK);
-                    dst[0] = make_int4(packed[0], packed[1], packed[2], packed[3]);
-                    dst[1] = make_int4(packed[4], packed[5], packed[6], packed[7]);
-                    xd[m * nb + kb] = h2f(dh);
+                    if (valid) {
+                        *reinterpret_cast<uint2 *>(xq + (int64_t)m * K + kb * QK + part * 8) = make_uint2(pk[0], pk[1]);
+                        if (part == 0) xd[m * nb + kb] = h2f(dh);
+                    }
                 }
             } else {
+                // fp16 operand, 8 values per thread
                 uint16_t *xh = reinterpret_cast<uint16_t *>(xq);
-                for (int e = ctid; e < M * K; e += ST_CONSUMERS) {
-                    const int m = e / K, k = e % K;
-                    xh[e] = f2h(__ldcg(op.x + (int64_t)m * op.ldx + k));
+                const int total = M * K / 8;
+                for (int e = ctid; e < total; e += ST_CONSUMERS) {
+                    const int m = (e * 8) / K, k = (e * 8) % K;
+                    const float4 *src = reinterpret_cast<const float4 *>(op.x + (int64_t)m * op.ldx + k);
+                    const float4 f0 = __ldcg(src), f1 = __ldcg(src + 1);
+                    uint4 o;
+                    o.x = (uint32_t)f2h(f0.x) | ((uint32_t)f2h(f0.y) << 16);
+                    o.y = (uint32_t)f2h(f0.z) | ((uint32_t)f2h(f0.w) << 16);
+                    o.z = (uint32_t)f2h(f1.x) | ((uint32_t)f2h(f1.y) << 16);
+                    o.w = (uint32_t)f2h(f1.z) | ((uint32_t)f2h(f1.w) << 16);
+                    *reinterpret_cast<uint4 *>(xh + (int64_t)m * K + k) = o;
                 }
             }
             consumer_sync(ST_CONSUMERS);
@@ -329,8 +423,22 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             last_ldx = op.ldx;
         }
 
+        bool fast_done = false;
+        if (op.wtype == VB_TYPE_Q8_0 && M == 1) {
+            bool ok = true;
+            fast_done = true;
+            switch (K) {
+                case 1024: ok = q8_m1_op<16, 4>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err); break;
+                case 2048: ok = q8_m1_op<16, 8>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err); break;
+                case 4096: ok = q8_m1_op<16, 16>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err); break;
+                case 6144: ok = q8_m1_op<32, 12>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err); break;
+                case 8192: ok = q8_m1_op<32, 16>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err); break;
+                default: fast_done = false; break;
+            }
+            if (!ok) bad = true;
+        }
         const int R = op.rows_per_chunk;
-        for (int64_t r = r0; r < r1; r += R) {
+        for (int64_t r = r0; !fast_done && r < r1; r += R) {
             const int nr = (int)((r1 - r) < R ? (r1 - r) : R);
             if (!wait_phase(&full[slot], phase, &s_abort)) {
                 if (!s_abort) { atomicCAS(err, 0, STREAM_TIMEOUT_FULL); s_abort = 1; }
