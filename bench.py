@@ -3,12 +3,16 @@
 
 Headline metric: Q8_0 GEMV GB/s.  One step = the seven MiniCPM4 projection
 GEMVs (q/k/v/o 2048->2048/256/256/2048, gate/up 2048->6144, down 6144->2048;
-BASELINE config 2 shapes at M=1) for each of 28 layers: 196 launches over
+BASELINE config 2 shapes at M=1) for each of 28 layers: 196 GEMVs over
 1,403,781,120 bytes of distinct Q8_0 weights (larger than the 126 MB L2, so no
-flush is needed between steps).  Algorithmic bytes per GEMV = N*K*34/32 +
-4*K + 4*N.  `value` replays a CUDA graph of the step with inputs resident in
-HBM; `e2e` goes through the C ABI with pinned host buffers: one H2D of every
-step input, the graph, one D2H of every output, all inside the timed region.
+flush is needed between steps), run as one weight-streaming program.
+Algorithmic bytes per GEMV = N*K*34/32 + 4*K + 4*N.  `value` replays a CUDA
+graph of the step with inputs resident in HBM; `e2e` goes through the C ABI
+with pinned host buffers: one H2D of every step input, the graph, one D2H of
+every output, all inside the timed region.  Also reported: the same GEMVs
+ordered as the dependency chain of a decode layer (decode_chain_gbs), as 196
+separate launches, config 1 alone, the config-2 sweep over M and weight type,
+and 28-layer decode tokens/s.
 
 --impl reference times the CPU restatement of ggml's Q8_0 mat-mul (the
 oracle; ggml itself is not buildable here) on the host cores on a bounded
@@ -167,7 +171,8 @@ def load_peaks():
 
 
 def config_block(n):
-    return {"workload": "BASELINE config 2 projection set at M=1, Q8_0, 28 MiniCPM4 layers per step",
+    return {"workload": "BASELINE config 2 projection sweep at M=1, Q8_0: 196 independent GEMVs "
+                        "(7 MiniCPM4 projection shapes x 28 layers of distinct weights) per step",
             "shapes": {s[0]: [s[1], s[2]] for s in SHAPES}, "layers": LAYERS, "M": 1,
             "bytes_per_step": STEP_BYTES, "l2": "inputs larger than L2 (1.40 GB distinct weights per step)",
             "parallelism": f"independent replicas x{n}"}
@@ -215,26 +220,33 @@ def run_b200(args, rank, world, local_rank):
     Y = torch.zeros(LAYERS * OUT_PER_LAYER, dtype=torch.float32, device="cuda")
     torch.cuda.synchronize()
 
-    # The step as ONE weight-streaming program: per layer the dependency
-    # groups of a decode layer, q,k,v | o | gate,up | down, each group
-    # waiting for the previous one on every SM.
+    # The step (config 2's projection sweep at M=1: 196 independent GEMVs)
+    # as ONE weight-streaming program.  The decode-shaped variant orders the
+    # same GEMVs in the dependency groups of a decode layer,
+    # q,k,v | o | gate,up | down, each group waiting for the previous one on
+    # every SM (reported as decode_chain_gbs).
     GROUP_OF = {"q": 0, "k": 0, "v": 0, "o": 1, "gate": 2, "up": 2, "down": 3}
-    ops = []
+    ops, ops_chain = [], []
     xo, yo = X.data_ptr(), Y.data_ptr()
     i = 0
     for l in range(LAYERS):
         off = 0
         for name, K, N, slot in SHAPES:
             grp = 4 * l + GROUP_OF[name]
-            ops.append(dict(w=weights[i][3], x=xo + 4 * (l * IN_PER_LAYER + IN_OFF[slot]),
-                            y=yo + 4 * (l * OUT_PER_LAYER + off), M=1, group=grp,
-                            wait_group=grp - 1))
+            o = dict(w=weights[i][3], x=xo + 4 * (l * IN_PER_LAYER + IN_OFF[slot]),
+                     y=yo + 4 * (l * OUT_PER_LAYER + off), M=1)
+            ops.append(dict(o, group=0, wait_group=-1))
+            ops_chain.append(dict(o, group=grp, wait_group=grp - 1))
             off += N
             i += 1
     prog = vb.Program(ctx, ops)
     ctx.graph_begin()
     prog.run()
     g = ctx.graph_end()
+    prog_chain = vb.Program(ctx, ops_chain)
+    ctx.graph_begin()
+    prog_chain.run()
+    g_chain = ctx.graph_end()
 
     # the same step as 196 separate launches (one vb_matmul per GEMV)
     ctx.graph_begin()
@@ -301,6 +313,17 @@ def run_b200(args, rank, world, local_rank):
     ms_l = timed(lambda: ctx.graph_launch(g_launch), kl)
     per_launch_gbs = STEP_BYTES * kl / (ms_l * 1e-3) / 1e9
 
+    # decode-shaped dependency chain of the same GEMVs
+    for _ in range(3):
+        ctx.graph_launch(g_chain)
+    ms_c = timed(lambda: ctx.graph_launch(g_chain), kl)
+    chain_gbs = STEP_BYTES * kl / (ms_c * 1e-3) / 1e9
+    rc, derr = prog_chain.status()
+    if rc != 0 or derr != 0:
+        raise RuntimeError(f"chained program reported device error {derr}: {ctx.last_error()}")
+
+    sweep = sweep_rows(ctx, weights, args) if not args.no_sweep else None
+
     # e2e through the C ABI: pinned host inputs -> graph -> pinned host outputs
     hx = torch.randn(LAYERS * IN_PER_LAYER, dtype=torch.float32).pin_memory()
     hy = torch.zeros(LAYERS * OUT_PER_LAYER, dtype=torch.float32).pin_memory()
@@ -348,13 +371,15 @@ def run_b200(args, rank, world, local_rank):
                          "traffic": NCU_TRAFFIC_CONFIG1, "traffic_unit": "bytes per config-1 GEMV",
                          "achieved_config1": c1_gbs, "config1_us_per_gemv": per_gemv_ms * 1e3,
                          "config1_alg_bytes": alg_bytes(2048, 6144),
-                         "separate_launches_gbs": per_launch_gbs},
+                         "separate_launches_gbs": per_launch_gbs,
+                         "decode_chain_gbs": chain_gbs},
+            "sweep": sweep,
             "cpu_baseline": base,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": ms_e2e / args.steps, "path": "vb_memcpy_h2d + vb_graph_launch + vb_memcpy_d2h"},
             "clocks": ck,
             "gpu_launches": args.steps,
-            "gpu_launches_note": "one stream_gemv_kernel launch (+1 memset of its 112 barrier counters) per step",
+            "gpu_launches_note": "one stream_gemv_kernel launch (+1 memset of its barrier counter) per step",
         }
         if decode:
             line["decode"] = decode
@@ -364,10 +389,75 @@ def run_b200(args, rank, world, local_rank):
     ctx.graph_destroy(g_launch)
     prog.close()
     prog1.close()
+    prog_chain.close()
+    ctx.graph_destroy(g_chain)
     for *_, w in weights:
         w.release()
     ctx.close()
     return 0
+
+
+def sweep_rows(ctx, q8_weights, args):
+    """BASELINE config 2 sweep: the 7 projection shapes x M x {Q8_0, F16}.
+    M <= 2 runs as one streaming program over distinct weights (> L2);
+    larger M runs the per-launch GEMV kernel on one layer's weights (the
+    tcgen05 GEMM for M >= 16 is not built yet, so these rows show today's
+    path).  GB/s counts algorithmic bytes, TFLOP/s counts 2*M*N*K."""
+    import torch
+    import vcpm_b200 as vb
+    rows = []
+    ev0, ev1 = ctx.event(), ctx.event()
+
+    def time_fn(fn, k):
+        for _ in range(2):
+            fn()
+        ctx.record(ev0)
+        for _ in range(k):
+            fn()
+        ctx.record(ev1)
+        return ctx.elapsed_ms(ev0, ev1) / k
+
+    def program_row(wtype, ws, M):
+        X = torch.randn(len(ws) * 6144 * M, device="cuda")
+        Y = torch.zeros(len(ws) * 6144 * M, device="cuda")
+        ops, nbytes, flops = [], 0, 0
+        for i, (K, N, w) in enumerate(ws):
+            ops.append(dict(w=w, x=X.data_ptr() + 4 * i * 6144 * M, y=Y.data_ptr() + 4 * i * 6144 * M, M=M,
+                            group=0))
+            nbytes += (q8_bytes(K, N) if wtype == "q8_0" else 2 * N * K) + 4 * K * M + 4 * N * M
+            flops += 2 * M * N * K
+        p = vb.Program(ctx, ops)
+        ms = time_fn(p.run, 10)
+        rc, derr = p.status()
+        p.close()
+        return {"wtype": wtype, "M": M, "path": "stream program", "weights_mb": nbytes / 1e6,
+                "gbs": nbytes / (ms * 1e-3) / 1e9, "tflops": flops / (ms * 1e-3) / 1e12, "device_error": derr}
+
+    def launch_row(wtype, ws, M):
+        X = torch.randn(M * 6144, device="cuda")
+        Y = torch.zeros(M * 6144, device="cuda")
+        nbytes = sum((q8_bytes(K, N) if wtype == "q8_0" else 2 * N * K) + 4 * K * M + 4 * N * M for K, N, _ in ws)
+        flops = sum(2 * M * N * K for K, N, _ in ws)
+        ms = time_fn(lambda: [ctx.matmul(w, X, M, Y) for K, N, w in ws], 5)
+        return {"wtype": wtype, "M": M, "path": "per-launch GEMV (weights L2-resident)",
+                "gbs": nbytes / (ms * 1e-3) / 1e9, "tflops": flops / (ms * 1e-3) / 1e12}
+
+    q8 = [(K, N, w) for (name, K, N, w) in q8_weights]
+    for M in (1, 2):
+        rows.append(program_row("q8_0", q8, M))
+    rng = np.random.default_rng(3)
+    f16 = []
+    for l in range(8):
+        for name, K, N, _ in SHAPES:
+            hw = (0.02 * rng.standard_normal((N, K))).astype(np.float16).view(np.uint16)
+            f16.append((K, N, ctx.weight(vb.TYPE_F16, K, N, hw)))
+    rows.append(program_row("f16", f16, 1))
+    for M in (16, 128, 512):
+        rows.append(launch_row("q8_0", q8[:7], M))
+        rows.append(launch_row("f16", f16[:7], M))
+    for _, _, w in f16:
+        w.release()
+    return rows
 
 
 def run_config1(args, local_rank):
@@ -456,6 +546,7 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=64)
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--mode", default="full", choices=["full", "config1"],
                     help="config1: only the config-1 streaming program (profiling case)")
     ap.add_argument("--copies", type=int, default=56)
