@@ -495,8 +495,11 @@ def run_config1(args, local_rank):
 
 def decode_bench(ctx, host_layers, args):
     """Secondary metric: MiniCPM4 28-layer decode tokens/s (
-    256-token prefill, then single-token steps against a bf16 KV cache of 512
-    slots) through vb_lm_forward, using the same synthetic Q8_0 weights."""
+    256-token prefill, then 128 single-token steps against a bf16 KV cache of
+    384 positions) with the same synthetic Q8_0 weights.  The product path is
+    the single-launch decoder (vb_decoder_step: the whole stack as one
+    persistent kernel per token); the per-op path (vb_lm_forward, T = 1) is
+    timed beside it on a second cache."""
     import torch
     import vcpm_b200 as vb
     rng = np.random.default_rng(7)
@@ -509,32 +512,49 @@ def decode_bench(ctx, host_layers, args):
     fn = (1.0 + 0.02 * rng.standard_normal(HIDDEN)).astype(np.float32)
     cfg = vb.LMConfig(HIDDEN, NH, NKV, HD, FFN, LAYERS, 1e-5, 10000.0, 0, 0.0, vb.TYPE_Q8_0)
     lm = vb.LM(ctx, cfg, layers, fn)
-    kv = vb.KV(ctx, lm, 1, 512)
     P, D = 256, args.decode_steps
+    kv_a = vb.KV(ctx, lm, 1, P + D)
+    kv_b = vb.KV(ctx, lm, 1, P + D)
     x = (torch.randn(P + D, HIDDEN, device="cuda") * 0.5).to(torch.bfloat16).float()
-    out = torch.zeros(P + D, HIDDEN, device="cuda")
+    out_a = torch.zeros(P + D, HIDDEN, device="cuda")
+    out_b = torch.zeros(P + D, HIDDEN, device="cuda")
     torch.cuda.synchronize()
     ev0, ev1 = ctx.event(), ctx.event()
     ctx.record(ev0)
-    lm.forward(kv, [0], [0], P, x[:P], out[:P])
+    lm.forward(kv_a, [0], [0], P, x[:P], out_a[:P])
     ctx.record(ev1)
     prefill_ms = ctx.elapsed_ms(ev0, ev1)
-    # decode: a few untimed steps, then the timed ones
+    lm.forward(kv_b, [0], [0], P, x[:P], out_b[:P])
+    dec = vb.Decoder(ctx, lm, kv_a, [0])
     warm = 4
-    for i in range(warm):
-        lm.forward(kv, [0], [P + i], 1, x[P + i:P + i + 1], out[P + i:P + i + 1])
+
+    def timed(step):
+        for i in range(warm):
+            step(P + i)
+        ctx.sync()
+        ctx.record(ev0)
+        for i in range(warm, D):
+            step(P + i)
+        ctx.record(ev1)
+        return ctx.elapsed_ms(ev0, ev1) / (D - warm)
+
+    ms = timed(lambda p: dec.step([p], x[p:p + 1], out_a[p:p + 1]))
+    rc, err = dec.status()
+    ms_op = timed(lambda p: lm.forward(kv_b, [0], [p], 1, x[p:p + 1], out_b[p:p + 1]))
     ctx.sync()
-    ctx.record(ev0)
-    for i in range(warm, D):
-        lm.forward(kv, [0], [P + i], 1, x[P + i:P + i + 1], out[P + i:P + i + 1])
-    ctx.record(ev1)
-    ms = ctx.elapsed_ms(ev0, ev1)
-    n = D - warm
-    kv.close()
+    a, b = out_a[P:].double(), out_b[P:].double()
+    cos = float((a * b).sum() / (a.norm() * b.norm()))
+    rel = float((a - b).norm() / b.norm())
+    dec.close()
+    kv_a.close()
+    kv_b.close()
     lm.close()
-    return {"metric": "LM decode tokens/s (28-layer MiniCPM4, Q8_0, batch 1)", "tokens_per_s": n / (ms * 1e-3),
-            "ms_per_token": ms / n, "prefill_ms_256": prefill_ms, "kv_positions": [P, P + D],
-            "weight_bytes_per_token": 1_403_781_120}
+    wb = 1_403_781_120
+    return {"metric": "LM decode tokens/s (28-layer MiniCPM4, Q8_0, batch 1)", "tokens_per_s": 1e3 / ms,
+            "ms_per_token": ms, "path": "vb_decoder_step (one persistent launch per token)",
+            "weight_gbs": wb / (ms * 1e-3) / 1e9, "per_op_tokens_per_s": 1e3 / ms_op,
+            "prefill_ms_256": prefill_ms, "kv_positions": [P, P + D], "weight_bytes_per_token": wb,
+            "decoder_vs_per_op": {"cos": cos, "rel_l2": rel}, "device_error": err}
 
 
 def main():
@@ -543,7 +563,7 @@ def main():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--decode-steps", type=int, default=64)
+    ap.add_argument("--decode-steps", type=int, default=128)
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")

@@ -287,6 +287,26 @@ int vb_lm_forward(vb_ctx *ctx, vb_lm *lm, vb_kv *kv, int n, const int32_t *seq,
  * T tokens, RoPE positions 0..T-1 in each; no final norm. h in place. */
 int vb_lm_forward_noncausal(vb_ctx *ctx, vb_lm *lm, int n, int T, float *h);
 
+/* Single-token decode of a whole stack as ONE persistent-kernel launch: the
+ * T = 1 call of vcpm_minicpm4_forward (src/minicpm4.c:536-572) that the
+ * reference makes per generated token for the TSLM and the RALM
+ * (src/gen_step.c:763, :894).  The decoder binds n KV slots `seq` of `kv`
+ * (1 <= n <= 8; n * K bytes of every projection's quantized activation must
+ * fit 16 KiB) and owns its buffers, RoPE table (positions below the next
+ * power of two >= capacity + 1, at least 512) and launch program.  Q8_0 and
+ * F16 stacks.  Each step appends one token per slot exactly as
+ * vb_lm_forward(n, seq, pos, T = 1) does; results agree with it within the
+ * fp32 accumulation-order tolerance.  x, out: device [n][hidden].  A step is
+ * asynchronous; vb_decoder_status synchronises and reports a device-side
+ * timeout (the kernel's waits are bounded). */
+typedef struct vb_decoder_s *vb_decoder;
+int vb_decoder_create(vb_ctx *ctx, vb_lm *lm, vb_kv *kv, int n,
+                      const int32_t *seq, vb_decoder *out);
+int vb_decoder_step(vb_ctx *ctx, vb_decoder d, const int32_t *pos,
+                    const float *x, float *out);
+int vb_decoder_status(vb_ctx *ctx, vb_decoder d, int *device_error);
+void vb_decoder_destroy(vb_decoder d);
+
 /* ------------------------------------------------------------------ */
 /* LocDiT estimator and the CFM loop                                   */
 /* (src/locdit.c:140-400, src/gen_step.c:472-652, src/cfm_solver.c)   */

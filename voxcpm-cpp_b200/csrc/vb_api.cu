@@ -62,13 +62,8 @@ int arena_reserve(vb_ctx *ctx, Arena &ws, size_t bytes) {
 // theta_0 = p, theta_{i+1} = theta_i * base^(-2/head_dim) in fp32
 // (src/minicpm4.c:205-213).  Built on the host with libm so the device uses
 // exactly the host's cosf/sinf values.
-const RopeTable *rope_table(vb_ctx *ctx, int head_dim, float theta, int use_factors, int need_pos) {
-    for (auto &r : ctx->ropes)
-        if (r.head_dim == head_dim && r.theta == theta && r.use_factors == use_factors && r.max_pos >= need_pos)
-            return &r;
-    int max_pos = 512;
-    while (max_pos < need_pos) max_pos *= 2;
-    std::vector<float> cs((size_t)max_pos * head_dim);
+void rope_table_host(int head_dim, float theta, int use_factors, int max_pos, std::vector<float> &cs) {
+    cs.assign((size_t)max_pos * head_dim, 0.0f);
     const float *ff = use_factors ? longrope_short_factors() : nullptr;
     const float theta_scale = powf(theta, -2.0f / (float)head_dim);
     for (int p = 0; p < max_pos; p++) {
@@ -82,6 +77,16 @@ const RopeTable *rope_table(vb_ctx *ctx, int head_dim, float theta, int use_fact
             th *= theta_scale;
         }
     }
+}
+
+const RopeTable *rope_table(vb_ctx *ctx, int head_dim, float theta, int use_factors, int need_pos) {
+    for (auto &r : ctx->ropes)
+        if (r.head_dim == head_dim && r.theta == theta && r.use_factors == use_factors && r.max_pos >= need_pos)
+            return &r;
+    int max_pos = 512;
+    while (max_pos < need_pos) max_pos *= 2;
+    std::vector<float> cs;
+    rope_table_host(head_dim, theta, use_factors, max_pos, cs);
     RopeTable t;
     t.head_dim = head_dim;
     t.theta = theta;

@@ -87,6 +87,8 @@ int check_launch(vb_ctx *ctx, const char *what);
 int arena_reserve(vb_ctx *ctx, Arena &a, size_t bytes);
 inline int ws_reserve(vb_ctx *ctx, size_t bytes) { return arena_reserve(ctx, ctx->ws, bytes); }
 const RopeTable *rope_table(vb_ctx *ctx, int head_dim, float theta, int use_factors, int need_pos);
+// The (cos, sin) table of positions 0..max_pos-1 on the host.
+void rope_table_host(int head_dim, float theta, int use_factors, int max_pos, std::vector<float> &cs);
 const float *longrope_short_factors();
 
 // ------------------------------------------------------- device helpers

@@ -11,6 +11,7 @@
 // values are unchanged).  The KV cache is bf16 [layer][n_kv][seq*cap][hd].
 #include "vb_common.cuh"
 #include "vb_kernels.cuh"
+#include "vb_stream_op.cuh"
 
 #include <algorithm>
 #include <cmath>
@@ -477,6 +478,264 @@ extern "C" int vb_lm_forward_noncausal(vb_ctx *ctx, vb_lm *lm, int n, int T, flo
     uint16_t *kc = cv.take<uint16_t>(kv_elems);
     uint16_t *vc = cv.take<uint16_t>(kv_elems);
     return run_layers(ctx, lm, M, h, tt, kc, vc, 0, M, cv);
+}
+
+// ============================================================ decoder
+// One decode token per bound sequence through the whole stack as ONE
+// persistent-kernel launch (the T = 1 call of vcpm_minicpm4_forward,
+// src/minicpm4.c:536-572, made once per generated token for the TSLM and
+// the RALM, src/gen_step.c:763 and :894).  Five grid-synchronised groups
+// per block, each an op of the streaming kernel:
+//   QKV  = W_qkv . bf16(bf16(rms_norm(h)) * attn_norm)        (bf16 out)
+//   ATTN : RoPE(q, k), bf16 K/V append, split softmax(q K^T) V, merged
+//   h    = bf16(h + scale * bf16(W_o . att))
+//   GU   = W_gu . bf16(bf16(rms_norm(h)) * ffn_norm)           (bf16 out)
+//   h    = bf16(h + scale * bf16(W_down . swiglu(GU)))
+// then the final norm.  Each op computes its activation operand in every
+// CTA (norm statistics, SwiGLU and Q8_0 quantization fused into the
+// weight-streaming pass), so the only global exchange is the barrier.
+struct vb_decoder_s {
+    vb_lm *lm = nullptr;
+    vb_kv *kv = nullptr;
+    int n = 0, max_pos = 0;
+    std::vector<int> seq;
+    vb_program prog = nullptr;
+    void *mem = nullptr;
+    float *h = nullptr, *out = nullptr;
+};
+
+// EPI_SWIGLU needs chunks of whole gate/up pairs with bulk-copied scales,
+// and (one activation row) the fast path's two rows per warp (K <= 4096).
+static bool swiglu_epilogue_ok(vb_weight w, int n) {
+    const int64_t K = w->K, N = w->N;
+    const int row_bytes = (int)(w->type == VB_TYPE_Q8_0 ? K : 2 * K);
+    const int R = ST_SLOT / row_bytes;
+    if (N % 2 || R < 2 || R % 2) return false;
+    if (w->type == VB_TYPE_Q8_0) return K % 256 == 0 && (n > 1 || K <= 4096);
+    return w->type == VB_TYPE_F16;
+}
+
+extern "C" void vb_decoder_destroy(vb_decoder d) {
+    if (!d) return;
+    vb_program_destroy(d->prog);
+    cudaFree(d->mem);
+    delete d;
+}
+
+extern "C" int vb_decoder_create(vb_ctx *ctx, vb_lm *lm, vb_kv *kv, int n, const int32_t *seq, vb_decoder *out) {
+    if (!ctx || !lm || !kv || !seq || !out || n < 1) return VB_ERR_INVALID_ARG;
+    *out = nullptr;
+    const vb_lm_config &c = lm->cfg;
+    if (n > ST_MMAX) return set_error(ctx, VB_ERR_INVALID_ARG, "vb_decoder_create: at most %d sequences", ST_MMAX);
+    if (kv->n_layers != c.n_layers || kv->n_kv != c.n_kv_heads || kv->head_dim != c.head_dim)
+        return set_error(ctx, VB_ERR_INVALID_ARG, "vb_decoder_create: KV cache shape does not match the stack");
+    for (int i = 0; i < n; i++) {
+        if (seq[i] < 0 || seq[i] >= kv->n_seqs)
+            return set_error(ctx, VB_ERR_INVALID_ARG, "vb_decoder_create: bad sequence slot %d", seq[i]);
+        for (int j = 0; j < i; j++)
+            if (seq[j] == seq[i]) return set_error(ctx, VB_ERR_INVALID_ARG, "vb_decoder_create: duplicate sequence slot");
+    }
+    const int64_t H = c.hidden, HD = c.head_dim, NH = c.n_heads, NKV = c.n_kv_heads, F = c.ffn;
+    const int64_t QD = NH * HD, KD = NKV * HD, QKV = QD + 2 * KD;
+    if (HD % 64 || HD > 256 || NKV < 1 || NH % NKV || H % 32 || F % 32 || QD % 32)
+        return set_error(ctx, VB_ERR_INVALID_ARG, "vb_decoder_create: unsupported head layout");
+    const int max_chunks = (kv->capacity + ST_ATT_ROWS - 1) / ST_ATT_ROWS;
+    if (stream_attn_aux_bytes((int)HD, max_chunks) > (size_t)ST_AUX_BYTES)
+        return set_error(ctx, VB_ERR_INVALID_ARG,
+                         "vb_decoder_create: attention scratch for %d KV positions exceeds %d bytes", kv->capacity,
+                         ST_AUX_BYTES);
+    int max_pos = 512;
+    while (max_pos < kv->capacity + 1) max_pos *= 2;
+
+    // device buffers: sizes first (null base), then the same carve for real
+    auto carve = [&](Carve &cv, float **h, float **qkv, float **att, float **gu, float **ob, float **part,
+                     float **ml, float **cs) {
+        *h = cv.take<float>((size_t)n * H);
+        *qkv = cv.take<float>((size_t)n * QKV);
+        *att = cv.take<float>((size_t)n * QD);
+        *gu = cv.take<float>((size_t)n * 2 * F);
+        *ob = cv.take<float>((size_t)n * H);
+        *part = cv.take<float>((size_t)n * NH * max_chunks * HD);
+        *ml = cv.take<float>((size_t)n * NH * max_chunks * 2);
+        *cs = c.no_rope ? nullptr : cv.take<float>((size_t)max_pos * HD);
+    };
+    float *h, *qkv, *att, *gu, *ob, *part, *ml, *cs;
+    Carve sz(nullptr);
+    carve(sz, &h, &qkv, &att, &gu, &ob, &part, &ml, &cs);
+    vb_decoder d = new vb_decoder_s();
+    d->lm = lm;
+    d->kv = kv;
+    d->n = n;
+    d->max_pos = c.no_rope ? 0 : max_pos;
+    d->seq.assign(seq, seq + n);
+    if (cudaMalloc(&d->mem, sz.off + 256) != cudaSuccess) {
+        delete d;
+        return set_error(ctx, VB_ERR_OOM, "vb_decoder_create: %zu bytes of buffers", sz.off);
+    }
+    Carve cv(d->mem);
+    carve(cv, &h, &qkv, &att, &gu, &ob, &part, &ml, &cs);
+    d->h = h;
+    d->out = ob;
+    if (cs) {
+        std::vector<float> t;
+        rope_table_host((int)HD, c.rope_theta, HD == 128, max_pos, t);
+        if (cudaMemcpy(cs, t.data(), t.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+            vb_decoder_destroy(d);
+            return set_error(ctx, VB_ERR_BACKEND, "vb_decoder_create: rope table upload failed");
+        }
+    }
+
+    float scale = 1.0f;
+    if (c.scale_depth > 0.0f && c.n_layers > 0) scale = c.scale_depth / sqrtf((float)c.n_layers);
+    std::vector<StreamOp> ops;
+    size_t wbytes = 0;
+    int rc = VB_OK;
+    auto gemv = [&](vb_weight w, const float *x, int64_t ldx, float *y, int64_t ldy, int group) {
+        StreamOp s{};
+        s.kind = OPK_GEMV;
+        s.pro = PRO_LOAD;
+        s.epi = EPI_STORE;
+        s.res_scale = 1.0f;
+        s.qrule = ctx->qrule;
+        s.wtype = w->type;
+        s.K = (int)w->K;
+        s.N = (int)w->N;
+        s.M = n;
+        s.w = (const uint8_t *)w->data;
+        s.sc = w->scales;
+        s.x = x;
+        s.ldx = ldx;
+        s.y = y;
+        s.ldy = ldy;
+        s.flags = VB_OUT_BF16;
+        s.group = group;
+        s.wait_group = group - 1;
+        s.last_in_group = 1;
+        if (!rc && w->type != VB_TYPE_Q8_0 && w->type != VB_TYPE_F16)
+            rc = set_error(ctx, VB_ERR_INVALID_ARG, "vb_decoder_create: weights must be Q8_0 or F16");
+        if (!rc) rc = stream_gemv_geometry(ctx, s, (int)ops.size());
+        wbytes += w->device_bytes;
+        ops.push_back(s);
+        return &ops.back();
+    };
+    const float kq_scale = 1.0f / sqrtf((float)HD);
+    const size_t kv_layer = kv->layer_elems();
+    for (int l = 0; l < c.n_layers && !rc; l++) {
+        LayerDev &L = lm->layers[l];
+        const int g0 = 5 * l;
+        StreamOp *o = gemv(L.qkv, h, H, qkv, QKV, g0);
+        o->pro = PRO_RMSNORM;
+        o->pro_w = L.attn_norm;
+        o->eps = c.eps;
+
+        StreamOp a{};
+        a.kind = OPK_ATTN;
+        a.M = n;
+        a.qkv = qkv;
+        a.ldqkv = QKV;
+        a.kc = kv->k + (size_t)l * kv_layer;
+        a.vc = kv->v + (size_t)l * kv_layer;
+        a.n_rows = kv->n_seqs * kv->capacity;
+        a.n_heads = (int)NH;
+        a.n_kv = (int)NKV;
+        a.head_dim = (int)HD;
+        a.use_rope = !c.no_rope;
+        a.rope_cs = cs;
+        a.part = part;
+        a.part_ml = ml;
+        a.max_chunks = max_chunks;
+        a.cnt = reinterpret_cast<unsigned *>((size_t)l * n * NH);   // index of the layer's counters
+        a.eps = kq_scale;
+        a.y = att;
+        a.ldy = QD;
+        a.group = g0 + 1;
+        a.wait_group = g0;
+        a.last_in_group = 1;
+        a.res_scale = 1.0f;
+        ops.push_back(a);
+
+        o = gemv(L.o, att, QD, h, H, g0 + 2);
+        o->epi = EPI_RESIDUAL;
+        o->res = h;
+        o->res_scale = scale;
+
+        // SwiGLU in the gate/up epilogue when the ring chunks hold whole
+        // gate/up pairs (else in every CTA's down-projection prologue)
+        const bool pair_epi = swiglu_epilogue_ok(L.gu, n);
+        o = gemv(L.gu, h, H, gu, pair_epi ? F : 2 * F, g0 + 3);
+        o->pro = PRO_RMSNORM;
+        o->pro_w = L.ffn_norm;
+        o->eps = c.eps;
+        if (pair_epi) o->epi = EPI_SWIGLU;
+
+        o = gemv(L.down, gu, pair_epi ? F : 2 * F, h, H, g0 + 4);
+        if (!pair_epi) {
+            o->pro = PRO_SWIGLU;
+            o->pro_len = (int)F;
+        }
+        o->epi = EPI_RESIDUAL;
+        o->res = h;
+        o->res_scale = scale;
+        if (!rc && o->K != F) rc = set_error(ctx, VB_ERR_INVALID_ARG, "vb_decoder_create: down projection K != ffn");
+    }
+    int n_groups = 5 * c.n_layers;
+    if (!rc && lm->final_norm) {
+        StreamOp f{};
+        f.kind = OPK_NORM;
+        f.M = n;
+        f.K = (int)H;
+        f.x = h;
+        f.ldx = H;
+        f.y = ob;
+        f.ldy = H;
+        f.pro_w = lm->final_norm;
+        f.eps = c.eps;
+        f.group = n_groups;
+        f.wait_group = n_groups - 1;
+        f.last_in_group = 1;
+        f.res_scale = 1.0f;
+        ops.push_back(f);
+        n_groups++;
+    }
+    const int n_counters = c.n_layers * n * (int)NH;
+    if (!rc) rc = stream_program_build(ctx, ops, n_groups, n_counters, wbytes, &d->prog);
+    if (rc) {
+        vb_decoder_destroy(d);
+        return rc;
+    }
+    *out = d;
+    return VB_OK;
+}
+
+extern "C" int vb_decoder_step(vb_ctx *ctx, vb_decoder d, const int32_t *pos, const float *x, float *out) {
+    if (!ctx || !d || !pos || !x || !out) return VB_ERR_INVALID_ARG;
+    vb_kv *kv = d->kv;
+    const vb_lm_config &c = d->lm->cfg;
+    StreamStep st{};
+    for (int i = 0; i < d->n; i++) {
+        const int s = d->seq[i], used = kv->n_used[s];
+        if (used + 1 > kv->capacity)
+            return set_error(ctx, VB_ERR_INVALID_ARG, "vb_decoder_step: KV cache full (%d + 1 > %d)", used, kv->capacity);
+        if (!c.no_rope && (pos[i] < 0 || pos[i] >= d->max_pos))
+            return set_error(ctx, VB_ERR_INVALID_ARG, "vb_decoder_step: position %d outside 0..%d", pos[i],
+                             d->max_pos - 1);
+        st.v[i][0] = c.no_rope ? 0 : pos[i];
+        st.v[i][1] = s * kv->capacity + used;
+        st.v[i][2] = s * kv->capacity;
+        st.v[i][3] = used + 1;
+    }
+    const size_t hb = (size_t)d->n * c.hidden * 4;
+    VB_CHECK(ctx, cudaMemcpyAsync(d->h, x, hb, cudaMemcpyDeviceToDevice, ctx->stream));
+    int rc = stream_program_launch(ctx, d->prog, st);
+    if (rc) return rc;
+    VB_CHECK(ctx, cudaMemcpyAsync(out, d->lm->final_norm ? d->out : d->h, hb, cudaMemcpyDeviceToDevice, ctx->stream));
+    for (int i = 0; i < d->n; i++) kv->n_used[d->seq[i]] += 1;
+    return VB_OK;
+}
+
+extern "C" int vb_decoder_status(vb_ctx *ctx, vb_decoder d, int *device_error) {
+    if (!ctx || !d || !device_error) return VB_ERR_INVALID_ARG;
+    return vb_program_status(ctx, d->prog, device_error);
 }
 
 // ================================================================== LocDiT

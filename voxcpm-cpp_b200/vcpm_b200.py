@@ -113,6 +113,10 @@ SIGNATURES = {
     "vb_kv_used": (_I, [_P, _I]),
     "vb_lm_forward": (_I, [_P, _P, _P, _I, _P, _P, _I, _P, _P]),
     "vb_lm_forward_noncausal": (_I, [_P, _P, _I, _I, _P]),
+    "vb_decoder_create": (_I, [_P, _P, _P, _I, _P, C.POINTER(_P)]),
+    "vb_decoder_step": (_I, [_P, _P, _P, _P, _P]),
+    "vb_decoder_status": (_I, [_P, _P, C.POINTER(C.c_int)]),
+    "vb_decoder_destroy": (None, [_P]),
     "vb_dit_create": (_I, [_P, _P, _P, C.POINTER(_P)]),
     "vb_dit_destroy": (None, [_P, _P]),
     "vb_dit_weight_bytes": (_SZ, [_P]),
@@ -380,6 +384,31 @@ class KV:
     def close(self):
         if self.h:
             self.ctx.L.vb_kv_destroy(self.ctx.h, self.h)
+            self.h = C.c_void_p()
+
+
+class Decoder:
+    """Single-launch decode step (vb_decoder) over KV slots `seq`."""
+
+    def __init__(self, ctx: Context, lm: LM, kv: KV, seq):
+        self.ctx, self.lm, self.kv = ctx, lm, kv
+        self.n = len(seq)
+        s = (C.c_int32 * self.n)(*seq)
+        self.h = C.c_void_p()
+        ctx.check(ctx.L.vb_decoder_create(ctx.h, lm.h, kv.h, self.n, s, C.byref(self.h)))
+
+    def step(self, pos, x, out):
+        p = (C.c_int32 * self.n)(*pos)
+        self.ctx.check(self.ctx.L.vb_decoder_step(self.ctx.h, self.h, p, _addr(x), _addr(out)))
+
+    def status(self):
+        e = C.c_int(0)
+        rc = self.ctx.L.vb_decoder_status(self.ctx.h, self.h, C.byref(e))
+        return rc, e.value
+
+    def close(self):
+        if self.h:
+            self.ctx.L.vb_decoder_destroy(self.h)
             self.h = C.c_void_p()
 
 
