@@ -67,6 +67,10 @@ const char *vb_last_error(const vb_ctx *ctx);
 /* Waits for all work on the context stream (the synchronous return of
  * vcpm_backend_compute_graph, src/ggml_backend.h:58-59). */
 int vb_sync(vb_ctx *ctx);
+/* Synchronise and report a device-side error code recorded by the
+ * tensor-core mat-mul (0 = none; its waits are bounded, a timeout records a
+ * code instead of hanging).  Returns VB_ERR_BACKEND when one was recorded. */
+int vb_device_status(vb_ctx *ctx, int *device_error);
 /* Use an external cudaStream_t (passed as void*); NULL restores the
  * context's own stream. */
 int vb_set_stream(vb_ctx *ctx, void *cuda_stream);

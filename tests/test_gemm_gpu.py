@@ -1,0 +1,118 @@
+"""Tensor-core mat-mul (tcgen05, M >= 16 activation rows) against the CPU
+oracle: Q8_0 (exact block values split into fp16 hi/lo operands) and F16
+weights, tile edges (N not a multiple of 128, M not a multiple of 16), one
+and many k tiles, split-K, bias / bf16 epilogue, both activation rounding
+rules, and agreement with the weight-streaming GEMV path on the same call."""
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+import synth as S
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+import vcpm_b200 as vb  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    c = vb.Context(0)
+    yield c
+    c.close()
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def run_matmul(ctx, wtype, K, N, M, flags=0, with_bias=False):
+    W = S.weight(wtype, N, K)
+    x = S.normal((M, K))
+    w = ctx.weight(wtype, K, N, W)
+    xd = dev(x)
+    y = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+    b = S.normal(N, 0.5) if with_bias else None
+    bd = dev(b) if with_bias else None
+    torch.cuda.synchronize()
+    ctx.matmul(w, xd, M, y, flags, bias=bd)
+    ctx.sync()
+    rc, err = ctx.device_status()
+    assert (rc, err) == (0, 0)
+    out = host(y)
+    w.release()
+    ref = O.matmul(wtype, W, K, N, x)
+    return out, ref, b
+
+
+@pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_F16])
+@pytest.mark.parametrize("K,N,M", [
+    (2048, 2048, 16), (2048, 256, 128), (2048, 6144, 256), (6144, 2048, 64), (1024, 2048, 512),
+    (64, 1024, 33), (1024, 64, 200), (2048, 200, 17), (4096, 384, 600), (1024, 4096, 22),
+])
+def test_gemm_vs_oracle(ctx, wtype, K, N, M):
+    out, ref, _ = run_matmul(ctx, wtype, K, N, M)
+    S.assert_matmul_close(out, ref, 1e-3)
+    # the split hi/lo operands reproduce the block products almost exactly
+    assert S.rel_l2(out, ref) < 2e-5
+
+
+@pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_F16])
+def test_gemm_bias_bf16_epilogue(ctx, wtype):
+    out, ref, b = run_matmul(ctx, wtype, 2048, 1024, 48, vb.OUT_BF16, with_bias=True)
+    S.assert_layer_close(out, O.bf16_round(ref + b), 1e-3)
+
+
+def test_gemm_qrule_ref(ctx):
+    K, N, M = 1024, 512, 32
+    W = S.weight(O.TYPE_Q8_0, N, K)
+    x = S.normal((M, K))
+    w = ctx.weight(O.TYPE_Q8_0, K, N, W)
+    xd = dev(x)
+    y = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+    ctx.set_qrule(vb.QRULE_REF)
+    try:
+        ctx.matmul(w, xd, M, y)
+        ctx.sync()
+    finally:
+        ctx.set_qrule(vb.QRULE_X86)
+    S.assert_matmul_close(host(y), O.matmul(O.TYPE_Q8_0, W, K, N, x, qrule=O.QRULE_REF), 1e-3)
+    w.release()
+
+
+def test_gemm_agrees_with_gemv_path(ctx):
+    """Same call through a context with the tensor-core path switched off
+    (VB_GEMM=0 at creation): both follow the same block arithmetic."""
+    K, N, M = 2048, 768, 40
+    W = S.weight(O.TYPE_Q8_0, N, K)
+    x = S.normal((M, K))
+    old = os.environ.get("VB_GEMM")
+    os.environ["VB_GEMM"] = "0"
+    try:
+        c2 = vb.Context(0)
+    finally:
+        if old is None:
+            del os.environ["VB_GEMM"]
+        else:
+            os.environ["VB_GEMM"] = old
+    outs = []
+    for c in (ctx, c2):
+        w = c.weight(O.TYPE_Q8_0, K, N, W)
+        xd = dev(x)
+        y = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        c.matmul(w, xd, M, y)
+        c.sync()
+        outs.append(host(y))
+        w.release()
+    c2.close()
+    S.assert_matmul_close(outs[0], outs[1], 1e-4)

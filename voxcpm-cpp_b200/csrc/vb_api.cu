@@ -166,6 +166,10 @@ extern "C" int vb_create(int device, vb_ctx **out) {
     c->device = device;
     c->sm_count = prop.multiProcessorCount;
     c->smem_optin = prop.sharedMemPerBlockOptin;
+    {
+        const char *g = getenv("VB_GEMM");
+        c->use_gemm = !(g && g[0] == '0');
+    }
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
         delete c;
         return VB_ERR_BACKEND;
@@ -188,12 +192,21 @@ extern "C" void vb_destroy(vb_ctx *ctx) {
     for (auto &r : ctx->ropes) cudaFree(r.d_cs);
     if (ctx->ws.ptr) cudaFree(ctx->ws.ptr);
     if (ctx->attn_ws.ptr) cudaFree(ctx->attn_ws.ptr);
+    gemm_free(ctx);
     if (ctx->own_stream_handle) cudaStreamDestroy(ctx->own_stream_handle);
     delete ctx;
 }
 
 extern "C" const char *vb_last_error(const vb_ctx *ctx) {
     return ctx ? ctx->last_error.c_str() : "null context";
+}
+
+extern "C" int vb_device_status(vb_ctx *ctx, int *device_error) {
+    if (!ctx || !device_error) return VB_ERR_INVALID_ARG;
+    int rc = gemm_device_error(ctx, device_error);
+    if (rc) return rc;
+    if (*device_error) return set_error(ctx, VB_ERR_BACKEND, "tensor-core kernel reported error %d", *device_error);
+    return VB_OK;
 }
 
 extern "C" int vb_sync(vb_ctx *ctx) {

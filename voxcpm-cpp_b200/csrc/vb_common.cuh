@@ -60,6 +60,8 @@ struct vb_weight_s {
     void *data = nullptr;
     uint16_t *scales = nullptr;
     size_t device_bytes = 0;
+    alignas(64) unsigned char tmap[128];   // tensor-core path: TMA descriptor of the weight tiles
+    bool tmap_ok = false;
 };
 
 // Host F32->BF16->F32 (round to nearest even, quiet NaN).
@@ -77,6 +79,8 @@ struct vb_ctx {
     std::vector<vb::RopeTable> ropes;   // cached rotary tables
     int sm_count = 0;
     size_t smem_optin = 0;
+    bool use_gemm = true;               // tensor-core path for M >= 16 (VB_GEMM=0 disables)
+    void *gemm = nullptr;               // tensor-core path state (vb_gemm.cu)
 };
 
 namespace vb {

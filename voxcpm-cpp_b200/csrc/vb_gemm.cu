@@ -1,0 +1,601 @@
+// vb_gemm.cu -- tensor-core mat-mul (tcgen05 + TMEM + TMA) for M >= 16
+// activation rows: prefill, CFG-batched LocDiT evaluations, multi-request
+// decode batches.  The M < 16 decode shapes stay on the weight-streaming
+// GEMV kernels.
+//
+// ggml semantics (src/minicpm4.c:270-458, src/locdit.c:150-391 call sites):
+//   Q8_0 weight: y[m][n] = sum_b d_w[n,b] * d_x[m,b] * sum_{j<32} qw[n,b,j] * qx[m,b,j]
+//                where (qx, d_x) is the Q8_0 quantization of x (ctx rule);
+//   F16 weight:  y[m][n] = sum_k w[n][k] * fp16(x[m][k]), fp32 accumulation.
+//
+// F16 runs as kind::f16 MMAs on the weights and fp16(x) directly: every
+// product is exact in fp32, as in the reference.
+//
+// Q8_0: the per-block scale pairs rule out accumulating integer products
+// across blocks, so both operands are dequantised per block to their exact
+// fp32 values v = d * q (an int8 times an fp16 needs 18 significant bits)
+// and each v is split into two fp16 terms v = hi + lo (hi = fp16(v),
+// lo = fp16(v - hi), exact up to fp16 subnormal spacing).  Three kind::f16
+// MMAs per k-step, hi*hi + hi*lo + lo*hi, give every product to about 2^-22
+// relative, accumulated in fp32 in TMEM: the result matches ggml's block
+// dot up to the fp32 accumulation order.  The activation side is prepared
+// once per call (gemm_act_kernel); weight tiles are converted in shared
+// memory as they stream in, so HBM carries Q8_0 bytes only.
+//
+// Tile: 128 weight rows (MMA M = TMEM lanes) x BN activation rows (MMA N =
+// TMEM columns, 16..256) x 64 k per stage (one 128-byte swizzle row of
+// fp16).  Warp 0 issues TMA loads, warp 1 allocates TMEM and issues MMAs
+// (one thread), warps 2..9 convert weight tiles and run the epilogue.  When
+// the tile grid is small the K range is split over CTAs; partial sums go to
+// a workspace and the last CTA of a tile (device-wide count) adds them in
+// split order, so results are deterministic.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "vb_common.cuh"
+#include "vb_device.cuh"
+#include "vb_kernels.cuh"
+#include "vb_stream.cuh"
+
+namespace vb {
+
+constexpr int GM_BM = 128;
+constexpr int GM_BK = 64;
+constexpr int GM_THREADS = 320;
+constexpr int GM_CONV_THREADS = 256;
+constexpr int GM_MAX_STAGES = 4;
+constexpr int GM_SMEM_BUDGET = 220 * 1024;
+
+struct GemmArgs {
+    int q8;                 // 1: Q8_0 weights (hi/lo split), 0: F16 weights
+    int K, N, M, BN;
+    int kt_total, kt_per_split, splits, tiles_m;
+    int n_tma, n_conv;      // pipeline depths
+    uint32_t tmem_cols;
+    const uint16_t *sc;     // Q8_0 scales [N][K/32]
+    float *y;
+    const float *bias;
+    unsigned flags;
+    int64_t ldy, seg, seg_stride, seg_off;
+    float *ws;              // split partials [splits][N][Mp]
+    int Mp;                 // tiles_m * BN
+    unsigned *cnt;          // per-tile arrival counters (self-resetting)
+    int *err;
+};
+
+__device__ __forceinline__ uint64_t sw128_desc(const void *p) {
+    uint64_t d = (uint64_t)((smem_u32(p) >> 4) & 0x3FFFu);
+    d |= (uint64_t)1 << 16;                 // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;       // stride byte offset: 8 rows x 128 B
+    d |= (uint64_t)1 << 46;                 // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;                 // 128-byte swizzle
+    return d;
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Bounded mbarrier wait (no abort flag: every role of the CTA reaches the
+// teardown on its own once its waits have ended).
+__device__ __forceinline__ bool gm_wait(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
+    return true;
+}
+
+__device__ __forceinline__ int64_t gm_out_row(const GemmArgs &a, int m) {
+    return (int64_t)(m / a.seg) * a.seg_stride + a.seg_off + (m % a.seg);
+}
+
+__device__ __forceinline__ float gm_epilogue(const GemmArgs &a, int n, float v) {
+    if (a.bias) v = __fadd_rn(v, a.bias[n]);
+    return (a.flags & VB_OUT_BF16) ? bf16r(v) : v;
+}
+
+__global__ void __launch_bounds__(GM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_bh,
+                const __grid_constant__ CUtensorMap tm_bl, const GemmArgs a) {
+    extern __shared__ uint8_t gsm_raw[];
+    uint8_t *gsm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~(uintptr_t)1023);
+    __shared__ uint64_t bars[4 * GM_MAX_STAGES + 1];
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_last;
+    uint64_t *full = bars, *empty = bars + GM_MAX_STAGES, *cfull = bars + 2 * GM_MAX_STAGES,
+             *cempty = bars + 3 * GM_MAX_STAGES, *tfull = bars + 4 * GM_MAX_STAGES;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int BN = a.BN;
+    const uint32_t a_bytes = a.q8 ? GM_BM * GM_BK : GM_BM * GM_BK * 2;   // raw int8 or fp16 tile
+    const uint32_t b_bytes = (uint32_t)BN * 128;
+    const uint32_t stage_bytes = a_bytes + b_bytes * (a.q8 ? 2 : 1);
+    uint8_t *conv = gsm + (size_t)a.n_tma * stage_bytes;                 // converted A: [n_conv][hi 16K | lo 16K]
+
+    int bid = blockIdx.x;
+    const int split = bid % a.splits;
+    bid /= a.splits;
+    const int tm = bid % a.tiles_m, tn = bid / a.tiles_m;
+    const int n0 = tn * GM_BM, m0 = tm * BN;
+    const int kt0 = split * a.kt_per_split;
+    const int nkt = min(a.kt_per_split, a.kt_total - kt0);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < GM_MAX_STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+            mbar_init(&cfull[s], GM_CONV_THREADS / 32);
+            mbar_init(&cempty[s], 1);
+        }
+        mbar_init(tfull, 1);
+        mbar_fence_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(a.tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------- TMA
+        if (lane == 0) {
+            int issued[GM_MAX_STAGES] = {0, 0, 0, 0};
+            for (int i = 0; i < nkt; i++) {
+                const int s = i % a.n_tma;
+                const uint32_t ph = (uint32_t)(i / a.n_tma) & 1u;
+                if (!gm_wait(&empty[s], ph ^ 1u)) { atomicCAS(a.err, 0, 11); break; }
+                uint8_t *st = gsm + (size_t)s * stage_bytes;
+                mbar_arrive_expect_tx(&full[s], stage_bytes);
+                const int kx = (kt0 + i) * GM_BK;
+                tma_load_2d(st, &tm_w, kx, n0, &full[s]);
+                tma_load_2d(st + a_bytes, &tm_bh, kx, m0, &full[s]);
+                if (a.q8) tma_load_2d(st + a_bytes + b_bytes, &tm_bl, kx, m0, &full[s]);
+                issued[s]++;
+            }
+            // every issued copy has landed before the CTA can finish
+            for (int s = 0; s < a.n_tma; s++)
+                if (issued[s]) gm_wait(&full[s], (uint32_t)(issued[s] - 1) & 1u);
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------- MMA
+        if (lane == 0) {
+            const uint32_t idesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(GM_BM >> 4) << 24);
+            bool ok = true;
+            for (int i = 0; i < nkt && ok; i++) {
+                const int s = i % a.n_tma;
+                const uint32_t ph = (uint32_t)(i / a.n_tma) & 1u;
+                const int c = i % a.n_conv;
+                const uint32_t cph = (uint32_t)(i / a.n_conv) & 1u;
+                if (!gm_wait(&full[s], ph) || (a.q8 && !gm_wait(&cfull[c], cph))) {
+                    atomicCAS(a.err, 0, 12);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                uint8_t *st = gsm + (size_t)s * stage_bytes;
+                const uint8_t *ahi = a.q8 ? conv + (size_t)c * 32768 : st;
+                const uint8_t *alo = ahi + 16384;
+                const uint8_t *bhi = st + a_bytes, *blo = bhi + b_bytes;
+#pragma unroll
+                for (int k = 0; k < GM_BK / 16; k++) {
+                    const uint32_t acc = (i | k) != 0;
+                    umma_f16(tmem, sw128_desc(ahi + 32 * k), sw128_desc(bhi + 32 * k), idesc, acc);
+                    if (a.q8) {
+                        umma_f16(tmem, sw128_desc(ahi + 32 * k), sw128_desc(blo + 32 * k), idesc, 1u);
+                        umma_f16(tmem, sw128_desc(alo + 32 * k), sw128_desc(bhi + 32 * k), idesc, 1u);
+                    }
+                }
+                umma_commit(&empty[s]);
+                if (a.q8) umma_commit(&cempty[c]);
+            }
+            umma_commit(tfull);   // fires once every MMA above has completed
+        }
+    } else {
+        // ------------------------------------------- convert, then epilogue
+        const int t = threadIdx.x - 64;
+        if (a.q8) {
+            // thread t: weight row t/2, Q8_0 block t%2 of each 64-wide k tile
+            const int r = t >> 1, half = t & 1;
+            const bool rv = n0 + r < a.N;
+            const int kb_total = a.K / 32;
+            const uint16_t *scr = a.sc + (int64_t)(rv ? n0 + r : 0) * kb_total;
+            float dnext = rv ? h2f(__ldg(scr + kt0 * 2 + half)) : 0.0f;
+            for (int i = 0; i < nkt; i++) {
+                const int s = i % a.n_tma;
+                const uint32_t ph = (uint32_t)(i / a.n_tma) & 1u;
+                const int c = i % a.n_conv;
+                const uint32_t cph = (uint32_t)(i / a.n_conv) & 1u;
+                const float d = dnext;
+                if (rv && i + 1 < nkt) dnext = h2f(__ldg(scr + (kt0 + i + 1) * 2 + half));
+                const bool okf = gm_wait(&full[s], ph), okc = gm_wait(&cempty[c], cph ^ 1u);
+                if (!okf || !okc) { atomicCAS(a.err, 0, 13); break; }
+                const int8_t *src = reinterpret_cast<const int8_t *>(gsm + (size_t)s * stage_bytes) + r * GM_BK + half * 32;
+                uint8_t *hi = conv + (size_t)c * 32768 + r * 128;
+                uint8_t *lo = hi + 16384;
+#pragma unroll
+                for (int q = 0; q < 4; q++) {   // 8 values = one 16-byte chunk of the fp16 row
+                    const int2 raw = *reinterpret_cast<const int2 *>(src + q * 8);
+                    const int8_t *b8 = reinterpret_cast<const int8_t *>(&raw);
+                    uint32_t h[4], l[4];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const float v0 = __fmul_rn(d, (float)b8[2 * e]), v1 = __fmul_rn(d, (float)b8[2 * e + 1]);
+                        const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+                        const __half l0 = __float2half_rn(__fsub_rn(v0, __half2float(h0)));
+                        const __half l1 = __float2half_rn(__fsub_rn(v1, __half2float(h1)));
+                        h[e] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+                        l[e] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+                    }
+                    const int chunk = (half * 4 + q) ^ (r & 7);   // 128-byte swizzle
+                    *reinterpret_cast<uint4 *>(hi + chunk * 16) = make_uint4(h[0], h[1], h[2], h[3]);
+                    *reinterpret_cast<uint4 *>(lo + chunk * 16) = make_uint4(l[0], l[1], l[2], l[3]);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor core
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&cfull[c]);
+            }
+        }
+        // epilogue: TMEM lane quarter (warp % 4) = 32 weight rows; the two
+        // warps of a quarter take alternate 16-column groups
+        const bool okt = gm_wait(tfull, 0);
+        tc_fence_after();
+        const int q = warp & 3, colgrp = (warp - 2) >> 2;
+        const int r = q * 32 + lane, n = n0 + r;
+        const bool split_k = a.splits > 1;
+        if (okt) {
+            for (int j = colgrp; j * 16 < BN; j += 2) {
+                uint32_t v[16];
+                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(j * 16), v);
+                if (n < a.N) {
+                    if (split_k) {
+                        // partials [split][N][Mp], this thread's 16 columns contiguous
+                        float4 *pw = reinterpret_cast<float4 *>(a.ws + ((int64_t)split * a.N + n) * a.Mp + m0 + j * 16);
+#pragma unroll
+                        for (int q4 = 0; q4 < 4; q4++)
+                            pw[q4] = make_float4(__uint_as_float(v[4 * q4]), __uint_as_float(v[4 * q4 + 1]),
+                                                 __uint_as_float(v[4 * q4 + 2]), __uint_as_float(v[4 * q4 + 3]));
+                    } else {
+#pragma unroll
+                        for (int cc = 0; cc < 16; cc++) {
+                            const int m = m0 + j * 16 + cc;
+                            if (m >= a.M) break;
+                            a.y[gm_out_row(a, m) * a.ldy + n] = gm_epilogue(a, n, __uint_as_float(v[cc]));
+                        }
+                    }
+                }
+            }
+        } else {
+            atomicCAS(a.err, 0, 14);
+        }
+        if (split_k) {
+            // last CTA of this tile adds the split partials in split order
+            asm volatile("bar.sync 2, %0;" ::"r"(GM_CONV_THREADS) : "memory");
+            if (t == 0) {
+                fence_acq_rel_gpu();
+                const unsigned tile = (unsigned)(tn * a.tiles_m + tm);
+                s_last = atomicAdd(a.cnt + tile, 1u) == (unsigned)(a.splits - 1);
+                if (s_last) {
+                    fence_acq_rel_gpu();
+                    a.cnt[tile] = 0;   // ready for the next launch
+                }
+            }
+            asm volatile("bar.sync 2, %0;" ::"r"(GM_CONV_THREADS) : "memory");
+            if (s_last && n < a.N) {
+                // 16 columns x 4 splits (16 vector loads) in flight at a
+                // time; the sums still run in split order
+#pragma unroll 1
+                for (int j = colgrp; j * 16 < BN; j += 2) {
+                    float4 acc[4];
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; q4++) acc[q4] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+                    for (int s0 = 0; s0 < a.splits; s0 += 4) {
+                        float4 v[4][4];
+#pragma unroll
+                        for (int u = 0; u < 4; u++) {
+                            const float4 *pr =
+                                reinterpret_cast<const float4 *>(a.ws + ((int64_t)(s0 + u) * a.N + n) * a.Mp + m0 + j * 16);
+#pragma unroll
+                            for (int q4 = 0; q4 < 4; q4++)
+                                v[u][q4] = s0 + u < a.splits ? __ldcg(pr + q4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+#pragma unroll
+                        for (int u = 0; u < 4; u++)
+                            if (s0 + u < a.splits)
+#pragma unroll
+                                for (int q4 = 0; q4 < 4; q4++) {
+                                    acc[q4].x = __fadd_rn(acc[q4].x, v[u][q4].x);
+                                    acc[q4].y = __fadd_rn(acc[q4].y, v[u][q4].y);
+                                    acc[q4].z = __fadd_rn(acc[q4].z, v[u][q4].z);
+                                    acc[q4].w = __fadd_rn(acc[q4].w, v[u][q4].w);
+                                }
+                    }
+                    const float *af = reinterpret_cast<const float *>(acc);
+#pragma unroll
+                    for (int cc = 0; cc < 16; cc++) {
+                        const int m = m0 + j * 16 + cc;
+                        if (m < a.M) a.y[gm_out_row(a, m) * a.ldy + n] = gm_epilogue(a, n, af[cc]);
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols) : "memory");
+    }
+}
+
+// Activation operand(s): Q8_0 -> (hi, lo) fp16 of the dequantised block
+// values (quantisation bit-exact with the GEMV path's, rule `rule`); F16 ->
+// fp16(x).  One warp per 32-value block; row m reads x row (m % x_mod).
+__global__ void gemm_act_kernel(const float *x, int64_t ldx, int64_t x_mod, int M, int K, int q8, int rule,
+                                __half *bh, __half *bl) {
+    const int64_t blk = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31, nb = K >> 5;
+    if (blk >= (int64_t)M * nb) return;
+    const int m = (int)(blk / nb), b = (int)(blk % nb);
+    const float v = x[(int64_t)(m % x_mod) * ldx + b * 32 + lane];
+    const int64_t o = (int64_t)m * K + b * 32 + lane;
+    if (!q8) {
+        bh[o] = __float2half_rn(v);
+        return;
+    }
+    int q;
+    uint16_t dh;
+    q8_quant_warp(v, rule, q, dh);
+    const float dv = __fmul_rn(h2f(dh), (float)q);
+    const __half h = __float2half_rn(dv);
+    bh[o] = h;
+    bl[o] = __float2half_rn(__fsub_rn(dv, __half2float(h)));
+}
+
+// ------------------------------------------------------------------ host
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 2-D tensor map over a row-major [rows][cols] array of `esize`-byte
+// elements, box [box_rows][box_cols].
+static bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, int esize, int64_t cols, int64_t rows,
+                     int box_cols, int box_rows, bool swizzle) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(cols * esize)};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct ActMaps {                // TMA descriptors of one activation buffer shape
+    const void *bh = nullptr, *bl = nullptr;
+    int K = 0, M = 0, BN = 0;
+    CUtensorMap th, tl;
+};
+
+struct GemmState {
+    Arena act;                  // activation operands
+    Arena part;                 // split partials
+    unsigned *cnt = nullptr;    // tile counters
+    int *err = nullptr;
+    bool init = false;
+    ActMaps cache[8];           // most recent activation descriptors
+    int next = 0;
+};
+
+static GemmState *gemm_state(vb_ctx *ctx) {
+    GemmState *g = static_cast<GemmState *>(ctx->gemm);
+    if (g) return g;
+    g = new GemmState();
+    if (cudaMalloc(&g->cnt, 65536 * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(g->cnt, 0, 65536 * sizeof(unsigned)) != cudaSuccess ||
+        cudaMalloc(&g->err, sizeof(int)) != cudaSuccess || cudaMemset(g->err, 0, sizeof(int)) != cudaSuccess) {
+        cudaFree(g->cnt);
+        cudaFree(g->err);
+        delete g;
+        return nullptr;
+    }
+    g->init = true;
+    ctx->gemm = g;
+    return g;
+}
+
+void gemm_free(vb_ctx *ctx) {
+    GemmState *g = static_cast<GemmState *>(ctx->gemm);
+    if (!g) return;
+    cudaFree(g->act.ptr);
+    cudaFree(g->part.ptr);
+    cudaFree(g->cnt);
+    cudaFree(g->err);
+    delete g;
+    ctx->gemm = nullptr;
+}
+
+int init_gemm(vb_ctx *ctx) {
+    VB_CHECK(ctx, cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GM_SMEM_BUDGET + 1024));
+    return VB_OK;
+}
+
+bool gemm_supported(vb_weight w, int64_t M) {
+    if (M < 16 || !encode_fn()) return false;
+    if (w->type == VB_TYPE_Q8_0) return w->K % GM_BK == 0;
+    if (w->type == VB_TYPE_F16) return w->K % GM_BK == 0;
+    return false;
+}
+
+int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx, int64_t x_mod,
+                const MatmulOut &out) {
+    GemmState *gs = gemm_state(ctx);
+    if (!gs) return set_error(ctx, VB_ERR_OOM, "gemm: state allocation failed");
+    const bool q8 = w->type == VB_TYPE_Q8_0;
+    const int K = (int)w->K, N = (int)w->N;
+    // Activation tile width: the widest (fewest weight re-reads) that still
+    // gives about one tile per SM; below that, split K to fill the SMs.
+    const int tiles_n = (N + GM_BM - 1) / GM_BM;
+    const int mr = (int)((M + 15) / 16 * 16);
+    int BN = std::min(256, mr);
+    for (int cand : {256, 128, 64}) {
+        if (cand > mr) continue;
+        BN = cand;
+        if ((int64_t)tiles_n * ((M + cand - 1) / cand) * 5 >= (int64_t)ctx->sm_count * 4) break;
+    }
+    const int tiles_m = (int)((M + BN - 1) / BN);
+    const int kt_total = K / GM_BK;
+    int splits = 1;
+    const int tiles = tiles_m * tiles_n;
+    if (tiles * 5 < ctx->sm_count * 4) {
+        splits = std::max(1, ctx->sm_count / tiles);
+        splits = std::min(splits, std::max(1, kt_total / 2));   // at least 2 k-tiles per split
+    }
+    const int kt_per_split = (kt_total + splits - 1) / splits;
+    splits = (kt_total + kt_per_split - 1) / kt_per_split;
+    if (tiles > 65536) return set_error(ctx, VB_ERR_INVALID_ARG, "gemm: too many tiles");
+
+    const uint32_t a_bytes = q8 ? GM_BM * GM_BK : GM_BM * GM_BK * 2;
+    const uint32_t b_bytes = (uint32_t)BN * 128;
+    const uint32_t stage = a_bytes + b_bytes * (q8 ? 2 : 1);
+    const int n_conv = q8 ? 2 : 1;
+    const size_t conv_bytes = q8 ? (size_t)n_conv * 32768 : 0;
+    int n_tma = (int)std::min<size_t>(GM_MAX_STAGES, (GM_SMEM_BUDGET - conv_bytes) / stage);
+    if (n_tma < 2) return set_error(ctx, VB_ERR_INVALID_ARG, "gemm: tile does not fit shared memory");
+    const size_t smem = (size_t)n_tma * stage + conv_bytes + 1024;
+    uint32_t cols = 32;
+    while (cols < (uint32_t)BN) cols <<= 1;
+
+    // activation operands
+    const size_t ab = (size_t)M * K * 2;
+    int rc = arena_reserve(ctx, gs->act, 2 * ab + 512);
+    if (rc) return rc;
+    __half *bh = (__half *)gs->act.ptr;
+    __half *bl = (__half *)((uint8_t *)gs->act.ptr + ((ab + 255) & ~(size_t)255));
+    {
+        const int64_t blocks = M * (K / 32);
+        const int wpb = 8;
+        gemm_act_kernel<<<(unsigned)((blocks + wpb - 1) / wpb), wpb * 32, 0, ctx->stream>>>(
+            x, ldx ? ldx : K, x_mod > 0 ? x_mod : M, (int)M, K, q8 ? 1 : 0, ctx->qrule, bh, bl);
+        VB_LAUNCH_CHECK(ctx, "gemm_act");
+    }
+    // descriptors: the weight's once per weight, the activations' per shape
+    if (!w->tmap_ok) {
+        CUtensorMap *tw = reinterpret_cast<CUtensorMap *>(w->tmap);
+        w->tmap_ok = q8 ? make_map(tw, w->data, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, GM_BK, GM_BM, false)
+                        : make_map(tw, w->data, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, N, GM_BK, GM_BM, true);
+        if (!w->tmap_ok) return set_error(ctx, VB_ERR_BACKEND, "gemm: weight tensor map encoding failed");
+    }
+    const void *blp = q8 ? (const void *)bl : (const void *)bh;
+    ActMaps *am = nullptr;
+    for (ActMaps &c : gs->cache)
+        if (c.bh == bh && c.bl == blp && c.K == K && c.M == (int)M && c.BN == BN) am = &c;
+    if (!am) {
+        am = &gs->cache[gs->next];
+        gs->next = (gs->next + 1) % 8;
+        am->bh = nullptr;
+        if (!make_map(&am->th, bh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, M, GM_BK, BN, true) ||
+            !make_map(&am->tl, blp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, M, GM_BK, BN, true))
+            return set_error(ctx, VB_ERR_BACKEND, "gemm: activation tensor map encoding failed");
+        am->bh = bh;
+        am->bl = blp;
+        am->K = K;
+        am->M = (int)M;
+        am->BN = BN;
+    }
+
+    GemmArgs g{};
+    g.q8 = q8;
+    g.K = K;
+    g.N = N;
+    g.M = (int)M;
+    g.BN = BN;
+    g.kt_total = kt_total;
+    g.kt_per_split = kt_per_split;
+    g.splits = splits;
+    g.tiles_m = tiles_m;
+    g.n_tma = n_tma;
+    g.n_conv = n_conv;
+    g.tmem_cols = cols;
+    g.sc = w->scales;
+    g.y = out.y;
+    g.bias = out.bias;
+    g.flags = out.flags;
+    g.ldy = out.ldy ? out.ldy : N;
+    g.seg = out.seg ? out.seg : M;
+    g.seg_stride = out.seg ? out.seg_stride : 0;
+    g.seg_off = out.seg ? out.seg_off : 0;
+    g.cnt = gs->cnt;
+    g.err = gs->err;
+    if (splits > 1) {
+        g.Mp = tiles_m * BN;
+        rc = arena_reserve(ctx, gs->part, (size_t)splits * N * g.Mp * 4);
+        if (rc) return rc;
+        g.ws = (float *)gs->part.ptr;
+    }
+    gemm_kernel<<<(unsigned)(tiles * splits), GM_THREADS, smem, ctx->stream>>>(
+        *reinterpret_cast<const CUtensorMap *>(w->tmap), am->th, am->tl, g);
+    VB_LAUNCH_CHECK(ctx, "gemm");
+    return VB_OK;
+}
+
+int gemm_device_error(vb_ctx *ctx, int *code) {
+    GemmState *gs = static_cast<GemmState *>(ctx->gemm);
+    *code = 0;
+    if (!gs) return VB_OK;
+    VB_CHECK(ctx, cudaStreamSynchronize(ctx->stream));
+    VB_CHECK(ctx, cudaMemcpy(code, gs->err, sizeof(int), cudaMemcpyDeviceToHost));
+    return VB_OK;
+}
+
+}  // namespace vb

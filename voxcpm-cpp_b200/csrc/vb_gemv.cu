@@ -266,6 +266,7 @@ int launch_matmul(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t l
     MatmulOut out = out_in;
     if (out.ldy == 0) out.ldy = w->N;
     if (out.seg == 0) { out.seg = M; out.seg_stride = 0; out.seg_off = 0; }
+    if (ctx->use_gemm && gemm_supported(w, M)) return launch_gemm(ctx, w, x, M, ldx, x_mod, out);
     GemvArgs a;
     a.w = w->data;
     a.sc = w->scales;

@@ -27,6 +27,13 @@ struct MatmulOut {
 int launch_matmul(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx, int64_t x_mod,
                   const MatmulOut &out);
 
+// Tensor-core path for M >= 16 (vb_gemm.cu); launch_matmul dispatches to it.
+bool gemm_supported(vb_weight w, int64_t M);
+int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx, int64_t x_mod,
+                const MatmulOut &out);
+int gemm_device_error(vb_ctx *ctx, int *code);
+void gemm_free(vb_ctx *ctx);
+
 int launch_quantize_q8_0(vb_ctx *ctx, const float *x, int64_t K, int64_t M, void *blocks, int rule);
 int launch_dequantize_q8_0(vb_ctx *ctx, const void *blocks, int64_t n, float *y);
 

@@ -9,12 +9,14 @@ int init_gemv(vb_ctx *ctx);
 int init_attention(vb_ctx *ctx);
 int init_model_kernels(vb_ctx *ctx);
 int init_stream(vb_ctx *ctx);
+int init_gemm(vb_ctx *ctx);
 
 int init_kernels(vb_ctx *ctx) {
     if (init_gemv(ctx)) return VB_ERR_BACKEND;
     if (init_stream(ctx)) return VB_ERR_BACKEND;
     if (init_attention(ctx)) return VB_ERR_BACKEND;
     if (init_model_kernels(ctx)) return VB_ERR_BACKEND;
+    if (init_gemm(ctx)) return VB_ERR_BACKEND;
     return VB_OK;
 }
 }  // namespace vb

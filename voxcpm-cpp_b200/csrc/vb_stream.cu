@@ -226,10 +226,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         const int grp = op.group;
         cp_async_wait_all();    // op i+1's descriptor has landed
         if (consumer_sync_or(bad, ST_CONSUMERS)) break;
-        if (arrive && ctid == 0) {
-            __threadfence();
-            red_release_gpu(bars + grp, 1u);
-        }
+        if (arrive && ctid == 0) red_release_gpu(bars + grp, 1u);
     }
 }
 

@@ -78,6 +78,15 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const unsigned *p) {
     return v;
 }
 
+// Acquire-release fence at GPU scope.  After a CTA barrier it also
+// releases what other threads of the CTA wrote before the barrier (the
+// fence is cumulative), so one thread can publish a whole CTA's results.
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
+// Release-add: the CTA's earlier writes (ordered by a preceding CTA barrier)
+// are visible to any thread that acquires the new value.
 __device__ __forceinline__ void red_release_gpu(unsigned *p, unsigned v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }

@@ -413,15 +413,24 @@ __device__ __forceinline__ void q8_prologue_batch(const StreamOp &op, int r0, bo
             if (lane == 0) red[r * ST_CONSUMER_WARPS + cw] = sq;
         }
         consumer_sync(ST_CONSUMERS);
-        if (ctid < M) {
-            double t = 0.0;
-            for (int r = 0; r < R; r++)
-                for (int w = 0; w < ST_CONSUMER_WARPS; w++) {
-                    const int it0 = (r0 + r) * ST_CONSUMERS + w * 32;
-                    if (it0 < total && it0 / ipr == ctid) t += red[r * ST_CONSUMER_WARPS + w];
-                }
-            const float mean = __double2float_rn(__ddiv_rn(t, (double)K));
-            aux[ctid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, op.eps)));
+        if (cw == 0) {
+            // warp 0: lane j holds warp-round j's partial (R * 8 <= 32);
+            // each row's total is a fixed-order tree sum, then lane m
+            // finishes row m.  Division by K is a multiplication when K is
+            // a power of two (exact).
+            const int it0 = (r0 + lane / ST_CONSUMER_WARPS) * ST_CONSUMERS + (lane % ST_CONSUMER_WARPS) * 32;
+            const bool have = lane < R * ST_CONSUMER_WARPS && it0 < total;
+            const double part = have ? red[lane] : 0.0;
+            const int row = have ? it0 / ipr : -1;
+            double mine = 0.0;
+            for (int mm = 0; mm < M; mm++) {
+                const double t = warp_sum_d(row == mm ? part : 0.0);
+                if (lane == mm) mine = t;
+            }
+            if (lane < M) {
+                const double md = (K & (K - 1)) == 0 ? __dmul_rn(mine, 1.0 / (double)K) : __ddiv_rn(mine, (double)K);
+                aux[lane] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__double2float_rn(md), op.eps)));
+            }
         }
         consumer_sync(ST_CONSUMERS);
     }
@@ -626,17 +635,20 @@ __device__ __noinline__ void stream_attn(const StreamOp &op, const int *st, uint
                     *reinterpret_cast<float2 *>(op.part + pi * HD + 2 * ctid) = o;
                 }
                 if (ctid == 0) *reinterpret_cast<float2 *>(op.part_ml + pi * 2) = make_float2(mx, l);
-                // Count the item once its partials are visible device-wide;
-                // the last of the (sequence, head) merges all its chunks.
-                __threadfence();
+                // Count the item once the CTA's partials are released
+                // (barrier, then a cumulative fence); the last item of the
+                // (sequence, head) acquires everyone's and merges the chunks.
                 consumer_sync(ST_CONSUMERS);
-                if (ctid == 0) s_last = atomicAdd(op.cnt + m * NH + h, 1u) == (unsigned)(nch - 1);
+                if (ctid == 0) {
+                    fence_acq_rel_gpu();
+                    s_last = atomicAdd(op.cnt + m * NH + h, 1u) == (unsigned)(nch - 1);
+                    if (s_last) fence_acq_rel_gpu();
+                }
                 consumer_sync(ST_CONSUMERS);
                 if (s_last) {
                     // Merge: every thread loads its chunks' partial outputs
                     // (4 dims, chunks sl, sl + S, ...) together with the
                     // chunk statistics, then rescales once the maximum is known.
-                    __threadfence();
                     const int D4 = HD >> 2, S = ST_CONSUMERS / D4, d4 = ctid % D4, sl = ctid / D4;
                     const float *po = op.part + ((int64_t)m * NH + h) * op.max_chunks * HD + 4 * d4;
                     const float *pml = op.part_ml + ((int64_t)m * NH + h) * op.max_chunks * 2;

@@ -65,6 +65,7 @@ SIGNATURES = {
     "vb_destroy": (None, [_P]),
     "vb_last_error": (C.c_char_p, [_P]),
     "vb_sync": (_I, [_P]),
+    "vb_device_status": (_I, [_P, C.POINTER(C.c_int)]),
     "vb_set_stream": (_I, [_P, _P]),
     "vb_get_stream": (_P, [_P]),
     "vb_set_qrule": (_I, [_P, _I]),
@@ -246,6 +247,12 @@ class Context:
         self.check(self.L.vb_weight_register(self.h, wtype, K, N, host_array.ctypes.data, host_array.nbytes,
                                              C.byref(w)))
         return Weight(self, w, wtype, K, N)
+
+    def device_status(self):
+        """(rc, code): synchronises; code != 0 is a device-side error record."""
+        e = C.c_int(0)
+        rc = self.L.vb_device_status(self.h, C.byref(e))
+        return rc, e.value
 
     # ---------------------------------------------------------------- ops
     def matmul(self, w, x, M, y, flags=0, bias=None):
