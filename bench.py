@@ -356,6 +356,10 @@ def run_b200(args, rank, world, local_rank):
     if not args.no_decode and world == 1:
         decode = decode_bench(ctx, host_layers, args)
 
+    e2e_tts = None
+    if not args.no_e2e:
+        e2e_tts = e2e_bench(ctx, host_layers, args, rank, world)
+
     base = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
 
     if rank == 0:
@@ -383,6 +387,8 @@ def run_b200(args, rank, world, local_rank):
         }
         if decode:
             line["decode"] = decode
+        if e2e_tts:
+            line["e2e_tts"] = e2e_tts
         print(json.dumps(line), flush=True)
     ctx.graph_destroy(g)
     ctx.graph_destroy(g1)
@@ -557,6 +563,107 @@ def decode_bench(ctx, host_layers, args):
             "decoder_vs_per_op": {"cos": cos, "rel_l2": rel}, "device_error": err}
 
 
+# DiT / LocEnc block shapes (hidden 1024, FFN 4096;
+# q 1024->2048 for 16 heads of 128, 2 KV heads) and the generation loop's
+# projections (config 4: FSQ 256, RALM 8 layers of the TSLM width).
+DIT_H, DIT_FFN, DIT_LAYERS, FEAT, PATCH, FSQ_DIM, RALM_LAYERS, ENC_LAYERS = 1024, 4096, 8, 64, 4, 256, 8, 8
+SAMPLES_PER_PATCH, SAMPLE_RATE = 7680, 48000
+
+
+def e2e_bench(ctx, host_layers, args, rank, world):
+    """end-to-end synthetic TTS.  args.e2e_utts utterances
+    (200 random-token prompts, args.e2e_patches patches of 7680 samples at
+    48 kHz each) sharded over the ranks; each rank runs its shard in lockstep
+    through vb_gen (prompt, then per patch: mu -> 10-step CFM with CFG-Zero*
+    -> LocEnc -> TSLM -> FSQ -> RALM -> stop head).  RTF = max-over-ranks
+    wall time / total audio seconds.  Excluded: text embedding lookup
+    (prompt embeddings are drawn directly) and the AudioVAE decoder."""
+    import torch
+    import vcpm_b200 as vb
+    rng = np.random.default_rng(11 + rank)
+    B = max(1, args.e2e_utts // world)
+    T, NP = 200, args.e2e_patches
+
+    def q8(N, K):
+        return synth_q8_0(rng, N, K)
+
+    def norm(n):
+        return (1.0 + 0.02 * rng.standard_normal(n)).astype(np.float32)
+
+    def small(n, std=0.02):
+        return (std * rng.standard_normal(n)).astype(np.float32)
+
+    def dit_layer():
+        return {"q": q8(NH * HD, DIT_H), "k": q8(NKV * HD, DIT_H), "v": q8(NKV * HD, DIT_H), "o": q8(DIT_H, NH * HD),
+                "gate": q8(DIT_FFN, DIT_H), "up": q8(DIT_FFN, DIT_H), "down": q8(DIT_H, DIT_FFN),
+                "attn_norm": norm(DIT_H), "ffn_norm": norm(DIT_H)}
+
+    tl = []
+    for hl in host_layers:
+        L = dict(hl)
+        L["attn_norm"], L["ffn_norm"] = norm(HIDDEN), norm(HIDDEN)
+        tl.append(L)
+    cfg = lambda n, no_rope, h, f: vb.LMConfig(h, NH, NKV, HD, f, n, 1e-5, 10000.0, no_rope, 0.0,  # noqa: E731
+                                               vb.TYPE_Q8_0)
+    tslm = vb.LM(ctx, cfg(LAYERS, 0, HIDDEN, FFN), tl, norm(HIDDEN))
+    ralm = vb.LM(ctx, cfg(RALM_LAYERS, 1, HIDDEN, FFN), tl[:RALM_LAYERS], norm(HIDDEN))
+    enc = vb.LM(ctx, cfg(ENC_LAYERS, 0, DIT_H, DIT_FFN), [dit_layer() for _ in range(ENC_LAYERS)], None)
+    dt = {"in_proj": q8(DIT_H, FEAT), "cond_proj": q8(DIT_H, FEAT), "out_proj": q8(FEAT, DIT_H),
+          "in_bias": small(DIT_H), "cond_bias": small(DIT_H), "out_bias": small(FEAT),
+          "t_w1": q8(DIT_H, DIT_H), "t_w2": q8(DIT_H, DIT_H), "dt_w1": q8(DIT_H, DIT_H), "dt_w2": q8(DIT_H, DIT_H),
+          "t_b1": small(DIT_H), "t_b2": small(DIT_H), "dt_b1": small(DIT_H), "dt_b2": small(DIT_H),
+          "norm": norm(DIT_H)}
+    dit = vb.DiT(ctx, vb.DiTConfig(DIT_H, DIT_LAYERS, NH, NKV, DIT_FFN, HD, FEAT, PATCH, 1e-5, vb.TYPE_Q8_0), dt,
+                 [dit_layer() for _ in range(DIT_LAYERS)])
+    shapes = {"enc_in": (FEAT, DIT_H), "enc_to_lm": (DIT_H, HIDDEN), "lm_to_dit": (HIDDEN, DIT_H),
+              "res_to_dit": (HIDDEN, DIT_H), "fsq_in": (HIDDEN, FSQ_DIM), "fsq_out": (FSQ_DIM, HIDDEN),
+              "fusion": (2 * HIDDEN, HIDDEN), "stop_proj": (HIDDEN, HIDDEN), "stop_head": (HIDDEN, 2)}
+    ws = {k: ctx.weight(vb.TYPE_Q8_0, K, N, q8(N, K)) for k, (K, N) in shapes.items()}
+    bs = {k + "_bias": torch.from_numpy(small(N)).cuda() for k, (K, N) in shapes.items()}
+    parts = dict(tslm=tslm, ralm=ralm, enc=enc, dit=dit, **ws, **bs,
+                 enc_special=torch.from_numpy(small(DIT_H, 0.5)).cuda(), enc_norm=torch.from_numpy(norm(DIT_H)).cuda(),
+                 feat_dim=FEAT, patch=PATCH, fsq_scale=9.0, eps=1e-5, cfm_steps=10, cfg_value=2.0)
+    gen = vb.Gen(ctx, parts, B, T + NP + 8)
+    emb = (torch.randn(B, T, HIDDEN, device="cuda") * 0.5).to(torch.bfloat16).float()
+    patches = torch.zeros(NP, B, PATCH, FEAT, device="cuda")
+    stops = torch.zeros(NP, B, 2, device="cuda")
+    ev = [ctx.event() for _ in range(3)]
+    ctx.sync()
+    if world > 1:
+        torch.distributed.barrier()
+    t0 = time.time()
+    ctx.record(ev[0])
+    gen.prefill(T, emb)
+    ctx.record(ev[1])
+    for s in range(NP):
+        gen.step(1000 + rank * B, patches[s], stops[s])
+    ctx.record(ev[2])
+    ctx.sync()
+    wall = time.time() - t0
+    pre_ms, steps_ms = ctx.elapsed_ms(ev[0], ev[1]), ctx.elapsed_ms(ev[1], ev[2])
+    rc, derr = ctx.device_status()
+    finite = bool(torch.isfinite(patches).all().item())
+    tt = torch.tensor([pre_ms + steps_ms, pre_ms, steps_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+    total_ms = float(tt[0])
+    audio_s = B * world * NP * SAMPLES_PER_PATCH / SAMPLE_RATE
+    gen.close()
+    for w in ws.values():
+        w.release()
+    for o in (tslm, ralm, enc):
+        o.close()
+    dit.close()
+    return {"metric": "end-to-end TTS RTF (synthetic, Q8_0)", "rtf": total_ms * 1e-3 / audio_s,
+            "unit": "s/s", "higher_is_better": False, "utterances": B * world, "utterances_per_gpu": B,
+            "patches": NP, "prompt_tokens": T, "audio_s": audio_s, "wall_ms_max_over_ranks": total_ms,
+            "prefill_ms": float(tt[1]), "steps_ms": float(tt[2]), "per_patch_ms": float(tt[2]) / NP,
+            "host_wall_s_rank0": wall, "device_error": derr, "patches_finite": finite,
+            "pipeline": "vb_gen: prompt (TSLM 28L, RALM 8L) then per patch mu -> CFM (9 LocDiT evals, CFG batch) "
+                        "-> LocEnc 8L -> TSLM step -> FSQ -> RALM step -> stop head",
+            "excluded": "text embedding lookup; AudioVAE decode (runs on the host CPU in the reference, not built)"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -567,6 +674,9 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-utts", type=int, default=64)
+    ap.add_argument("--e2e-patches", type=int, default=100)
     ap.add_argument("--mode", default="full", choices=["full", "config1"],
                     help="config1: only the config-1 streaming program (profiling case)")
     ap.add_argument("--copies", type=int, default=56)

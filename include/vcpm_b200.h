@@ -355,6 +355,44 @@ int vb_dit_forward(vb_ctx *ctx, vb_dit *dit, int n, const float *x,
 int vb_cfm_solve(vb_ctx *ctx, vb_dit *dit, int n, const float *mu,
                  const float *cond, float *x, int n_steps, float cfg_value);
 
+/* ------------------------------------------------------------------ */
+/* Autoregressive generation on the device for a batch of utterances  */
+/* (src/gen_run.c:60-241, src/gen_prompt.c:186-272,                    */
+/*  src/gen_step.c:294-927, src/gen_stop.c:385-530)                     */
+/* ------------------------------------------------------------------ */
+/* The parts are created beforehand and stay owned by the caller: TSLM and
+ * RALM stacks with their final norms, the LocEnc blocks (no final norm;
+ * enc_norm is applied to the CLS row), the LocDiT estimator and the
+ * projections (weights [K -> N], biases device fp32 or NULL):
+ *   enc_in      feat -> enc hidden        enc_to_lm   enc hidden -> hidden
+ *   lm_to_dit   hidden -> dit hidden      res_to_dit  hidden -> dit hidden
+ *   fsq_in      hidden -> fsq dim         fsq_out     fsq dim -> hidden
+ *   fusion      2*hidden -> hidden        stop_proj / stop_head (optional)
+ * enc_special: device [enc hidden] CLS token; enc_norm: device [enc hidden]. */
+typedef struct {
+    vb_lm *tslm, *ralm, *enc;
+    vb_dit *dit;
+    vb_weight enc_in, enc_to_lm, lm_to_dit, res_to_dit, fsq_in, fsq_out, fusion, stop_proj, stop_head;
+    const float *enc_in_bias, *enc_special, *enc_norm, *enc_to_lm_bias, *lm_to_dit_bias, *res_to_dit_bias,
+        *fsq_in_bias, *fsq_out_bias, *fusion_bias, *stop_proj_bias, *stop_head_bias;
+    int feat_dim, patch;
+    float fsq_scale, eps;
+    int cfm_steps;
+    float cfg_value;
+} vb_gen_parts;
+
+typedef struct vb_gen_s *vb_gen;
+/* `batch` utterances, each with its own KV slots of `max_len` positions. */
+int vb_gen_create(vb_ctx *ctx, const vb_gen_parts *parts, int batch, int max_len, vb_gen *out);
+/* Prompt of T positions per utterance; embeds: device [batch][T][hidden]. */
+int vb_gen_prefill(vb_ctx *ctx, vb_gen g, int T, const float *embeds);
+/* One AR step for every utterance: mu -> CFM patch (noise stream seed + i,
+ * this step) -> LocEnc -> TSLM -> FSQ -> RALM -> stop head.
+ * patches: device [batch][patch][feat] or NULL; stop_logits: device
+ * [batch][stop_head N] or NULL. */
+int vb_gen_step(vb_ctx *ctx, vb_gen g, uint64_t seed, float *patches, float *stop_logits);
+void vb_gen_destroy(vb_ctx *ctx, vb_gen g);
+
 /* Host helpers restated from the reference for its callers. */
 float vb_cfm_sway_t_bf16(int step, int n_steps);   /* src/cfm_solver.c:27-37 */
 int vb_cfm_zero_star_steps(int n_steps);           /* src/gen_step.c:50-54 */

@@ -57,6 +57,16 @@ class DiTHost(C.Structure):
         "t_w1", "t_w2", "dt_w1", "dt_w2", "t_b1", "t_b2", "dt_b1", "dt_b2", "norm", "layers")]
 
 
+class GenParts(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in (
+        "tslm", "ralm", "enc", "dit",
+        "enc_in", "enc_to_lm", "lm_to_dit", "res_to_dit", "fsq_in", "fsq_out", "fusion", "stop_proj", "stop_head",
+        "enc_in_bias", "enc_special", "enc_norm", "enc_to_lm_bias", "lm_to_dit_bias", "res_to_dit_bias",
+        "fsq_in_bias", "fsq_out_bias", "fusion_bias", "stop_proj_bias", "stop_head_bias")] + [
+        ("feat_dim", C.c_int), ("patch", C.c_int), ("fsq_scale", C.c_float), ("eps", C.c_float),
+        ("cfm_steps", C.c_int), ("cfg_value", C.c_float)]
+
+
 # exported name -> (restype, argtypes)
 _P, _I, _I64, _F, _SZ, _U = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t, C.c_uint
 SIGNATURES = {
@@ -123,6 +133,10 @@ SIGNATURES = {
     "vb_dit_weight_bytes": (_SZ, [_P]),
     "vb_dit_forward": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _P, _P]),
     "vb_cfm_solve": (_I, [_P, _P, _I, _P, _P, _P, _I, _F]),
+    "vb_gen_create": (_I, [_P, _P, _I, _I, C.POINTER(_P)]),
+    "vb_gen_prefill": (_I, [_P, _P, _I, _P]),
+    "vb_gen_step": (_I, [_P, _P, C.c_uint64, _P, _P]),
+    "vb_gen_destroy": (None, [_P, _P]),
     "vb_cfm_sway_t_bf16": (_F, [_I, _I]),
     "vb_cfm_zero_star_steps": (_I, [_I]),
     "vb_cfm_noise": (None, [C.c_uint64, _I, _P, _I]),
@@ -416,6 +430,39 @@ class Decoder:
     def close(self):
         if self.h:
             self.ctx.L.vb_decoder_destroy(self.h)
+            self.h = C.c_void_p()
+
+
+class Gen:
+    """Batch TTS generation loop on the device (vb_gen).  parts: dict of
+    GenParts field -> object (LM/DiT/Weight, device tensor) or number."""
+
+    def __init__(self, ctx: Context, parts: dict, batch, max_len):
+        self.ctx = ctx
+        self._keep = parts
+        gp = GenParts()
+        for name, ftype in GenParts._fields_:
+            v = parts.get(name)
+            if v is None:
+                continue
+            if ftype is not C.c_void_p:
+                setattr(gp, name, v)
+            elif hasattr(v, "h"):
+                setattr(gp, name, v.h.value if isinstance(v.h, C.c_void_p) else v.h)
+            else:
+                setattr(gp, name, _addr(v))
+        self.h = C.c_void_p()
+        ctx.check(ctx.L.vb_gen_create(ctx.h, C.byref(gp), batch, max_len, C.byref(self.h)))
+
+    def prefill(self, T, embeds):
+        self.ctx.check(self.ctx.L.vb_gen_prefill(self.ctx.h, self.h, T, _addr(embeds)))
+
+    def step(self, seed, patches=None, stop_logits=None):
+        self.ctx.check(self.ctx.L.vb_gen_step(self.ctx.h, self.h, seed, _addr(patches), _addr(stop_logits)))
+
+    def close(self):
+        if self.h:
+            self.ctx.L.vb_gen_destroy(self.ctx.h, self.h)
             self.h = C.c_void_p()
 
 
