@@ -44,7 +44,7 @@ constexpr int GM_BM = 128;
 constexpr int GM_BK = 64;
 constexpr int GM_THREADS = 320;
 constexpr int GM_CONV_THREADS = 256;
-constexpr int GM_MAX_STAGES = 4;
+constexpr int GM_MAX_STAGES = 6;
 constexpr int GM_SMEM_BUDGET = 220 * 1024;
 
 struct GemmArgs {
@@ -58,6 +58,7 @@ struct GemmArgs {
     const float *bias;
     unsigned flags;
     int64_t ldy, seg, seg_stride, seg_off;
+    int seg_plain;          // output row = activation row
     float *ws;              // split partials [splits][N][Mp]
     int Mp;                 // tiles_m * BN
     unsigned *cnt;          // per-tile arrival counters (self-resetting)
@@ -117,7 +118,9 @@ __device__ __forceinline__ bool gm_wait(uint64_t *bar, uint32_t parity) {
 }
 
 __device__ __forceinline__ int64_t gm_out_row(const GemmArgs &a, int m) {
-    return (int64_t)(m / a.seg) * a.seg_stride + a.seg_off + (m % a.seg);
+    if (a.seg_plain) return m;
+    const int sg = (int)a.seg;
+    return (int64_t)(m / sg) * a.seg_stride + a.seg_off + (m % sg);
 }
 
 __device__ __forceinline__ float gm_epilogue(const GemmArgs &a, int n, float v) {
@@ -175,7 +178,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     if (warp == 0) {
         // ---------------------------------------------------------- TMA
         if (lane == 0) {
-            int issued[GM_MAX_STAGES] = {0, 0, 0, 0};
+            int issued[GM_MAX_STAGES] = {0, 0, 0, 0, 0, 0};
             for (int i = 0; i < nkt; i++) {
                 const int s = i % a.n_tma;
                 const uint32_t ph = (uint32_t)(i / a.n_tma) & 1u;
@@ -230,41 +233,75 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         // ------------------------------------------- convert, then epilogue
         const int t = threadIdx.x - 64;
         if (a.q8) {
-            // thread t: weight row t/2, Q8_0 block t%2 of each 64-wide k tile
-            const int r = t >> 1, half = t & 1;
-            const bool rv = n0 + r < a.N;
+            // thread t converts the 16-byte pieces t and t + 256 of the raw
+            // tile (row i/4, values 16*(i%4) .. +16: half of Q8_0 block
+            // (i%4)/2), so a warp reads 512 consecutive bytes (no bank
+            // conflicts) and writes whole swizzled 16-byte chunks.
             const int kb_total = a.K / 32;
-            const uint16_t *scr = a.sc + (int64_t)(rv ? n0 + r : 0) * kb_total;
-            float dnext = rv ? h2f(__ldg(scr + kt0 * 2 + half)) : 0.0f;
+            int rr[2], qq[2];
+            const uint16_t *scp[2];
+            bool rv[2];
+            float dn[2];
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int i = t + 256 * u;
+                rr[u] = i >> 2;
+                qq[u] = i & 3;
+                rv[u] = n0 + rr[u] < a.N;
+                scp[u] = a.sc + (int64_t)(rv[u] ? n0 + rr[u] : 0) * kb_total + (qq[u] >> 1);
+                dn[u] = rv[u] ? h2f(__ldg(scp[u] + kt0 * 2)) : 0.0f;
+            }
             for (int i = 0; i < nkt; i++) {
                 const int s = i % a.n_tma;
                 const uint32_t ph = (uint32_t)(i / a.n_tma) & 1u;
                 const int c = i % a.n_conv;
                 const uint32_t cph = (uint32_t)(i / a.n_conv) & 1u;
-                const float d = dnext;
-                if (rv && i + 1 < nkt) dnext = h2f(__ldg(scr + (kt0 + i + 1) * 2 + half));
+                float d[2];
+#pragma unroll
+                for (int u = 0; u < 2; u++) {
+                    d[u] = dn[u];
+                    if (rv[u] && i + 1 < nkt) dn[u] = h2f(__ldg(scp[u] + (kt0 + i + 1) * 2));
+                }
                 const bool okf = gm_wait(&full[s], ph), okc = gm_wait(&cempty[c], cph ^ 1u);
                 if (!okf || !okc) { atomicCAS(a.err, 0, 13); break; }
-                const int8_t *src = reinterpret_cast<const int8_t *>(gsm + (size_t)s * stage_bytes) + r * GM_BK + half * 32;
-                uint8_t *hi = conv + (size_t)c * 32768 + r * 128;
-                uint8_t *lo = hi + 16384;
+                const int4 *src = reinterpret_cast<const int4 *>(gsm + (size_t)s * stage_bytes);
+                int4 raw[2];
 #pragma unroll
-                for (int q = 0; q < 4; q++) {   // 8 values = one 16-byte chunk of the fp16 row
-                    const int2 raw = *reinterpret_cast<const int2 *>(src + q * 8);
-                    const int8_t *b8 = reinterpret_cast<const int8_t *>(&raw);
-                    uint32_t h[4], l[4];
+                for (int u = 0; u < 2; u++) raw[u] = src[t + 256 * u];
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const float v0 = __fmul_rn(d, (float)b8[2 * e]), v1 = __fmul_rn(d, (float)b8[2 * e + 1]);
-                        const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
-                        const __half l0 = __float2half_rn(__fsub_rn(v0, __half2float(h0)));
-                        const __half l1 = __float2half_rn(__fsub_rn(v1, __half2float(h1)));
-                        h[e] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-                        l[e] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+                for (int u = 0; u < 2; u++) {
+                    uint8_t *hi = conv + (size_t)c * 32768 + rr[u] * 128;
+                    uint8_t *lo = hi + 16384;
+                    const __half2 d2 = __half2half2(__float2half_rn(d[u]));   // the fp16 scale itself
+                    const uint32_t w4[4] = {(uint32_t)raw[u].x, (uint32_t)raw[u].y, (uint32_t)raw[u].z,
+                                            (uint32_t)raw[u].w};
+#pragma unroll
+                    for (int hc = 0; hc < 2; hc++) {   // two 8-value chunks
+                        uint32_t h[4], l[4];
+#pragma unroll
+                        for (int e = 0; e < 2; e++) {
+                            // 4 int8 -> two exact half2: bytes q+128 under exponent 0x64
+                            // give 1152 + q, minus 1152 exactly
+                            const uint32_t x = w4[2 * hc + e] ^ 0x80808080u;
+                            const uint32_t p01 = __byte_perm(x, 0x64646464u, 0x5140);
+                            const uint32_t p23 = __byte_perm(x, 0x64646464u, 0x7362);
+                            const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6480));   // 1152
+                            const __half2 q01 = __hsub2(*reinterpret_cast<const __half2 *>(&p01), bias);
+                            const __half2 q23 = __hsub2(*reinterpret_cast<const __half2 *>(&p23), bias);
+                            // hi = fp16(d*q) (one rounding of the exact product);
+                            // lo = fp16(d*q - hi) (fused: exact remainder, one rounding)
+                            const __half2 h01 = __hmul2(d2, q01), h23 = __hmul2(d2, q23);
+                            const __half2 l01 = __hfma2(d2, q01, __hneg2(h01));
+                            const __half2 l23 = __hfma2(d2, q23, __hneg2(h23));
+                            h[2 * e] = *reinterpret_cast<const uint32_t *>(&h01);
+                            h[2 * e + 1] = *reinterpret_cast<const uint32_t *>(&h23);
+                            l[2 * e] = *reinterpret_cast<const uint32_t *>(&l01);
+                            l[2 * e + 1] = *reinterpret_cast<const uint32_t *>(&l23);
+                        }
+                        const int chunk = (2 * qq[u] + hc) ^ (rr[u] & 7);   // 128-byte swizzle
+                        *reinterpret_cast<uint4 *>(hi + chunk * 16) = make_uint4(h[0], h[1], h[2], h[3]);
+                        *reinterpret_cast<uint4 *>(lo + chunk * 16) = make_uint4(l[0], l[1], l[2], l[3]);
                     }
-                    const int chunk = (half * 4 + q) ^ (r & 7);   // 128-byte swizzle
-                    *reinterpret_cast<uint4 *>(hi + chunk * 16) = make_uint4(h[0], h[1], h[2], h[3]);
-                    *reinterpret_cast<uint4 *>(lo + chunk * 16) = make_uint4(l[0], l[1], l[2], l[3]);
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor core
                 __syncwarp();
@@ -490,6 +527,7 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
     int BN = std::min(256, mr);
     for (int cand : {256, 128, 64}) {
         if (cand > mr) continue;
+        if (q8 && cand > 128 && mr > 128) continue;   // hi/lo operands: keep 4 ring stages
         BN = cand;
         if ((int64_t)tiles_n * ((M + cand - 1) / cand) * 5 >= (int64_t)ctx->sm_count * 4) break;
     }
@@ -575,6 +613,7 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
     g.seg = out.seg ? out.seg : M;
     g.seg_stride = out.seg ? out.seg_stride : 0;
     g.seg_off = out.seg ? out.seg_off : 0;
+    g.seg_plain = g.seg >= M && g.seg_off == 0;
     g.cnt = gs->cnt;
     g.err = gs->err;
     if (splits > 1) {
