@@ -31,7 +31,8 @@
 namespace vb {
 
 __global__ void __launch_bounds__(ST_THREADS, 1)
-    stream_gemv_kernel(const StreamOp *__restrict__ ops, int n_ops, unsigned *bars, int *err, const StreamStep step) {
+    stream_gemv_kernel(const StreamOp *__restrict__ ops, const int2 *__restrict__ rows, int n_ops, unsigned *bars, int *err,
+                       const StreamStep step) {
     extern __shared__ __align__(128) uint8_t sm[];
     uint8_t *wslot = sm;
     uint8_t *sslot = wslot + (size_t)ST_STAGES * ST_SLOT;
@@ -43,6 +44,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     __shared__ volatile int s_abort;
     __shared__ int s_step[ST_MMAX * 4];
     __shared__ StreamOp s_ops[2];
+    __shared__ int2 s_rows[ST_MAX_OPS];   // this CTA's rows [x, y) of every op
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, cta = blockIdx.x;
@@ -58,6 +60,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
 #pragma unroll
     for (int i = 0; i < ST_MMAX * 4; i++)
         if (threadIdx.x == i) s_step[i] = step.v[i / 4][i % 4];
+    for (int i = threadIdx.x; i < n_ops; i += ST_THREADS) s_rows[i] = rows[(int64_t)blockIdx.x * n_ops + i];
     __syncthreads();
 
     // ------------------------------------------------------------ producer
@@ -71,8 +74,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             if (op.kind == OPK_ATTN) attn_prefetch(op, s_step, cta, G);
             if (op.kind != OPK_GEMV) continue;       // no weights to stream
             if (op.pro == PRO_RMSNORM && (op.K % 4) == 0) prefetch_l2(op.pro_w, (uint32_t)op.K * 4u);
-            int64_t r0, r1;
-            op_rows(op, cta, G, r0, r1);
+            const int64_t r0 = s_rows[i].x, r1 = s_rows[i].y;
             const int R = op.rows_per_chunk;
             const int nb = op.K / QK;
             const bool swz = op.epi == EPI_SWIGLU;
@@ -154,8 +156,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             stream_norm(op, reinterpret_cast<float *>(aux), cta, G, ctid, cw, lane);
         } else {
             const int K = op.K, M = op.M, nb = K / QK;
-            int64_t r0, r1;
-            op_rows(op, cta, G, r0, r1);
+            const int64_t r0 = s_rows[i].x, r1 = s_rows[i].y;
             // The previous op ended with a consumer barrier, so no warp still
             // reads the activation buffers when they are rewritten here.
             if (r1 > r0) {
@@ -253,6 +254,7 @@ int stream_gemv_geometry(vb_ctx *ctx, StreamOp &s, int i) {
 
 struct vb_program_s {
     StreamOp *d_ops = nullptr;
+    int2 *d_rows = nullptr;       // [grid][n_ops] row ranges
     unsigned *d_bars = nullptr;   // n_groups barriers, then n_counters counters
     int *d_err = nullptr;
     int n_ops = 0, n_groups = 0, n_counters = 0, grid = 0;
@@ -280,6 +282,31 @@ int stream_program_build(vb_ctx *ctx, std::vector<StreamOp> ops, int n_groups, i
         if (waits) waited = ops[i].wait_group;
         ops[i].reuse_prev = i > 0 && !waits && same_operand(ops[i - 1], ops[i]);
     }
+    // Row partition over the CTAs: the GEMV ops of one group are
+    // independent, so their weight bytes form one space split evenly over
+    // the CTAs (op_rows_host).
+    for (size_t i = 0; i < ops.size();) {
+        size_t j = i;
+        int64_t total = 0;
+        for (; j < ops.size() && ops[j].group == ops[i].group; j++) {
+            if (ops[j].kind != OPK_GEMV) continue;
+            ops[j].part_off = total;
+            total += (int64_t)ops[j].N * ops[j].row_bytes;
+        }
+        for (size_t k = i; k < j; k++) ops[k].part_total = total;
+        i = j;
+    }
+    if ((int)ops.size() > ST_MAX_OPS)
+        return set_error(ctx, VB_ERR_INVALID_ARG, "stream program: more than %d ops", ST_MAX_OPS);
+    const int G = ctx->sm_count;
+    std::vector<int2> rows((size_t)G * ops.size(), make_int2(0, 0));
+    for (int c = 0; c < G; c++)
+        for (size_t i = 0; i < ops.size(); i++) {
+            if (ops[i].kind != OPK_GEMV) continue;
+            int64_t r0, r1;
+            op_rows_host(ops[i], c, G, r0, r1);
+            rows[(size_t)c * ops.size() + i] = make_int2((int)r0, (int)r1);
+        }
     int per_sm = 0;
     VB_CHECK(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stream_gemv_kernel, ST_THREADS, ST_SMEM_ALL));
     if (per_sm < 1) return set_error(ctx, VB_ERR_BACKEND, "streaming kernel does not fit on an SM");
@@ -292,6 +319,8 @@ int stream_program_build(vb_ctx *ctx, std::vector<StreamOp> ops, int n_groups, i
     cudaError_t e = cudaMalloc(&p->d_ops, sizeof(StreamOp) * ops.size());
     if (e == cudaSuccess) e = cudaMalloc(&p->d_bars, sizeof(unsigned) * (size_t)(n_groups + n_counters));
     if (e == cudaSuccess) e = cudaMalloc(&p->d_err, sizeof(int));
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_rows, sizeof(int2) * rows.size());
+    if (e == cudaSuccess) e = cudaMemcpy(p->d_rows, rows.data(), sizeof(int2) * rows.size(), cudaMemcpyHostToDevice);
     for (StreamOp &op : ops)
         if (op.kind == OPK_ATTN && p->d_bars) op.cnt = p->d_bars + n_groups + reinterpret_cast<size_t>(op.cnt);
     if (e == cudaSuccess) e = cudaMemcpy(p->d_ops, ops.data(), sizeof(StreamOp) * ops.size(), cudaMemcpyHostToDevice);
@@ -316,8 +345,8 @@ int stream_program_launch(vb_ctx *ctx, vb_program p, const StreamStep &step) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    VB_CHECK(ctx, cudaLaunchKernelEx(&cfg, stream_gemv_kernel, (const StreamOp *)p->d_ops, p->n_ops, p->d_bars,
-                                     p->d_err, step));
+    VB_CHECK(ctx, cudaLaunchKernelEx(&cfg, stream_gemv_kernel, (const StreamOp *)p->d_ops, (const int2 *)p->d_rows,
+                                     p->n_ops, p->d_bars, p->d_err, step));
     VB_LAUNCH_CHECK(ctx, "stream_gemv");
     return VB_OK;
 }
@@ -388,6 +417,7 @@ extern "C" int vb_program_status(vb_ctx *ctx, vb_program p, int *device_error) {
 extern "C" void vb_program_destroy(vb_program p) {
     if (!p) return;
     cudaFree(p->d_ops);
+    cudaFree(p->d_rows);
     cudaFree(p->d_bars);
     cudaFree(p->d_err);
     delete p;

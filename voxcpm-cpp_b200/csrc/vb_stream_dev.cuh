@@ -38,10 +38,6 @@ __device__ __forceinline__ void swiglu_store(const StreamOp &op, int m, int64_t 
     op.y[(int64_t)m * op.ldy + t] = bf16r(__fmul_rn(bf16r(silu_f(bf16r(g))), bf16r(u)));
 }
 
-// Rows [r0, r1) of op this CTA owns, in logical rows (an EPI_SWIGLU op is
-// split in whole gate/up pairs).
-__device__ __forceinline__ void op_rows(const StreamOp &op, int cta, int G, int64_t &r0, int64_t &r1);
-
 // Bounded wait on an mbarrier phase; false on timeout or abort.
 __device__ __forceinline__ bool wait_phase(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -66,16 +62,6 @@ __device__ __forceinline__ bool wait_grid(const unsigned *ctr, unsigned target, 
 __device__ __forceinline__ void rows_of(int64_t N, int cta, int G, int64_t &r0, int64_t &r1) {
     r0 = N * cta / G;
     r1 = N * (cta + 1) / G;
-}
-
-__device__ __forceinline__ void op_rows(const StreamOp &op, int cta, int G, int64_t &r0, int64_t &r1) {
-    if (op.epi == EPI_SWIGLU) {
-        rows_of(op.N / 2, cta, G, r0, r1);
-        r0 *= 2;
-        r1 *= 2;
-    } else {
-        rows_of(op.N, cta, G, r0, r1);
-    }
 }
 
 __device__ __forceinline__ int dot32_i8(const int4 &a0, const int4 &a1, const int4 &b0, const int4 &b1) {

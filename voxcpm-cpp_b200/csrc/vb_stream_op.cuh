@@ -42,6 +42,7 @@ struct alignas(16) StreamOp {
     int rows_per_chunk, row_bytes, sc_bulk;
     int qrule;              // Q8_0 activation rule (VB_QRULE_*)
     int reuse_prev;         // same activation operand as the previous op, no wait between (set at build)
+    int64_t part_off, part_total;   // this op's first weight byte in its group, the group's bytes (set at build)
     // prologue / epilogue
     int kind, pro, epi;
     const float *pro_w;     // RMSNorm weight
@@ -69,6 +70,7 @@ constexpr int ST_CONSUMERS = ST_CONSUMER_WARPS * 32;
 constexpr int ST_THREADS = ST_CONSUMERS + 32;
 constexpr int ST_XBYTES = 16384;                // activation operand (int8 or fp16)
 constexpr int ST_MMAX = 8;
+constexpr int ST_MAX_OPS = 1024;                // ops per program (row table in shared memory)
 constexpr size_t ST_SMEM = (size_t)ST_STAGES * ST_SLOT + (size_t)ST_STAGES * ST_SC_SLOT + ST_XBYTES +
                            (ST_XBYTES / 32) * 4 + 2 * ST_STAGES * 8 + 64;
 
@@ -100,6 +102,28 @@ inline bool same_operand(const StreamOp &a, const StreamOp &b) {
     return a.kind == OPK_GEMV && b.kind == OPK_GEMV && a.x == b.x && a.K == b.K && a.M == b.M &&
            a.wtype == b.wtype && a.ldx == b.ldx && a.pro == b.pro && a.pro_w == b.pro_w && a.qrule == b.qrule &&
            a.pro_len == b.pro_len && a.eps == b.eps;
+}
+
+// Rows [r0, r1) of GEMV op `op` that CTA `cta` of G streams.  The ops of
+// one group are independent, so their weight bytes form one space that is
+// split evenly: CTA c streams bytes [c*T/G, (c+1)*T/G) of the group
+// (T = part_total), whole rows of at most a few ops.  A small op is then
+// read by a few CTAs in whole ring chunks rather than a sliver by every
+// CTA, and each CTA quantizes only the activations of the ops it touches.
+// Units are rows, or gate/up row pairs for EPI_SWIGLU.  Computed once on
+// the host into the program's row table.
+inline void op_rows_host(const StreamOp &op, int cta, int G, int64_t &r0, int64_t &r1) {
+    const bool swz = op.epi == EPI_SWIGLU;
+    const int64_t units = swz ? op.N / 2 : op.N;
+    const int64_t ub = swz ? 2 * (int64_t)op.row_bytes : (int64_t)op.row_bytes;
+    const int64_t lo = op.part_total * cta / G - op.part_off;
+    const int64_t hi = op.part_total * (cta + 1) / G - op.part_off;
+    int64_t u0 = lo <= 0 ? 0 : (lo + ub - 1) / ub;
+    int64_t u1 = hi <= 0 ? 0 : (hi + ub - 1) / ub;
+    u0 = u0 < units ? u0 : units;
+    u1 = u1 < units ? u1 : units;
+    r0 = swz ? 2 * u0 : u0;
+    r1 = swz ? 2 * u1 : u1;
 }
 
 // Ring geometry of a GEMV op (wtype, K, N, M set); op index i for messages.
