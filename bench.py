@@ -47,9 +47,9 @@ IN_LEN = {"a": HIDDEN, "o": NH * HD, "d": FFN}
 IN_OFF = {"a": 0, "o": HIDDEN, "d": HIDDEN + NH * HD}
 IN_PER_LAYER = HIDDEN + NH * HD + FFN
 OUT_PER_LAYER = sum(s[2] for s in SHAPES)
-# dram bytes per launch of the config-1 GEMV (N=6144, K=2048) from the ncu
-# capture summarised in profiles/gemv_q8_0_config1.md; None until captured.
-NCU_TRAFFIC_CONFIG1 = None
+# dram bytes (read + write) of one headline-step launch of stream_gemv_kernel
+# from the ncu capture summarised in profiles/stream_gemv_headline_step.md
+NCU_TRAFFIC_STEP = 1_412_116_664
 
 
 def q8_bytes(K, N):
@@ -372,7 +372,9 @@ def run_b200(args, rank, world, local_rank):
             "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s", "frac": per_gpu / peak,
                          "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                          "kernel": "vb::stream_gemv_kernel (one persistent launch per step)",
-                         "traffic": NCU_TRAFFIC_CONFIG1, "traffic_unit": "bytes per config-1 GEMV",
+                         "traffic": NCU_TRAFFIC_STEP / 1e9 * args.steps / (ms * 1e-3) if NCU_TRAFFIC_STEP else None,
+                         "traffic_unit": "GB/s (ncu dram bytes per launch x launches / time)",
+                         "traffic_bytes_per_launch": NCU_TRAFFIC_STEP, "alg_bytes_per_launch": STEP_BYTES,
                          "achieved_config1": c1_gbs, "config1_us_per_gemv": per_gemv_ms * 1e3,
                          "config1_alg_bytes": alg_bytes(2048, 6144),
                          "separate_launches_gbs": per_launch_gbs,
@@ -495,6 +497,78 @@ def run_config1(args, local_rank):
     prog.close()
     for w in ws:
         w.release()
+    ctx.close()
+    return 0 if rc == 0 else 1
+
+
+def run_gemm_case(args, local_rank):
+    """Profiling case: one tensor-core mat-mul shape (--gemm-shape M,K,N,
+    --gemm-type q8_0|f16) launched warmup + steps times.  Prints TFLOP/s."""
+    import torch
+    import vcpm_b200 as vb
+    torch.cuda.set_device(local_rank)
+    ctx = vb.Context(local_rank)
+    M, K, N = (int(v) for v in args.gemm_shape.split(","))
+    rng = np.random.default_rng(5)
+    if args.gemm_type == "q8_0":
+        w = ctx.weight(vb.TYPE_Q8_0, K, N, synth_q8_0(rng, N, K))
+    else:
+        w = ctx.weight(vb.TYPE_F16, K, N, (0.02 * rng.standard_normal((N, K))).astype(np.float16).view(np.uint16))
+    x = torch.randn(M, K, device="cuda")
+    y = torch.zeros(M, N, device="cuda")
+    ev0, ev1 = ctx.event(), ctx.event()
+    for _ in range(args.warmup):
+        ctx.matmul(w, x, M, y)
+    ctx.record(ev0)
+    for _ in range(args.steps):
+        ctx.matmul(w, x, M, y)
+    ctx.record(ev1)
+    ms = ctx.elapsed_ms(ev0, ev1) / args.steps
+    rc, derr = ctx.device_status()
+    print(json.dumps({"mode": "gemm", "shape": [M, K, N], "type": args.gemm_type, "us_per_call": ms * 1e3,
+                      "tflops": 2 * M * N * K / (ms * 1e-3) / 1e12, "device_error": derr}), flush=True)
+    w.release()
+    ctx.close()
+    return 0 if rc == 0 else 1
+
+
+def run_decode_case(args, local_rank):
+    """Profiling case: the 28-layer decode step (vb_decoder_step, one
+    persistent launch per token) after a 256-token prefill; warmup + steps
+    tokens.  Prints tokens/s."""
+    import torch
+    import vcpm_b200 as vb
+    torch.cuda.set_device(local_rank)
+    ctx = vb.Context(local_rank)
+    rng = np.random.default_rng(7)
+    layers = []
+    for l in range(LAYERS):
+        L = {name: synth_q8_0(rng, N, K) for name, K, N, _ in SHAPES}
+        L["attn_norm"] = (1.0 + 0.02 * rng.standard_normal(HIDDEN)).astype(np.float32)
+        L["ffn_norm"] = (1.0 + 0.02 * rng.standard_normal(HIDDEN)).astype(np.float32)
+        layers.append(L)
+    fn = (1.0 + 0.02 * rng.standard_normal(HIDDEN)).astype(np.float32)
+    lm = vb.LM(ctx, vb.LMConfig(HIDDEN, NH, NKV, HD, FFN, LAYERS, 1e-5, 10000.0, 0, 0.0, vb.TYPE_Q8_0), layers, fn)
+    P = 256
+    kv = vb.KV(ctx, lm, 1, P + args.warmup + args.steps)
+    x = (torch.randn(P + args.warmup + args.steps, HIDDEN, device="cuda") * 0.5).to(torch.bfloat16).float()
+    out = torch.zeros_like(x)
+    lm.forward(kv, [0], [0], P, x[:P], out[:P])
+    dec = vb.Decoder(ctx, lm, kv, [0])
+    ev0, ev1 = ctx.event(), ctx.event()
+    for i in range(args.warmup):
+        dec.step([P + i], x[P + i:P + i + 1], out[P + i:P + i + 1])
+    ctx.record(ev0)
+    for i in range(args.warmup, args.warmup + args.steps):
+        dec.step([P + i], x[P + i:P + i + 1], out[P + i:P + i + 1])
+    ctx.record(ev1)
+    ms = ctx.elapsed_ms(ev0, ev1) / args.steps
+    rc, derr = dec.status()
+    print(json.dumps({"mode": "decode", "tokens_per_s": 1e3 / ms, "ms_per_token": ms, "device_error": derr}),
+          flush=True)
+    dec.close()
+    kv.close()
+    lm.close()
     ctx.close()
     return 0 if rc == 0 else 1
 
@@ -677,8 +751,11 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-utts", type=int, default=64)
     ap.add_argument("--e2e-patches", type=int, default=100)
-    ap.add_argument("--mode", default="full", choices=["full", "config1"],
-                    help="config1: only the config-1 streaming program (profiling case)")
+    ap.add_argument("--mode", default="full", choices=["full", "config1", "gemm", "decode"],
+                    help="config1 / gemm / decode: small profiling cases (config-1 streaming program, one "
+                         "tensor-core mat-mul shape, the single-launch decode step)")
+    ap.add_argument("--gemm-shape", default="1408,1024,8192")
+    ap.add_argument("--gemm-type", default="q8_0", choices=["q8_0", "f16"])
     ap.add_argument("--copies", type=int, default=56)
     args = ap.parse_args()
     if args.warmup < 3:
@@ -690,6 +767,10 @@ def main():
         return run_reference(args, rank, world)
     if args.mode == "config1":
         return run_config1(args, local_rank)
+    if args.mode == "gemm":
+        return run_gemm_case(args, local_rank)
+    if args.mode == "decode":
+        return run_decode_case(args, local_rank)
     if world > 1:
         import datetime
         import torch
