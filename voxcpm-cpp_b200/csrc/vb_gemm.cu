@@ -42,15 +42,16 @@ namespace vb {
 
 constexpr int GM_BM = 128;
 constexpr int GM_BK = 64;
-constexpr int GM_THREADS = 320;
+constexpr int GM_THREADS = 448;        // warp 0 TMA, 1 MMA + TMEM, 2..9 convert, 10..13 epilogue
 constexpr int GM_CONV_THREADS = 256;
+constexpr int GM_EPI_THREADS = 128;
 constexpr int GM_MAX_STAGES = 6;
 constexpr int GM_SMEM_BUDGET = 220 * 1024;
 
 struct GemmArgs {
     int q8;                 // 1: Q8_0 weights (hi/lo split), 0: F16 weights
     int K, N, M, BN;
-    int kt_total, kt_per_split, splits, tiles_m;
+    int kt_total, kt_per_split, splits, tiles_m, tiles_n;
     int n_tma, n_conv;      // pipeline depths
     uint32_t tmem_cols;
     const uint16_t *sc;     // Q8_0 scales [N][K/32]
@@ -133,11 +134,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 const __grid_constant__ CUtensorMap tm_bl, const GemmArgs a) {
     extern __shared__ uint8_t gsm_raw[];
     uint8_t *gsm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~(uintptr_t)1023);
-    __shared__ uint64_t bars[4 * GM_MAX_STAGES + 1];
+    __shared__ uint64_t bars[4 * GM_MAX_STAGES + 4];
     __shared__ uint32_t s_tmem;
     __shared__ int s_last;
     uint64_t *full = bars, *empty = bars + GM_MAX_STAGES, *cfull = bars + 2 * GM_MAX_STAGES,
-             *cempty = bars + 3 * GM_MAX_STAGES, *tfull = bars + 4 * GM_MAX_STAGES;
+             *cempty = bars + 3 * GM_MAX_STAGES, *tfull = bars + 4 * GM_MAX_STAGES, *tempty = tfull + 2;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int BN = a.BN;
@@ -145,14 +146,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     const uint32_t b_bytes = (uint32_t)BN * 128;
     const uint32_t stage_bytes = a_bytes + b_bytes * (a.q8 ? 2 : 1);
     uint8_t *conv = gsm + (size_t)a.n_tma * stage_bytes;                 // converted A: [n_conv][hi 16K | lo 16K]
-
-    int bid = blockIdx.x;
-    const int split = bid % a.splits;
-    bid /= a.splits;
-    const int tm = bid % a.tiles_m, tn = bid / a.tiles_m;
-    const int n0 = tn * GM_BM, m0 = tm * BN;
-    const int kt0 = split * a.kt_per_split;
-    const int nkt = min(a.kt_per_split, a.kt_total - kt0);
+    const int n_tiles = a.tiles_n * a.tiles_m * a.splits;
+    const uint32_t acc_cols = a.tmem_cols >> 1;                         // two accumulators
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < GM_MAX_STAGES; s++) {
@@ -161,7 +156,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             mbar_init(&cfull[s], GM_CONV_THREADS / 32);
             mbar_init(&cempty[s], 1);
         }
-        mbar_init(tfull, 1);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], GM_EPI_THREADS / 32);
+        }
         mbar_fence_init();
     }
     if (warp == 1) {
@@ -175,154 +173,190 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = s_tmem;
 
+    // Tiles t = blockIdx.x, + gridDim.x, ...; split fastest, then the
+    // activation tile, so CTAs running at the same time share weight tiles.
+    auto coords = [&](int t, int &n0, int &m0, int &split, int &kt0, int &nkt) {
+        split = t % a.splits;
+        t /= a.splits;
+        m0 = (t % a.tiles_m) * BN;
+        n0 = (t / a.tiles_m) * GM_BM;
+        kt0 = split * a.kt_per_split;
+        nkt = min(a.kt_per_split, a.kt_total - kt0);
+    };
+
     if (warp == 0) {
         // ---------------------------------------------------------- TMA
         if (lane == 0) {
-            int issued[GM_MAX_STAGES] = {0, 0, 0, 0, 0, 0};
-            for (int i = 0; i < nkt; i++) {
-                const int s = i % a.n_tma;
-                const uint32_t ph = (uint32_t)(i / a.n_tma) & 1u;
-                if (!gm_wait(&empty[s], ph ^ 1u)) { atomicCAS(a.err, 0, 11); break; }
-                uint8_t *st = gsm + (size_t)s * stage_bytes;
-                mbar_arrive_expect_tx(&full[s], stage_bytes);
-                const int kx = (kt0 + i) * GM_BK;
-                tma_load_2d(st, &tm_w, kx, n0, &full[s]);
-                tma_load_2d(st + a_bytes, &tm_bh, kx, m0, &full[s]);
-                if (a.q8) tma_load_2d(st + a_bytes + b_bytes, &tm_bl, kx, m0, &full[s]);
-                issued[s]++;
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+                int n0, m0, split, kt0, nkt;
+                coords(t, n0, m0, split, kt0, nkt);
+                for (int i = 0; i < nkt; i++, it++) {
+                    const int s = it % a.n_tma;
+                    const uint32_t ph = (uint32_t)(it / a.n_tma) & 1u;
+                    if (!gm_wait(&empty[s], ph ^ 1u)) { atomicCAS(a.err, 0, 11); ok = false; break; }
+                    uint8_t *st = gsm + (size_t)s * stage_bytes;
+                    mbar_arrive_expect_tx(&full[s], stage_bytes);
+                    const int kx = (kt0 + i) * GM_BK;
+                    tma_load_2d(st, &tm_w, kx, n0, &full[s]);
+                    tma_load_2d(st + a_bytes, &tm_bh, kx, m0, &full[s]);
+                    if (a.q8) tma_load_2d(st + a_bytes + b_bytes, &tm_bl, kx, m0, &full[s]);
+                }
             }
             // every issued copy has landed before the CTA can finish
-            for (int s = 0; s < a.n_tma; s++)
-                if (issued[s]) gm_wait(&full[s], (uint32_t)(issued[s] - 1) & 1u);
+            for (int s = 0; s < a.n_tma; s++) {
+                const int fills = it / a.n_tma + (it % a.n_tma > s ? 1 : 0);
+                if (fills) gm_wait(&full[s], (uint32_t)(fills - 1) & 1u);
+            }
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------- MMA
         if (lane == 0) {
             const uint32_t idesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(GM_BM >> 4) << 24);
+            int it = 0, tc = 0;
             bool ok = true;
-            for (int i = 0; i < nkt && ok; i++) {
-                const int s = i % a.n_tma;
-                const uint32_t ph = (uint32_t)(i / a.n_tma) & 1u;
-                const int c = i % a.n_conv;
-                const uint32_t cph = (uint32_t)(i / a.n_conv) & 1u;
-                if (!gm_wait(&full[s], ph) || (a.q8 && !gm_wait(&cfull[c], cph))) {
-                    atomicCAS(a.err, 0, 12);
-                    ok = false;
-                    break;
-                }
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, tc++) {
+                int n0, m0, split, kt0, nkt;
+                coords(t, n0, m0, split, kt0, nkt);
+                const int buf = tc & 1;
+                if (!gm_wait(&tempty[buf], ((uint32_t)(tc >> 1) & 1u) ^ 1u)) { atomicCAS(a.err, 0, 15); break; }
                 tc_fence_after();
-                uint8_t *st = gsm + (size_t)s * stage_bytes;
-                const uint8_t *ahi = a.q8 ? conv + (size_t)c * 32768 : st;
-                const uint8_t *alo = ahi + 16384;
-                const uint8_t *bhi = st + a_bytes, *blo = bhi + b_bytes;
-#pragma unroll
-                for (int k = 0; k < GM_BK / 16; k++) {
-                    const uint32_t acc = (i | k) != 0;
-                    umma_f16(tmem, sw128_desc(ahi + 32 * k), sw128_desc(bhi + 32 * k), idesc, acc);
-                    if (a.q8) {
-                        umma_f16(tmem, sw128_desc(ahi + 32 * k), sw128_desc(blo + 32 * k), idesc, 1u);
-                        umma_f16(tmem, sw128_desc(alo + 32 * k), sw128_desc(bhi + 32 * k), idesc, 1u);
+                const uint32_t acc_t = tmem + (uint32_t)buf * acc_cols;
+                for (int i = 0; i < nkt; i++, it++) {
+                    const int s = it % a.n_tma;
+                    const uint32_t ph = (uint32_t)(it / a.n_tma) & 1u;
+                    const int c = it % a.n_conv;
+                    const uint32_t cph = (uint32_t)(it / a.n_conv) & 1u;
+                    if (!gm_wait(&full[s], ph) || (a.q8 && !gm_wait(&cfull[c], cph))) {
+                        atomicCAS(a.err, 0, 12);
+                        ok = false;
+                        break;
                     }
+                    tc_fence_after();
+                    uint8_t *st = gsm + (size_t)s * stage_bytes;
+                    const uint8_t *ahi = a.q8 ? conv + (size_t)c * 32768 : st;
+                    const uint8_t *alo = ahi + 16384;
+                    const uint8_t *bhi = st + a_bytes, *blo = bhi + b_bytes;
+#pragma unroll
+                    for (int k = 0; k < GM_BK / 16; k++) {
+                        const uint32_t acc = (i | k) != 0;
+                        umma_f16(acc_t, sw128_desc(ahi + 32 * k), sw128_desc(bhi + 32 * k), idesc, acc);
+                        if (a.q8) {
+                            umma_f16(acc_t, sw128_desc(ahi + 32 * k), sw128_desc(blo + 32 * k), idesc, 1u);
+                            umma_f16(acc_t, sw128_desc(alo + 32 * k), sw128_desc(bhi + 32 * k), idesc, 1u);
+                        }
+                    }
+                    umma_commit(&empty[s]);
+                    if (a.q8) umma_commit(&cempty[c]);
                 }
-                umma_commit(&empty[s]);
-                if (a.q8) umma_commit(&cempty[c]);
+                umma_commit(&tfull[buf]);   // fires once this tile's MMAs have completed
             }
-            umma_commit(tfull);   // fires once every MMA above has completed
+        }
+    } else if (warp < 2 + GM_CONV_THREADS / 32) {
+        // ------------------------------------------------ convert (Q8_0)
+        // thread t converts the 16-byte pieces t and t + 256 of the raw
+        // tile (row i/4, values 16*(i%4) .. +16: half of Q8_0 block
+        // (i%4)/2), so a warp reads 512 consecutive bytes (no bank
+        // conflicts) and writes whole swizzled 16-byte chunks.
+        if (a.q8) {
+            const int t = threadIdx.x - 64;
+            const int kb_total = a.K / 32;
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+                int n0, m0, split, kt0, nkt;
+                coords(tile, n0, m0, split, kt0, nkt);
+                int rr[2], qq[2];
+                const uint16_t *scp[2];
+                bool rv[2];
+#pragma unroll
+                for (int u = 0; u < 2; u++) {
+                    const int i = t + 256 * u;
+                    rr[u] = i >> 2;
+                    qq[u] = i & 3;
+                    rv[u] = n0 + rr[u] < a.N;
+                    scp[u] = a.sc + (int64_t)(rv[u] ? n0 + rr[u] : 0) * kb_total + (qq[u] >> 1);
+                }
+                for (int i = 0; i < nkt; i++, it++) {
+                    const int s = it % a.n_tma;
+                    const uint32_t ph = (uint32_t)(it / a.n_tma) & 1u;
+                    const int c = it % a.n_conv;
+                    const uint32_t cph = (uint32_t)(it / a.n_conv) & 1u;
+                    uint16_t dh[2];
+#pragma unroll
+                    for (int u = 0; u < 2; u++) dh[u] = rv[u] ? __ldg(scp[u] + (kt0 + i) * 2) : (uint16_t)0;
+                    const bool okf = gm_wait(&full[s], ph), okc = gm_wait(&cempty[c], cph ^ 1u);
+                    if (!okf || !okc) { atomicCAS(a.err, 0, 13); ok = false; break; }
+                    const int4 *src = reinterpret_cast<const int4 *>(gsm + (size_t)s * stage_bytes);
+                    int4 raw[2];
+#pragma unroll
+                    for (int u = 0; u < 2; u++) raw[u] = src[t + 256 * u];
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        uint8_t *hi = conv + (size_t)c * 32768 + rr[u] * 128;
+                        uint8_t *lo = hi + 16384;
+                        const __half2 d2 = __half2half2(__ushort_as_half(dh[u]));   // the fp16 scale itself
+                        const uint32_t w4[4] = {(uint32_t)raw[u].x, (uint32_t)raw[u].y, (uint32_t)raw[u].z,
+                                                (uint32_t)raw[u].w};
+#pragma unroll
+                        for (int hc = 0; hc < 2; hc++) {   // two 8-value chunks
+                            uint32_t h[4], l[4];
+#pragma unroll
+                            for (int e = 0; e < 2; e++) {
+                                // 4 int8 -> two exact half2: bytes q+128 under exponent 0x64
+                                // give 1152 + q, minus 1152 exactly
+                                const uint32_t x = w4[2 * hc + e] ^ 0x80808080u;
+                                const uint32_t p01 = __byte_perm(x, 0x64646464u, 0x5140);
+                                const uint32_t p23 = __byte_perm(x, 0x64646464u, 0x7362);
+                                const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6480));   // 1152
+                                const __half2 q01 = __hsub2(*reinterpret_cast<const __half2 *>(&p01), bias);
+                                const __half2 q23 = __hsub2(*reinterpret_cast<const __half2 *>(&p23), bias);
+                                // hi = fp16(d*q) (one rounding of the exact product);
+                                // lo = fp16(d*q - hi) (fused: exact remainder, one rounding)
+                                const __half2 h01 = __hmul2(d2, q01), h23 = __hmul2(d2, q23);
+                                const __half2 l01 = __hfma2(d2, q01, __hneg2(h01));
+                                const __half2 l23 = __hfma2(d2, q23, __hneg2(h23));
+                                h[2 * e] = *reinterpret_cast<const uint32_t *>(&h01);
+                                h[2 * e + 1] = *reinterpret_cast<const uint32_t *>(&h23);
+                                l[2 * e] = *reinterpret_cast<const uint32_t *>(&l01);
+                                l[2 * e + 1] = *reinterpret_cast<const uint32_t *>(&l23);
+                            }
+                            const int chunk = (2 * qq[u] + hc) ^ (rr[u] & 7);   // 128-byte swizzle
+                            *reinterpret_cast<uint4 *>(hi + chunk * 16) = make_uint4(h[0], h[1], h[2], h[3]);
+                            *reinterpret_cast<uint4 *>(lo + chunk * 16) = make_uint4(l[0], l[1], l[2], l[3]);
+                        }
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor core
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&cfull[c]);
+                }
+            }
         }
     } else {
-        // ------------------------------------------- convert, then epilogue
-        const int t = threadIdx.x - 64;
-        if (a.q8) {
-            // thread t converts the 16-byte pieces t and t + 256 of the raw
-            // tile (row i/4, values 16*(i%4) .. +16: half of Q8_0 block
-            // (i%4)/2), so a warp reads 512 consecutive bytes (no bank
-            // conflicts) and writes whole swizzled 16-byte chunks.
-            const int kb_total = a.K / 32;
-            int rr[2], qq[2];
-            const uint16_t *scp[2];
-            bool rv[2];
-            float dn[2];
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                const int i = t + 256 * u;
-                rr[u] = i >> 2;
-                qq[u] = i & 3;
-                rv[u] = n0 + rr[u] < a.N;
-                scp[u] = a.sc + (int64_t)(rv[u] ? n0 + rr[u] : 0) * kb_total + (qq[u] >> 1);
-                dn[u] = rv[u] ? h2f(__ldg(scp[u] + kt0 * 2)) : 0.0f;
-            }
-            for (int i = 0; i < nkt; i++) {
-                const int s = i % a.n_tma;
-                const uint32_t ph = (uint32_t)(i / a.n_tma) & 1u;
-                const int c = i % a.n_conv;
-                const uint32_t cph = (uint32_t)(i / a.n_conv) & 1u;
-                float d[2];
-#pragma unroll
-                for (int u = 0; u < 2; u++) {
-                    d[u] = dn[u];
-                    if (rv[u] && i + 1 < nkt) dn[u] = h2f(__ldg(scp[u] + (kt0 + i + 1) * 2));
-                }
-                const bool okf = gm_wait(&full[s], ph), okc = gm_wait(&cempty[c], cph ^ 1u);
-                if (!okf || !okc) { atomicCAS(a.err, 0, 13); break; }
-                const int4 *src = reinterpret_cast<const int4 *>(gsm + (size_t)s * stage_bytes);
-                int4 raw[2];
-#pragma unroll
-                for (int u = 0; u < 2; u++) raw[u] = src[t + 256 * u];
-#pragma unroll
-                for (int u = 0; u < 2; u++) {
-                    uint8_t *hi = conv + (size_t)c * 32768 + rr[u] * 128;
-                    uint8_t *lo = hi + 16384;
-                    const __half2 d2 = __half2half2(__float2half_rn(d[u]));   // the fp16 scale itself
-                    const uint32_t w4[4] = {(uint32_t)raw[u].x, (uint32_t)raw[u].y, (uint32_t)raw[u].z,
-                                            (uint32_t)raw[u].w};
-#pragma unroll
-                    for (int hc = 0; hc < 2; hc++) {   // two 8-value chunks
-                        uint32_t h[4], l[4];
-#pragma unroll
-                        for (int e = 0; e < 2; e++) {
-                            // 4 int8 -> two exact half2: bytes q+128 under exponent 0x64
-                            // give 1152 + q, minus 1152 exactly
-                            const uint32_t x = w4[2 * hc + e] ^ 0x80808080u;
-                            const uint32_t p01 = __byte_perm(x, 0x64646464u, 0x5140);
-                            const uint32_t p23 = __byte_perm(x, 0x64646464u, 0x7362);
-                            const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6480));   // 1152
-                            const __half2 q01 = __hsub2(*reinterpret_cast<const __half2 *>(&p01), bias);
-                            const __half2 q23 = __hsub2(*reinterpret_cast<const __half2 *>(&p23), bias);
-                            // hi = fp16(d*q) (one rounding of the exact product);
-                            // lo = fp16(d*q - hi) (fused: exact remainder, one rounding)
-                            const __half2 h01 = __hmul2(d2, q01), h23 = __hmul2(d2, q23);
-                            const __half2 l01 = __hfma2(d2, q01, __hneg2(h01));
-                            const __half2 l23 = __hfma2(d2, q23, __hneg2(h23));
-                            h[2 * e] = *reinterpret_cast<const uint32_t *>(&h01);
-                            h[2 * e + 1] = *reinterpret_cast<const uint32_t *>(&h23);
-                            l[2 * e] = *reinterpret_cast<const uint32_t *>(&l01);
-                            l[2 * e + 1] = *reinterpret_cast<const uint32_t *>(&l23);
-                        }
-                        const int chunk = (2 * qq[u] + hc) ^ (rr[u] & 7);   // 128-byte swizzle
-                        *reinterpret_cast<uint4 *>(hi + chunk * 16) = make_uint4(h[0], h[1], h[2], h[3]);
-                        *reinterpret_cast<uint4 *>(lo + chunk * 16) = make_uint4(l[0], l[1], l[2], l[3]);
-                    }
-                }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor core
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&cfull[c]);
-            }
-        }
-        // epilogue: TMEM lane quarter (warp % 4) = 32 weight rows; the two
-        // warps of a quarter take alternate 16-column groups
-        const bool okt = gm_wait(tfull, 0);
-        tc_fence_after();
-        const int q = warp & 3, colgrp = (warp - 2) >> 2;
-        const int r = q * 32 + lane, n = n0 + r;
-        const bool split_k = a.splits > 1;
-        if (okt) {
-            for (int j = colgrp; j * 16 < BN; j += 2) {
+        // -------------------------------------------------------- epilogue
+        // warp w reads TMEM lanes 32*(w%4) .. +32 (weight rows) of the
+        // accumulator; the MMAs of the next tile run into the other one.
+        const int et = threadIdx.x - (2 + GM_CONV_THREADS / 32) * 32;
+        const int q = warp & 3;
+        int tc = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, tc++) {
+            int n0, m0, split, kt0, nkt;
+            coords(tile, n0, m0, split, kt0, nkt);
+            const int buf = tc & 1;
+            const bool okt = gm_wait(&tfull[buf], (uint32_t)(tc >> 1) & 1u);
+            tc_fence_after();
+            const int r = q * 32 + lane, n = n0 + r;
+            const bool split_k = a.splits > 1;
+            if (!okt) atomicCAS(a.err, 0, 14);
+            for (int j = 0; okt && j * 16 < BN; j++) {
                 uint32_t v[16];
-                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(j * 16), v);
+                tmem_ld16(tmem + (uint32_t)buf * acc_cols + ((uint32_t)(q * 32) << 16) + (uint32_t)(j * 16), v);
                 if (n < a.N) {
                     if (split_k) {
                         // partials [split][N][Mp], this thread's 16 columns contiguous
-                        float4 *pw = reinterpret_cast<float4 *>(a.ws + ((int64_t)split * a.N + n) * a.Mp + m0 + j * 16);
+                        float4 *pw =
+                            reinterpret_cast<float4 *>(a.ws + ((int64_t)split * a.N + n) * a.Mp + m0 + j * 16);
 #pragma unroll
                         for (int q4 = 0; q4 < 4; q4++)
                             pw[q4] = make_float4(__uint_as_float(v[4 * q4]), __uint_as_float(v[4 * q4 + 1]),
@@ -337,59 +371,62 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                     }
                 }
             }
-        } else {
-            atomicCAS(a.err, 0, 14);
-        }
-        if (split_k) {
-            // last CTA of this tile adds the split partials in split order
-            asm volatile("bar.sync 2, %0;" ::"r"(GM_CONV_THREADS) : "memory");
-            if (t == 0) {
-                fence_acq_rel_gpu();
-                const unsigned tile = (unsigned)(tn * a.tiles_m + tm);
-                s_last = atomicAdd(a.cnt + tile, 1u) == (unsigned)(a.splits - 1);
-                if (s_last) {
+            // the accumulator is free for the tile after next
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+            if (split_k) {
+                // the last CTA of this tile adds the split partials in split order
+                asm volatile("bar.sync 2, %0;" ::"r"(GM_EPI_THREADS) : "memory");
+                if (et == 0) {
                     fence_acq_rel_gpu();
-                    a.cnt[tile] = 0;   // ready for the next launch
+                    const unsigned tid = (unsigned)(tile / a.splits);
+                    s_last = atomicAdd(a.cnt + tid, 1u) == (unsigned)(a.splits - 1);
+                    if (s_last) {
+                        fence_acq_rel_gpu();
+                        a.cnt[tid] = 0;   // ready for the next launch
+                    }
                 }
-            }
-            asm volatile("bar.sync 2, %0;" ::"r"(GM_CONV_THREADS) : "memory");
-            if (s_last && n < a.N) {
-                // 16 columns x 4 splits (16 vector loads) in flight at a
-                // time; the sums still run in split order
+                asm volatile("bar.sync 2, %0;" ::"r"(GM_EPI_THREADS) : "memory");
+                if (s_last && n < a.N) {
+                    // 16 columns x 4 splits (16 vector loads) in flight at a
+                    // time; the sums still run in split order
 #pragma unroll 1
-                for (int j = colgrp; j * 16 < BN; j += 2) {
-                    float4 acc[4];
+                    for (int j = 0; j * 16 < BN; j++) {
+                        float4 acc[4];
 #pragma unroll
-                    for (int q4 = 0; q4 < 4; q4++) acc[q4] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (int q4 = 0; q4 < 4; q4++) acc[q4] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
-                    for (int s0 = 0; s0 < a.splits; s0 += 4) {
-                        float4 v[4][4];
+                        for (int s0 = 0; s0 < a.splits; s0 += 4) {
+                            float4 vv[4][4];
 #pragma unroll
-                        for (int u = 0; u < 4; u++) {
-                            const float4 *pr =
-                                reinterpret_cast<const float4 *>(a.ws + ((int64_t)(s0 + u) * a.N + n) * a.Mp + m0 + j * 16);
+                            for (int u = 0; u < 4; u++) {
+                                const float4 *pr = reinterpret_cast<const float4 *>(
+                                    a.ws + ((int64_t)(s0 + u) * a.N + n) * a.Mp + m0 + j * 16);
 #pragma unroll
-                            for (int q4 = 0; q4 < 4; q4++)
-                                v[u][q4] = s0 + u < a.splits ? __ldcg(pr + q4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                                for (int q4 = 0; q4 < 4; q4++)
+                                    vv[u][q4] = s0 + u < a.splits ? __ldcg(pr + q4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                            }
+#pragma unroll
+                            for (int u = 0; u < 4; u++)
+                                if (s0 + u < a.splits)
+#pragma unroll
+                                    for (int q4 = 0; q4 < 4; q4++) {
+                                        acc[q4].x = __fadd_rn(acc[q4].x, vv[u][q4].x);
+                                        acc[q4].y = __fadd_rn(acc[q4].y, vv[u][q4].y);
+                                        acc[q4].z = __fadd_rn(acc[q4].z, vv[u][q4].z);
+                                        acc[q4].w = __fadd_rn(acc[q4].w, vv[u][q4].w);
+                                    }
                         }
+                        const float *af = reinterpret_cast<const float *>(acc);
 #pragma unroll
-                        for (int u = 0; u < 4; u++)
-                            if (s0 + u < a.splits)
-#pragma unroll
-                                for (int q4 = 0; q4 < 4; q4++) {
-                                    acc[q4].x = __fadd_rn(acc[q4].x, v[u][q4].x);
-                                    acc[q4].y = __fadd_rn(acc[q4].y, v[u][q4].y);
-                                    acc[q4].z = __fadd_rn(acc[q4].z, v[u][q4].z);
-                                    acc[q4].w = __fadd_rn(acc[q4].w, v[u][q4].w);
-                                }
-                    }
-                    const float *af = reinterpret_cast<const float *>(acc);
-#pragma unroll
-                    for (int cc = 0; cc < 16; cc++) {
-                        const int m = m0 + j * 16 + cc;
-                        if (m < a.M) a.y[gm_out_row(a, m) * a.ldy + n] = gm_epilogue(a, n, af[cc]);
+                        for (int cc = 0; cc < 16; cc++) {
+                            const int m = m0 + j * 16 + cc;
+                            if (m < a.M) a.y[gm_out_row(a, m) * a.ldy + n] = gm_epilogue(a, n, af[cc]);
+                        }
                     }
                 }
+                asm volatile("bar.sync 2, %0;" ::"r"(GM_EPI_THREADS) : "memory");   // s_last reused next tile
             }
         }
     }
@@ -520,25 +557,43 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
     if (!gs) return set_error(ctx, VB_ERR_OOM, "gemm: state allocation failed");
     const bool q8 = w->type == VB_TYPE_Q8_0;
     const int K = (int)w->K, N = (int)w->N;
-    // Activation tile width: the widest (fewest weight re-reads) that still
-    // gives about one tile per SM; below that, split K to fill the SMs.
+    // Tile width and K split (choices measured on B200).  F16: the widest
+    // tile that still gives about one tile per SM, then a K split only when
+    // tiles are scarce.  Q8_0 (three MMAs per k-step, so per-unit work is
+    // heavier): a small cost model of the persistent grid, time ~ waves x
+    // (BN x k-tiles per unit + a fixed per-unit overhead), which also
+    // splits K to even out the last wave.
     const int tiles_n = (N + GM_BM - 1) / GM_BM;
     const int mr = (int)((M + 15) / 16 * 16);
-    int BN = std::min(256, mr);
-    for (int cand : {256, 128, 64}) {
-        if (cand > mr) continue;
-        if (q8 && cand > 128 && mr > 128) continue;   // hi/lo operands: keep 4 ring stages
-        BN = cand;
-        if ((int64_t)tiles_n * ((M + cand - 1) / cand) * 5 >= (int64_t)ctx->sm_count * 4) break;
+    const int kt_total = K / GM_BK;
+    int BN = 0, splits = 1;
+    if (!q8) {
+        BN = std::min(256, mr);
+        for (int cand : {256, 128, 64}) {
+            if (cand > mr) continue;
+            BN = cand;
+            if ((int64_t)tiles_n * ((M + cand - 1) / cand) * 5 >= (int64_t)ctx->sm_count * 4) break;
+        }
+        const int64_t tiles0 = (int64_t)tiles_n * ((M + BN - 1) / BN);
+        if (tiles0 * 5 < (int64_t)ctx->sm_count * 4)
+            splits = (int)std::min<int64_t>(std::max<int64_t>(1, ctx->sm_count / tiles0), std::max(1, kt_total / 2));
+    } else {
+        double best = 1e300;
+        for (int cand : {128, 64, 32, 16}) {
+            if (cand > mr && (cand >> 1) >= mr) continue;   // no wider than M needs
+            const int64_t tiles = (int64_t)tiles_n * ((M + cand - 1) / cand);
+            for (int sp = 1; sp <= std::max(1, kt_total / 2); sp++) {
+                const int kps = (kt_total + sp - 1) / sp;
+                const int64_t units = tiles * ((kt_total + kps - 1) / kps);
+                const int64_t waves = (units + ctx->sm_count - 1) / ctx->sm_count;
+                const double t = (double)waves * ((double)cand * kps + 2048.0) + (sp > 1 ? 0.02 * sp * cand : 0.0);
+                if (t < best * 0.999) { best = t; BN = cand; splits = sp; }
+                if (units >= 4 * ctx->sm_count) break;
+            }
+        }
     }
     const int tiles_m = (int)((M + BN - 1) / BN);
-    const int kt_total = K / GM_BK;
-    int splits = 1;
     const int tiles = tiles_m * tiles_n;
-    if (tiles * 5 < ctx->sm_count * 4) {
-        splits = std::max(1, ctx->sm_count / tiles);
-        splits = std::min(splits, std::max(1, kt_total / 2));   // at least 2 k-tiles per split
-    }
     const int kt_per_split = (kt_total + splits - 1) / splits;
     splits = (kt_total + kt_per_split - 1) / kt_per_split;
     if (tiles > 65536) return set_error(ctx, VB_ERR_INVALID_ARG, "gemm: too many tiles");
@@ -553,6 +608,7 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
     const size_t smem = (size_t)n_tma * stage + conv_bytes + 1024;
     uint32_t cols = 32;
     while (cols < (uint32_t)BN) cols <<= 1;
+    cols *= 2;   // two accumulators: the epilogue of one tile overlaps the next tile's MMAs
 
     // activation operands
     const size_t ab = (size_t)M * K * 2;
@@ -602,6 +658,7 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
     g.kt_per_split = kt_per_split;
     g.splits = splits;
     g.tiles_m = tiles_m;
+    g.tiles_n = tiles_n;
     g.n_tma = n_tma;
     g.n_conv = n_conv;
     g.tmem_cols = cols;
@@ -622,7 +679,8 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
         if (rc) return rc;
         g.ws = (float *)gs->part.ptr;
     }
-    gemm_kernel<<<(unsigned)(tiles * splits), GM_THREADS, smem, ctx->stream>>>(
+    const int n_work = tiles * splits;
+    gemm_kernel<<<(unsigned)std::min(n_work, ctx->sm_count), GM_THREADS, smem, ctx->stream>>>(
         *reinterpret_cast<const CUtensorMap *>(w->tmap), am->th, am->tl, g);
     VB_LAUNCH_CHECK(ctx, "gemm");
     return VB_OK;
