@@ -25,6 +25,7 @@ namespace vb {
 constexpr int ATT_CH = 64;         // K/V rows per CTA
 constexpr int ATT_WARPS = 8;
 constexpr int ATT_HD_MAX = 256;
+constexpr int ATT_SEG_PAIRS = 16;   // (token, head) pairs per segment-attention CTA
 
 struct AttnArgs {
     const float *q;
@@ -147,6 +148,84 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) attn_chunk_kernel(AttnArgs a) 
     }
 }
 
+// Bidirectional segments of T <= 32 tokens (LocDiT, LocEnc): a CTA per
+// (KV group, segment, 16 (token, query head) pairs of the group) stages the
+// segment's K/V rows once for its pairs, one pair per warp at a time.  Per pair the arithmetic is
+// attn_chunk_kernel's with one chunk (same order of every fp32 operation),
+// so the results are identical while K/V are read once per segment instead
+// of once per token.
+__global__ void __launch_bounds__(ATT_WARPS * 32) attn_segment_kernel(AttnArgs a, int T) {
+    extern __shared__ __align__(16) uint32_t sm[];
+    const int g = blockIdx.x, sgi = blockIdx.y;
+    const int HD = a.head_dim, HW = HD >> 1;
+    const int rw = (HW & 1) ? HW : HW + 1;
+    const int qpk = a.n_heads / a.n_kv;
+    uint32_t *ks = sm;                                          // [T][rw]
+    uint32_t *vs = ks + 32 * rw;                                // [T][rw]
+    float *qs = reinterpret_cast<float *>(vs + 32 * rw);        // [warps][HD]
+    float *es = qs + ATT_WARPS * HD;                            // [warps][32]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t base = ((int64_t)g * a.n_rows + (int64_t)sgi * T) * HW;
+    const uint32_t *kg = reinterpret_cast<const uint32_t *>(a.k) + base;
+    const uint32_t *vg = reinterpret_cast<const uint32_t *>(a.v) + base;
+    for (int i = threadIdx.x; i < T * HW; i += blockDim.x) {
+        const int r = i / HW, w = i % HW;
+        ks[r * rw + w] = __ldg(kg + i);
+        vs[r * rw + w] = __ldg(vg + i);
+    }
+    __syncthreads();
+    float *qv = qs + warp * HD;
+    float *e = es + warp * 32;
+    const int pr_end = min(T * qpk, (int)(blockIdx.z + 1) * ATT_SEG_PAIRS);
+    for (int pr = blockIdx.z * ATT_SEG_PAIRS + warp; pr < pr_end; pr += ATT_WARPS) {
+        const int t = pr / qpk, j = pr % qpk, h = g * qpk + j;
+        const int64_t tok = (int64_t)sgi * T + t;
+        for (int d = lane; d < HD; d += 32) qv[d] = a.q[tok * a.ldq + (int64_t)h * HD + d];
+        __syncwarp();
+        float s = -INFINITY;
+        if (lane < T) {
+            float acc = 0.0f;
+            const uint32_t *kr = ks + lane * rw;
+            for (int w = 0; w < HW; w++) {
+                const uint32_t kk = kr[w];
+                acc = fmaf(__uint_as_float(kk << 16), qv[2 * w], acc);
+                acc = fmaf(__uint_as_float(kk & 0xffff0000u), qv[2 * w + 1], acc);
+            }
+            s = __fmul_rn(acc, a.kq_scale);
+        }
+        const float mx = warp_max(s);
+        const float ev = (lane < T) ? expf(s - mx) : 0.0f;
+        e[lane] = ev;
+        float l = 0.0f;
+        l += ev;
+        l = warp_sum(l);
+        __syncwarp();
+        float o[ATT_HD_MAX / 32];
+#pragma unroll
+        for (int u = 0; u < ATT_HD_MAX / 32; u++) o[u] = 0.0f;
+        for (int p = 0; p < T; p++) {
+            const float ep = e[p];
+            const uint32_t *vr = vs + p * rw;
+#pragma unroll
+            for (int u = 0; u < ATT_HD_MAX / 32; u++) {
+                const int d = lane + 32 * u;
+                if (d < HD) {
+                    const uint32_t vv = vr[d >> 1];
+                    const float vf = __uint_as_float((d & 1) ? (vv & 0xffff0000u) : (vv << 16));
+                    o[u] = fmaf(ep, vf, o[u]);
+                }
+            }
+        }
+        float *dst = a.out + tok * a.ldo + (int64_t)h * HD;
+#pragma unroll
+        for (int u = 0; u < ATT_HD_MAX / 32; u++) {
+            const int d = lane + 32 * u;
+            if (d < HD) dst[d] = __fdiv_rn(o[u], l);
+        }
+        __syncwarp();
+    }
+}
+
 // Merge chunk partials: o = sum_c o_c e^(m_c-m) / sum_c l_c e^(m_c-m).
 __global__ void attn_combine_kernel(AttnArgs a) {
     const int t = blockIdx.x, h = blockIdx.y;
@@ -183,6 +262,34 @@ static size_t attn_smem(int n_heads, int n_kv, int head_dim) {
 
 int init_attention(vb_ctx *ctx) {
     VB_CHECK(ctx, cudaFuncSetAttribute(attn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+    return VB_OK;
+}
+
+int launch_attention_segments(vb_ctx *ctx, const float *q, int64_t ldq, const uint16_t *k, const uint16_t *v,
+                              int n_rows, int n_seg, int T, int n_heads, int n_kv, int head_dim, float *out,
+                              int64_t ldo) {
+    if (n_seg == 0) return VB_OK;
+    if (!q || !k || !v || !out || T <= 0 || T > 32 || n_kv <= 0 || n_heads % n_kv || head_dim % 2 ||
+        head_dim > ATT_HD_MAX)
+        return set_error(ctx, VB_ERR_INVALID_ARG, "segment attention: bad argument");
+    const int HW = head_dim >> 1, rw = (HW & 1) ? HW : HW + 1;
+    const size_t sm = (size_t)2 * 32 * rw * 4 + (size_t)ATT_WARPS * head_dim * 4 + (size_t)ATT_WARPS * 32 * 4;
+    AttnArgs a{};
+    a.q = q;
+    a.ldq = ldq ? ldq : (int64_t)n_heads * head_dim;
+    a.k = k;
+    a.v = v;
+    a.n_rows = n_rows;
+    a.n_heads = n_heads;
+    a.n_kv = n_kv;
+    a.head_dim = head_dim;
+    a.out = out;
+    a.ldo = ldo ? ldo : (int64_t)n_heads * head_dim;
+    a.kq_scale = 1.0f / sqrtf((float)head_dim);
+    const int pairs = T * (n_heads / n_kv);
+    attn_segment_kernel<<<dim3((unsigned)n_kv, (unsigned)n_seg, (unsigned)((pairs + ATT_SEG_PAIRS - 1) / ATT_SEG_PAIRS)),
+                          ATT_WARPS * 32, sm, ctx->stream>>>(a, T);
+    VB_LAUNCH_CHECK(ctx, "attn_segment");
     return VB_OK;
 }
 

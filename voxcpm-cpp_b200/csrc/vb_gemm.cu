@@ -58,6 +58,8 @@ struct GemmArgs {
     float *y;
     const float *bias;
     unsigned flags;
+    const float *res;       // residual epilogue source (rows like y) or null
+    float res_scale;
     int64_t ldy, seg, seg_stride, seg_off;
     int seg_plain;          // output row = activation row
     float *ws;              // split partials [splits][N][Mp]
@@ -124,9 +126,28 @@ __device__ __forceinline__ int64_t gm_out_row(const GemmArgs &a, int m) {
     return (int64_t)(m / sg) * a.seg_stride + a.seg_off + (m % sg);
 }
 
-__device__ __forceinline__ float gm_epilogue(const GemmArgs &a, int n, float v) {
-    if (a.bias) v = __fadd_rn(v, a.bias[n]);
-    return (a.flags & VB_OUT_BF16) ? bf16r(v) : v;
+// Epilogue of 16 outputs (activation rows m0 .. m0+15, weight row n).  The
+// residual rows are all loaded before any store: they may alias y, so
+// interleaving would serialise 16 memory round trips.
+__device__ __forceinline__ void gm_store16(const GemmArgs &a, int m0, int n, const float *acc) {
+    float r[16];
+    if (a.res) {
+#pragma unroll
+        for (int cc = 0; cc < 16; cc++) r[cc] = __ldcg(a.res + gm_out_row(a, min(m0 + cc, a.M - 1)) * a.ldy + n);
+    }
+    const float b = a.bias ? a.bias[n] : 0.0f;
+#pragma unroll
+    for (int cc = 0; cc < 16; cc++) {
+        if (m0 + cc >= a.M) break;
+        float v = acc[cc];
+        if (a.bias) v = __fadd_rn(v, b);
+        if (a.flags & VB_OUT_BF16) v = bf16r(v);
+        if (a.res) {
+            if (a.res_scale != 1.0f) v = __fmul_rn(v, a.res_scale);
+            v = bf16r(__fadd_rn(r[cc], v));
+        }
+        a.y[gm_out_row(a, m0 + cc) * a.ldy + n] = v;
+    }
 }
 
 __global__ void __launch_bounds__(GM_THREADS, 1)
@@ -362,12 +383,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                             pw[q4] = make_float4(__uint_as_float(v[4 * q4]), __uint_as_float(v[4 * q4 + 1]),
                                                  __uint_as_float(v[4 * q4 + 2]), __uint_as_float(v[4 * q4 + 3]));
                     } else {
-#pragma unroll
-                        for (int cc = 0; cc < 16; cc++) {
-                            const int m = m0 + j * 16 + cc;
-                            if (m >= a.M) break;
-                            a.y[gm_out_row(a, m) * a.ldy + n] = gm_epilogue(a, n, __uint_as_float(v[cc]));
-                        }
+                        gm_store16(a, m0 + j * 16, n, reinterpret_cast<const float *>(v));
                     }
                 }
             }
@@ -389,7 +405,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 }
                 asm volatile("bar.sync 2, %0;" ::"r"(GM_EPI_THREADS) : "memory");
                 if (s_last && n < a.N) {
-                    // 16 columns x 4 splits (16 vector loads) in flight at a
+                    // 16 columns x 2 splits (8 vector loads) in flight at a
                     // time; the sums still run in split order
 #pragma unroll 1
                     for (int j = 0; j * 16 < BN; j++) {
@@ -397,10 +413,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 #pragma unroll
                         for (int q4 = 0; q4 < 4; q4++) acc[q4] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
-                        for (int s0 = 0; s0 < a.splits; s0 += 4) {
-                            float4 vv[4][4];
+                        for (int s0 = 0; s0 < a.splits; s0 += 2) {
+                            float4 vv[2][4];
 #pragma unroll
-                            for (int u = 0; u < 4; u++) {
+                            for (int u = 0; u < 2; u++) {
                                 const float4 *pr = reinterpret_cast<const float4 *>(
                                     a.ws + ((int64_t)(s0 + u) * a.N + n) * a.Mp + m0 + j * 16);
 #pragma unroll
@@ -408,7 +424,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                                     vv[u][q4] = s0 + u < a.splits ? __ldcg(pr + q4) : make_float4(0.f, 0.f, 0.f, 0.f);
                             }
 #pragma unroll
-                            for (int u = 0; u < 4; u++)
+                            for (int u = 0; u < 2; u++)
                                 if (s0 + u < a.splits)
 #pragma unroll
                                     for (int q4 = 0; q4 < 4; q4++) {
@@ -418,12 +434,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                                         acc[q4].w = __fadd_rn(acc[q4].w, vv[u][q4].w);
                                     }
                         }
-                        const float *af = reinterpret_cast<const float *>(acc);
-#pragma unroll
-                        for (int cc = 0; cc < 16; cc++) {
-                            const int m = m0 + j * 16 + cc;
-                            if (m < a.M) a.y[gm_out_row(a, m) * a.ldy + n] = gm_epilogue(a, n, af[cc]);
-                        }
+                        gm_store16(a, m0 + j * 16, n, reinterpret_cast<const float *>(acc));
                     }
                 }
                 asm volatile("bar.sync 2, %0;" ::"r"(GM_EPI_THREADS) : "memory");   // s_last reused next tile
@@ -440,26 +451,68 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 
 // Activation operand(s): Q8_0 -> (hi, lo) fp16 of the dequantised block
 // values (quantisation bit-exact with the GEMV path's, rule `rule`); F16 ->
-// fp16(x).  One warp per 32-value block; row m reads x row (m % x_mod).
-__global__ void gemm_act_kernel(const float *x, int64_t ldx, int64_t x_mod, int M, int K, int q8, int rule,
+// fp16(x).  One thread per 8 values, four threads per 32-value block (the
+// block maximum is a two-step shuffle); row m reads x row (m % x_mod).
+// vec: x rows are 16-byte aligned (float4 loads).
+__global__ void gemm_act_kernel(const float *x, int64_t ldx, int64_t x_mod, int M, int K, int q8, int rule, int vec,
                                 __half *bh, __half *bl) {
-    const int64_t blk = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31, nb = K >> 5;
-    if (blk >= (int64_t)M * nb) return;
-    const int m = (int)(blk / nb), b = (int)(blk % nb);
-    const float v = x[(int64_t)(m % x_mod) * ldx + b * 32 + lane];
-    const int64_t o = (int64_t)m * K + b * 32 + lane;
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // item of 8 values
+    const int ipr = K >> 3;
+    const bool valid = e < (int64_t)M * ipr;
+    const int m = valid ? (int)(e / ipr) : 0, k0 = valid ? (int)(e - (int64_t)m * ipr) * 8 : 0;
+    const float *xr = x + (int64_t)(m % x_mod) * ldx + k0;
+    float v[8];
+    if (vec) {
+        const float4 a0 = *reinterpret_cast<const float4 *>(xr), a1 = *reinterpret_cast<const float4 *>(xr + 4);
+        v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w; v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = xr[j];
+    }
+    const int64_t o = (int64_t)m * K + k0;
     if (!q8) {
-        bh[o] = __float2half_rn(v);
+        if (valid) {
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                w[j] = (uint32_t)__half_as_ushort(__float2half_rn(v[2 * j])) |
+                       ((uint32_t)__half_as_ushort(__float2half_rn(v[2 * j + 1])) << 16);
+            *reinterpret_cast<uint4 *>(bh + o) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
         return;
     }
-    int q;
-    uint16_t dh;
-    q8_quant_warp(v, rule, q, dh);
-    const float dv = __fmul_rn(h2f(dh), (float)q);
-    const __half h = __float2half_rn(dv);
-    bh[o] = h;
-    bl[o] = __float2half_rn(__fsub_rn(dv, __half2float(h)));
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) amax = fmaxf(amax, fabsf(v[j]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const uint16_t dh = f2h(d);
+    const bool x86 = rule == VB_QRULE_X86;
+    float id;
+    if (x86) id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
+    else id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float df = h2f(dh);
+    uint32_t wh[4], wl[4];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float t = __fmul_rn(v[j], id);
+        const int q = x86 ? __float2int_rn(t) : (int)roundf(t);
+        const float dv = __fmul_rn(df, (float)q);
+        const __half h = __float2half_rn(dv);
+        const __half l = __float2half_rn(__fsub_rn(dv, __half2float(h)));
+        if (j & 1) {
+            wh[j >> 1] |= (uint32_t)__half_as_ushort(h) << 16;
+            wl[j >> 1] |= (uint32_t)__half_as_ushort(l) << 16;
+        } else {
+            wh[j >> 1] = __half_as_ushort(h);
+            wl[j >> 1] = __half_as_ushort(l);
+        }
+    }
+    if (valid) {
+        *reinterpret_cast<uint4 *>(bh + o) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+        *reinterpret_cast<uint4 *>(bl + o) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+    }
 }
 
 // ------------------------------------------------------------------ host
@@ -617,10 +670,11 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
     __half *bh = (__half *)gs->act.ptr;
     __half *bl = (__half *)((uint8_t *)gs->act.ptr + ((ab + 255) & ~(size_t)255));
     {
-        const int64_t blocks = M * (K / 32);
-        const int wpb = 8;
-        gemm_act_kernel<<<(unsigned)((blocks + wpb - 1) / wpb), wpb * 32, 0, ctx->stream>>>(
-            x, ldx ? ldx : K, x_mod > 0 ? x_mod : M, (int)M, K, q8 ? 1 : 0, ctx->qrule, bh, bl);
+        const int64_t items = M * (K / 8);
+        const int64_t lx = ldx ? ldx : K;
+        const int vec = ((uintptr_t)x % 16 == 0) && (lx % 4 == 0);
+        gemm_act_kernel<<<(unsigned)((items + 255) / 256), 256, 0, ctx->stream>>>(
+            x, lx, x_mod > 0 ? x_mod : M, (int)M, K, q8 ? 1 : 0, ctx->qrule, vec, bh, bl);
         VB_LAUNCH_CHECK(ctx, "gemm_act");
     }
     // descriptors: the weight's once per weight, the activations' per shape
@@ -666,6 +720,8 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
     g.y = out.y;
     g.bias = out.bias;
     g.flags = out.flags;
+    g.res = out.res;
+    g.res_scale = out.res_scale;
     g.ldy = out.ldy ? out.ldy : N;
     g.seg = out.seg ? out.seg : M;
     g.seg_stride = out.seg ? out.seg_stride : 0;

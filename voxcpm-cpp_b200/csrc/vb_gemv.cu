@@ -35,6 +35,10 @@ __device__ __forceinline__ void gemv_store(const MatmulOut &o, int64_t m, int64_
     if (o.bias) v = __fadd_rn(v, o.bias[n]);
     if (o.flags & VB_OUT_BF16) v = bf16r(v);
     int64_t row = (m / o.seg) * o.seg_stride + o.seg_off + (m % o.seg);
+    if (o.res) {
+        if (o.res_scale != 1.0f) v = __fmul_rn(v, o.res_scale);
+        v = bf16r(__fadd_rn(o.res[row * o.ldy + n], v));
+    }
     o.y[row * o.ldy + n] = v;
 }
 

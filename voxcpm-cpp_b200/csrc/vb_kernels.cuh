@@ -20,6 +20,11 @@ struct MatmulOut {
     unsigned flags = 0;            // VB_OUT_BF16
     int64_t ldy = 0;
     int64_t seg = 0, seg_stride = 0, seg_off = 0;
+    // residual epilogue: y = bf16(res + res_scale * value), value after bias
+    // and the bf16 flag (block residual, src/minicpm4.c:496-528); res rows
+    // follow y's mapping and may alias y
+    const float *res = nullptr;
+    float res_scale = 1.0f;
 };
 
 // Input mapping: logical row m reads x row (m % x_mod) (x_mod = M: plain),
@@ -53,6 +58,12 @@ int launch_kv_write(vb_ctx *ctx, const float *k, const float *v, int64_t ldkv, u
 int launch_fill(vb_ctx *ctx, float *x, float v, int64_t n);
 
 // attention (vb_attn.cu)
+// Bidirectional attention over n_seg uniform segments of T <= 32 tokens
+// (token t of segment s attends to K/V rows s*T .. s*T+T-1): one CTA per
+// (segment, KV group) stages the segment's K/V once for all its tokens.
+int launch_attention_segments(vb_ctx *ctx, const float *q, int64_t ldq, const uint16_t *k, const uint16_t *v,
+                              int n_rows, int n_seg, int T, int n_heads, int n_kv, int head_dim, float *out,
+                              int64_t ldo);
 int launch_attention(vb_ctx *ctx, const float *q, int64_t ldq, const uint16_t *k, const uint16_t *v, int n_rows,
                      int T, int n_heads, int n_kv, int head_dim, const int32_t *row_start, const int32_t *kv_len,
                      int max_kv_len, float *out, int64_t ldo);

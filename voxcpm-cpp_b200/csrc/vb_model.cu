@@ -308,6 +308,7 @@ namespace vb {
 struct TokenTables {
     int32_t *pos, *dst, *start, *len;
     int max_len;
+    int seg_T = 0;   // > 0: bidirectional, uniform segments of seg_T tokens (K/V rows = token rows)
 };
 
 // The layer loop shared by causal and bidirectional stacks.  h: [M][H]
@@ -332,6 +333,7 @@ static int run_layers(vb_ctx *ctx, vb_lm *lm, int M, float *h, const TokenTables
         cs = rt->d_cs;
     }
     int rc;
+    const bool dumping = getenv("VB_DUMP_DIR") && getenv("VB_DUMP_DIR")[0];
     for (int l = 0; l < c.n_layers; l++) {
         LayerDev &L = lm->layers[l];
         uint16_t *kc = kc_base + (size_t)l * kv_layer_elems;
@@ -352,14 +354,25 @@ static int run_layers(vb_ctx *ctx, vb_lm *lm, int M, float *h, const TokenTables
         if ((rc = launch_kv_write(ctx, qkv + QD, qkv + QD + KD, QKV, kc, vc, kv_rows, M, c.n_kv_heads, c.head_dim,
                                   tt.dst)))
             return rc;
-        if ((rc = launch_attention(ctx, qkv, QKV, kc, vc, kv_rows, M, c.n_heads, c.n_kv_heads, c.head_dim, tt.start,
-                                   tt.len, tt.max_len, att, QD)))
+        if (tt.seg_T > 0 && tt.seg_T <= 32) {
+            if ((rc = launch_attention_segments(ctx, qkv, QKV, kc, vc, kv_rows, M / tt.seg_T, tt.seg_T, c.n_heads,
+                                                c.n_kv_heads, c.head_dim, att, QD)))
+                return rc;
+        } else if ((rc = launch_attention(ctx, qkv, QKV, kc, vc, kv_rows, M, c.n_heads, c.n_kv_heads, c.head_dim,
+                                          tt.start, tt.len, tt.max_len, att, QD))) {
             return rc;
+        }
         dumpf(ctx, att, QD, M, "L%d.att", l);
-        o.y = a;
+        // residual add fused into the projection's epilogue, except when the
+        // projection itself is dumped
+        const bool fuse_res = !dumping;
+        o.y = fuse_res ? h : a;
+        o.res = fuse_res ? h : nullptr;
+        o.res_scale = scale;
         if ((rc = launch_matmul(ctx, L.o, att, M, 0, 0, o))) return rc;
+        o.res = nullptr;
         dumpf(ctx, a, H, M, "L%d.o", l);
-        if ((rc = launch_residual(ctx, h, a, scale, h, (int64_t)M * H, VB_OUT_BF16))) return rc;
+        if (!fuse_res && (rc = launch_residual(ctx, h, a, scale, h, (int64_t)M * H, VB_OUT_BF16))) return rc;
         dumpf(ctx, h, H, M, "L%d.h_attn", l);
         if ((rc = launch_rms_norm(ctx, h, L.ffn_norm, xn, H, M, c.eps, VB_OUT_BF16))) return rc;
         dumpf(ctx, xn, H, M, "L%d.ffn_norm", l);
@@ -370,10 +383,13 @@ static int run_layers(vb_ctx *ctx, vb_lm *lm, int M, float *h, const TokenTables
         swiglu_rows_kernel<<<(unsigned)((ne + 255) / 256), 256, 0, ctx->stream>>>(gu, act, M, c.ffn);
         VB_LAUNCH_CHECK(ctx, "swiglu_rows");
         dumpf(ctx, act, c.ffn, M, "L%d.act", l);
-        o.y = a;
+        o.y = fuse_res ? h : a;
+        o.res = fuse_res ? h : nullptr;
+        o.res_scale = scale;
         if ((rc = launch_matmul(ctx, L.down, act, M, 0, 0, o))) return rc;
+        o.res = nullptr;
         dumpf(ctx, a, H, M, "L%d.down", l);
-        if ((rc = launch_residual(ctx, h, a, scale, h, (int64_t)M * H, VB_OUT_BF16))) return rc;
+        if (!fuse_res && (rc = launch_residual(ctx, h, a, scale, h, (int64_t)M * H, VB_OUT_BF16))) return rc;
         dumpf(ctx, h, H, M, "L%d.out", l);
     }
     return VB_OK;
@@ -475,6 +491,7 @@ extern "C" int vb_lm_forward_noncausal(vb_ctx *ctx, vb_lm *lm, int n, int T, flo
     TokenTables tt;
     if ((rc = upload_tables(ctx, cv, M, tab, tt))) return rc;
     tt.max_len = T;
+    tt.seg_T = T;
     uint16_t *kc = cv.take<uint16_t>(kv_elems);
     uint16_t *vc = cv.take<uint16_t>(kv_elems);
     return run_layers(ctx, lm, M, h, tt, kc, vc, 0, M, cv);
@@ -930,6 +947,7 @@ static int dit_forward_impl(vb_ctx *ctx, vb_dit *d, int n, const float *x, const
         TokenTables tt;
         if ((rc = upload_tables(ctx, inner, M2, tab, tt))) return rc;
         tt.max_len = (int)T;
+        tt.seg_T = (int)T;
         const size_t kv_elems = (size_t)lc.n_kv_heads * M2 * lc.head_dim;
         uint16_t *kc = inner.take<uint16_t>(kv_elems);
         uint16_t *vc = inner.take<uint16_t>(kv_elems);
