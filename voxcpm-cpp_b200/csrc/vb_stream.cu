@@ -31,25 +31,27 @@
 namespace vb {
 
 __global__ void __launch_bounds__(ST_THREADS, 1)
-    stream_gemv_kernel(const StreamOp *__restrict__ ops, const int2 *__restrict__ rows, int n_ops, unsigned *bars, int *err,
-                       const StreamStep step) {
+    stream_gemv_kernel(const StreamOp *__restrict__ ops, const int2 *__restrict__ rows,
+                       const uint16_t *__restrict__ idx, const int *__restrict__ counts, int n_ops, unsigned *bars,
+                       int *err, const StreamStep step, const int ns) {
     extern __shared__ __align__(128) uint8_t sm[];
     uint8_t *wslot = sm;
-    uint8_t *sslot = wslot + (size_t)ST_STAGES * ST_SLOT;
-    int8_t *xq = reinterpret_cast<int8_t *>(sslot + (size_t)ST_STAGES * ST_SC_SLOT);
+    uint8_t *sslot = wslot + (size_t)ns * ST_SLOT;
+    int8_t *xq = reinterpret_cast<int8_t *>(sslot + (size_t)ns * ST_SC_SLOT);
     float *xd = reinterpret_cast<float *>(xq + ST_XBYTES);
     uint64_t *full = reinterpret_cast<uint64_t *>(xd + ST_XBYTES / 32);
-    uint64_t *empty = full + ST_STAGES;
-    uint8_t *aux = sm + ST_SMEM;                     // non-GEMV op scratch
+    uint64_t *empty = full + ST_STAGES_MAX;
+    uint8_t *aux = sm + st_smem(ns, false);          // non-GEMV op scratch (aux programs only)
     __shared__ volatile int s_abort;
     __shared__ int s_step[ST_MMAX * 4];
     __shared__ StreamOp s_ops[2];
-    __shared__ int2 s_rows[ST_MAX_OPS];   // this CTA's rows [x, y) of every op
+    __shared__ int2 s_rows[ST_MAX_OPS];        // rows [x, y) of this CTA's k-th op
+    __shared__ uint16_t s_idx[ST_MAX_OPS];     // program index of this CTA's k-th op
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, cta = blockIdx.x;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < ST_STAGES; s++) {
+        for (int s = 0; s < ns; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], ST_CONSUMER_WARPS);
         }
@@ -60,7 +62,13 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
 #pragma unroll
     for (int i = 0; i < ST_MMAX * 4; i++)
         if (threadIdx.x == i) s_step[i] = step.v[i / 4][i % 4];
-    for (int i = threadIdx.x; i < n_ops; i += ST_THREADS) s_rows[i] = rows[(int64_t)blockIdx.x * n_ops + i];
+    // This CTA's op list: the ops it streams rows of, every non-GEMV op and
+    // every group's last op (its barrier arrival); see stream_program_build.
+    const int n_list = counts[cta];
+    for (int k = threadIdx.x; k < n_list; k += ST_THREADS) {
+        s_rows[k] = rows[(int64_t)cta * n_ops + k];
+        s_idx[k] = idx[(int64_t)cta * n_ops + k];
+    }
     __syncthreads();
 
     // ------------------------------------------------------------ producer
@@ -69,12 +77,13 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
         int slot = 0;
         uint32_t phase = 0;
         long long fills = 0;
-        for (int i = 0; i < n_ops && !s_abort; i++) {
-            const StreamOp &op = ops[i];
+        for (int k = 0; k < n_list && !s_abort; k++) {
+            const StreamOp &op = ops[s_idx[k]];
             if (op.kind == OPK_ATTN) attn_prefetch(op, s_step, cta, G);
             if (op.kind != OPK_GEMV) continue;       // no weights to stream
+            const int64_t r0 = s_rows[k].x, r1 = s_rows[k].y;
+            if (r1 <= r0) continue;
             if (op.pro == PRO_RMSNORM && (op.K % 4) == 0) prefetch_l2(op.pro_w, (uint32_t)op.K * 4u);
-            const int64_t r0 = s_rows[i].x, r1 = s_rows[i].y;
             const int R = op.rows_per_chunk;
             const int nb = op.K / QK;
             const bool swz = op.epi == EPI_SWIGLU;
@@ -103,13 +112,13 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                     if (sb) bulk_g2s(sdst, op.sc + r * nb, sb, &full[slot]);
                 }
                 fills++;
-                if (++slot == ST_STAGES) { slot = 0; phase ^= 1u; }
+                if (++slot == ns) { slot = 0; phase ^= 1u; }
             }
         }
         // Drain: the last fill of every stage must have landed before this
         // thread exits (normally the consumers have already seen it).
-        for (int s = 0; s < ST_STAGES; s++) {
-            const long long n_s = fills / ST_STAGES + ((fills % ST_STAGES) > s ? 1 : 0);
+        for (int s = 0; s < ns; s++) {
+            const long long n_s = fills / ns + ((fills % ns) > s ? 1 : 0);
             if (n_s == 0) continue;
             const uint32_t par = (uint32_t)((n_s - 1) & 1);
             const long long t0 = clock64();
@@ -121,12 +130,14 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     }
 
     // ----------------------------------------------------------- consumers
-    // The descriptor of op i lives in s_ops[i & 1]; op i+1's is fetched with
-    // cp.async while op i runs, so no field read waits on global memory.
+    // The descriptor of list entry k lives in s_ops[k & 1]; entry k+1's is
+    // fetched with cp.async while entry k runs, so no field read waits on
+    // global memory.
     constexpr int OPW = (int)(sizeof(StreamOp) / 16);
     static_assert(sizeof(StreamOp) % 16 == 0 && OPW <= ST_CONSUMERS, "descriptor copy");
     const int ctid = threadIdx.x - 32, cw = warp - 1;
-    if (ctid < OPW) cp_async16(reinterpret_cast<int4 *>(&s_ops[0]) + ctid, reinterpret_cast<const int4 *>(ops) + ctid);
+    if (ctid < OPW && n_list > 0)
+        cp_async16(reinterpret_cast<int4 *>(&s_ops[0]) + ctid, reinterpret_cast<const int4 *>(ops + s_idx[0]) + ctid);
     cp_async_wait_all();
     consumer_sync(ST_CONSUMERS);
     int slot = 0;
@@ -136,11 +147,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     bool bad = false;   // this thread saw a timeout or an abort
     // Every consumer_sync / consumer_sync_or below is executed by all
     // consumer warps in the same order; loops end only on a uniform flag.
-    for (int i = 0; i < n_ops; i++) {
-        const StreamOp &op = s_ops[i & 1];
-        if (i + 1 < n_ops && ctid < OPW)
-            cp_async16(reinterpret_cast<int4 *>(&s_ops[(i + 1) & 1]) + ctid,
-                       reinterpret_cast<const int4 *>(ops + i + 1) + ctid);
+    for (int k = 0; k < n_list; k++) {
+        const StreamOp &op = s_ops[k & 1];
+        const int i = s_idx[k];
+        if (k + 1 < n_list && ctid < OPW)
+            cp_async16(reinterpret_cast<int4 *>(&s_ops[(k + 1) & 1]) + ctid,
+                       reinterpret_cast<const int4 *>(ops + s_idx[k + 1]) + ctid);
         if (op.wait_group > waited) {
             if (ctid == 0 && !wait_grid(bars + op.wait_group, (unsigned)G, &s_abort)) {
                 if (!s_abort) { atomicCAS(err, 0, STREAM_TIMEOUT_GRID); s_abort = 1; }
@@ -156,7 +168,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             stream_norm(op, reinterpret_cast<float *>(aux), cta, G, ctid, cw, lane);
         } else {
             const int K = op.K, M = op.M, nb = K / QK;
-            const int64_t r0 = s_rows[i].x, r1 = s_rows[i].y;
+            const int64_t r0 = s_rows[k].x, r1 = s_rows[k].y;
             // The previous op ended with a consumer barrier, so no warp still
             // reads the activation buffers when they are rewritten here.
             if (r1 > r0) {
@@ -172,11 +184,11 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                 bool ok = true;
                 fast_done = true;
                 switch (K) {
-                    case 1024: ok = q8_m1_op<16, 4>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err); break;
-                    case 2048: ok = q8_m1_op<16, 8>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err); break;
-                    case 4096: ok = q8_m1_op<16, 16>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err); break;
-                    case 6144: ok = q8_m1_op<32, 12>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err); break;
-                    case 8192: ok = q8_m1_op<32, 16>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err); break;
+                    case 1024: ok = q8_m1_op<16, 4>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns); break;
+                    case 2048: ok = q8_m1_op<16, 8>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns); break;
+                    case 4096: ok = q8_m1_op<16, 16>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns); break;
+                    case 6144: ok = q8_m1_op<32, 12>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns); break;
+                    case 8192: ok = q8_m1_op<32, 16>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns); break;
                     default: fast_done = false; break;
                 }
                 if (!ok) bad = true;
@@ -218,14 +230,14 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[slot]);
-                if (++slot == ST_STAGES) { slot = 0; phase ^= 1u; }
+                if (++slot == ns) { slot = 0; phase ^= 1u; }
             }
         }
         // Read what the arrival needs before the barrier: after it the
         // other threads may already overwrite this descriptor's buffer.
         const bool arrive = op.last_in_group;
         const int grp = op.group;
-        cp_async_wait_all();    // op i+1's descriptor has landed
+        cp_async_wait_all();    // the next entry's descriptor has landed
         if (consumer_sync_or(bad, ST_CONSUMERS)) break;
         if (arrive && ctid == 0) red_release_gpu(bars + grp, 1u);
     }
@@ -254,10 +266,14 @@ int stream_gemv_geometry(vb_ctx *ctx, StreamOp &s, int i) {
 
 struct vb_program_s {
     StreamOp *d_ops = nullptr;
-    int2 *d_rows = nullptr;       // [grid][n_ops] row ranges
+    int2 *d_rows = nullptr;       // [grid][n_ops] row ranges of each CTA's op list
+    uint16_t *d_idx = nullptr;    // [grid][n_ops] program indices of each CTA's op list
+    int *d_counts = nullptr;      // [grid] op-list lengths
     unsigned *d_bars = nullptr;   // n_groups barriers, then n_counters counters
     int *d_err = nullptr;
     int n_ops = 0, n_groups = 0, n_counters = 0, grid = 0;
+    int stages = 0;               // ring depth of this program's launches
+    size_t smem = 0;              // dynamic shared memory per CTA
     size_t weight_bytes = 0;
 };
 
@@ -273,9 +289,18 @@ int stream_program_build(vb_ctx *ctx, std::vector<StreamOp> ops, int n_groups, i
     for (const StreamOp &op : ops)
         if (op.kind == OPK_ATTN && reinterpret_cast<size_t>(op.cnt) + (size_t)op.M * op.n_heads > (size_t)n_counters)
             return set_error(ctx, VB_ERR_INVALID_ARG, "stream program: attention counters out of range");
+    // Grid waits as a running maximum: a CTA waits before an op exactly when
+    // its wait_group exceeds every earlier one, and a wait for group g
+    // implies all groups below g (every CTA arrives on g after its earlier
+    // groups).  With the maximum in every op, a CTA that skips ops it has
+    // no rows of still makes each wait before its next op.
+    int run = -1;
+    for (StreamOp &op : ops) {
+        run = op.wait_group > run ? op.wait_group : run;
+        op.wait_group = run;
+    }
     // An op reuses the quantized operand of the op before it when both read
-    // the same activation the same way and no grid wait separates them
-    // (the device waits exactly when wait_group exceeds every earlier one).
+    // the same activation the same way and no grid wait separates them.
     int waited = -1;
     for (size_t i = 0; i < ops.size(); i++) {
         const bool waits = ops[i].wait_group > waited;
@@ -298,29 +323,50 @@ int stream_program_build(vb_ctx *ctx, std::vector<StreamOp> ops, int n_groups, i
     }
     if ((int)ops.size() > ST_MAX_OPS)
         return set_error(ctx, VB_ERR_INVALID_ARG, "stream program: more than %d ops", ST_MAX_OPS);
+    // Each CTA walks only its own op list: the GEMV ops it has rows of,
+    // every attention / norm op (all CTAs share those) and the last op of
+    // every group (the CTA's arrival on the group's barrier).  A CTA of a
+    // wide program then touches a few descriptors instead of all of them.
     const int G = ctx->sm_count;
-    std::vector<int2> rows((size_t)G * ops.size(), make_int2(0, 0));
+    const size_t n = ops.size();
+    std::vector<int2> rows((size_t)G * n, make_int2(0, 0));
+    std::vector<uint16_t> idx((size_t)G * n, 0);
+    std::vector<int> counts(G, 0);
     for (int c = 0; c < G; c++)
-        for (size_t i = 0; i < ops.size(); i++) {
-            if (ops[i].kind != OPK_GEMV) continue;
-            int64_t r0, r1;
-            op_rows_host(ops[i], c, G, r0, r1);
-            rows[(size_t)c * ops.size() + i] = make_int2((int)r0, (int)r1);
+        for (size_t i = 0; i < n; i++) {
+            int64_t r0 = 0, r1 = 0;
+            if (ops[i].kind == OPK_GEMV) op_rows_host(ops[i], c, G, r0, r1);
+            if (ops[i].kind == OPK_GEMV && r1 <= r0 && !ops[i].last_in_group) continue;
+            const size_t at = (size_t)c * n + counts[c]++;
+            rows[at] = make_int2((int)r0, (int)r1);
+            idx[at] = (uint16_t)i;
         }
+    // Programs of plain GEMV ops (no attention / norm op, no RMSNorm
+    // prologue) need no aux scratch and run a deeper ring.
+    bool aux = false;
+    for (const StreamOp &op : ops) aux = aux || op.kind != OPK_GEMV || op.pro == PRO_RMSNORM;
+    const int stages = aux ? ST_STAGES_AUX : ST_STAGES_MAX;
+    const size_t smem = st_smem(stages, aux);
     int per_sm = 0;
-    VB_CHECK(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stream_gemv_kernel, ST_THREADS, ST_SMEM_ALL));
+    VB_CHECK(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stream_gemv_kernel, ST_THREADS, smem));
     if (per_sm < 1) return set_error(ctx, VB_ERR_BACKEND, "streaming kernel does not fit on an SM");
     vb_program p = new vb_program_s();
     p->n_ops = (int)ops.size();
     p->n_groups = n_groups;
     p->n_counters = n_counters;
     p->grid = ctx->sm_count;
+    p->stages = stages;
+    p->smem = smem;
     p->weight_bytes = weight_bytes;
     cudaError_t e = cudaMalloc(&p->d_ops, sizeof(StreamOp) * ops.size());
     if (e == cudaSuccess) e = cudaMalloc(&p->d_bars, sizeof(unsigned) * (size_t)(n_groups + n_counters));
     if (e == cudaSuccess) e = cudaMalloc(&p->d_err, sizeof(int));
     if (e == cudaSuccess) e = cudaMalloc(&p->d_rows, sizeof(int2) * rows.size());
     if (e == cudaSuccess) e = cudaMemcpy(p->d_rows, rows.data(), sizeof(int2) * rows.size(), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_idx, sizeof(uint16_t) * idx.size());
+    if (e == cudaSuccess) e = cudaMemcpy(p->d_idx, idx.data(), sizeof(uint16_t) * idx.size(), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMalloc(&p->d_counts, sizeof(int) * counts.size());
+    if (e == cudaSuccess) e = cudaMemcpy(p->d_counts, counts.data(), sizeof(int) * counts.size(), cudaMemcpyHostToDevice);
     for (StreamOp &op : ops)
         if (op.kind == OPK_ATTN && p->d_bars) op.cnt = p->d_bars + n_groups + reinterpret_cast<size_t>(op.cnt);
     if (e == cudaSuccess) e = cudaMemcpy(p->d_ops, ops.data(), sizeof(StreamOp) * ops.size(), cudaMemcpyHostToDevice);
@@ -338,7 +384,7 @@ int stream_program_launch(vb_ctx *ctx, vb_program p, const StreamStep &step) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p->grid);
     cfg.blockDim = dim3(ST_THREADS);
-    cfg.dynamicSmemBytes = ST_SMEM_ALL;
+    cfg.dynamicSmemBytes = p->smem;
     cfg.stream = ctx->stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeCooperative;
@@ -346,7 +392,8 @@ int stream_program_launch(vb_ctx *ctx, vb_program p, const StreamStep &step) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     VB_CHECK(ctx, cudaLaunchKernelEx(&cfg, stream_gemv_kernel, (const StreamOp *)p->d_ops, (const int2 *)p->d_rows,
-                                     p->n_ops, p->d_bars, p->d_err, step));
+                                     (const uint16_t *)p->d_idx, (const int *)p->d_counts, p->n_ops, p->d_bars,
+                                     p->d_err, step, p->stages));
     VB_LAUNCH_CHECK(ctx, "stream_gemv");
     return VB_OK;
 }
@@ -418,6 +465,8 @@ extern "C" void vb_program_destroy(vb_program p) {
     if (!p) return;
     cudaFree(p->d_ops);
     cudaFree(p->d_rows);
+    cudaFree(p->d_idx);
+    cudaFree(p->d_counts);
     cudaFree(p->d_bars);
     cudaFree(p->d_err);
     delete p;

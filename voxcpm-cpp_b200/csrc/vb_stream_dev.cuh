@@ -192,7 +192,7 @@ template <int LPR, int IT>
 __device__ __forceinline__ bool q8_m1_op(const StreamOp &op, const uint8_t *wslot, const uint8_t *sslot,
                                          const int8_t *xq, const float *xd, uint64_t *full, uint64_t *empty,
                                          int &slot, uint32_t &phase, int64_t r0, int64_t r1, int cw, int lane,
-                                         volatile int *abort_flag, int *err) {
+                                         volatile int *abort_flag, int *err, int ns) {
     constexpr int RPW = 32 / LPR;                       // rows per warp per pass
     constexpr int RPP = RPW * ST_CONSUMER_WARPS;        // rows per pass of all warps
     const int K = op.K, nb = K >> 5;
@@ -256,7 +256,7 @@ __device__ __forceinline__ bool q8_m1_op(const StreamOp &op, const uint8_t *wslo
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
-        if (++slot == ST_STAGES) { slot = 0; phase ^= 1u; }
+        if (++slot == ns) { slot = 0; phase ^= 1u; }
     }
     return true;
 }

@@ -62,7 +62,8 @@ struct alignas(16) StreamOp {
     unsigned *cnt;          // [M][n_heads] finished chunks (zeroed before each run)
 };
 
-constexpr int ST_STAGES = 5;
+constexpr int ST_STAGES_MAX = 6;                // ring depth of GEMV-only programs
+constexpr int ST_STAGES_AUX = 5;                // ring depth when ops need the aux scratch
 constexpr int ST_SLOT = 32768;                  // weight bytes per ring stage
 constexpr int ST_SC_SLOT = ST_SLOT / 16;        // Q8_0 scale bytes per stage
 constexpr int ST_CONSUMER_WARPS = 8;
@@ -70,14 +71,23 @@ constexpr int ST_CONSUMERS = ST_CONSUMER_WARPS * 32;
 constexpr int ST_THREADS = ST_CONSUMERS + 32;
 constexpr int ST_XBYTES = 16384;                // activation operand (int8 or fp16)
 constexpr int ST_MMAX = 8;
-constexpr int ST_MAX_OPS = 1024;                // ops per program (row table in shared memory)
-constexpr size_t ST_SMEM = (size_t)ST_STAGES * ST_SLOT + (size_t)ST_STAGES * ST_SC_SLOT + ST_XBYTES +
-                           (ST_XBYTES / 32) * 4 + 2 * ST_STAGES * 8 + 64;
+constexpr int ST_MAX_OPS = 384;                 // ops per program (row table in shared memory)
 
 // Scratch of the non-GEMV ops (attention chunk staging, row statistics).
 constexpr int ST_ATT_ROWS = 32;                  // K/V rows per attention item
 constexpr int ST_AUX_BYTES = 26624;
-constexpr size_t ST_SMEM_ALL = ST_SMEM + ST_AUX_BYTES;
+
+// Dynamic shared memory of a launch with `ns` ring stages: weight slots,
+// scale slots, the activation operand, the mbarriers, then (if the program
+// has attention / norm ops or RMSNorm prologues) the aux scratch.  Programs
+// without aux use the freed bytes for a sixth stage (more bytes in flight).
+constexpr size_t st_smem(int ns, bool aux) {
+    return (size_t)ns * ST_SLOT + (size_t)ns * ST_SC_SLOT + ST_XBYTES + (ST_XBYTES / 32) * 4 +
+           2 * ST_STAGES_MAX * 8 + 64 + (aux ? ST_AUX_BYTES : 0);
+}
+constexpr size_t ST_SMEM_ALL = st_smem(ST_STAGES_MAX, false) > st_smem(ST_STAGES_AUX, true)
+                                   ? st_smem(ST_STAGES_MAX, false)
+                                   : st_smem(ST_STAGES_AUX, true);
 
 // Per-launch row parameters of a decode step (kernel argument, so a step
 // needs no host-to-device copy): rope position, KV write row, first visible
