@@ -89,6 +89,8 @@ class ClockSampler:
         self.t = None
 
     def start(self):
+        """Starts sampling and returns once the first sample has arrived, so
+        that the samples taken during the caller's timed region are kept."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -97,12 +99,19 @@ class ClockSampler:
             self.t.start()
         except (OSError, ValueError):
             self.proc = None
+            return
+        deadline = time.time() + 5.0
+        while not self.lines and time.time() < deadline and self.proc.poll() is None:
+            time.sleep(0.005)
+        self.t0 = time.time()
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
 
     def stop(self):
+        t1 = time.time()
+        time.sleep(0.03)        # a sample taken just before t1 may still be in the pipe
         if self.proc:
             self.proc.terminate()
             try:
@@ -111,9 +120,13 @@ class ClockSampler:
                 self.proc.kill()
             if self.t:
                 self.t.join(timeout=2)
+        t0 = getattr(self, "t0", 0.0)
+        inside = [l for ts, l in self.lines if t0 <= ts <= t1 + 0.03]
+        if not inside:      # region shorter than the sampling period: the first sample after it began
+            inside = [l for ts, l in self.lines if ts >= t0][:1]
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in self.lines:
+        for l in inside:
             f = [x.strip() for x in l.split(",")]
             if len(f) < 9:
                 continue
@@ -283,11 +296,12 @@ def run_b200(args, rank, world, local_rank):
     for _ in range(args.warmup):
         ctx.graph_launch(g)
     ctx.sync()
+    vis = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip().isdigit()]
+    gpu_index = int(vis[local_rank]) if local_rank < len(vis) else local_rank
+    clocks = ClockSampler(gpu_index)
+    clocks.start()
     barrier()
     ctx.sync()
-    vis = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip().isdigit()]
-    clocks = ClockSampler(int(vis[local_rank]) if local_rank < len(vis) else local_rank)
-    clocks.start()
     ms = timed(lambda: ctx.graph_launch(g), args.steps)
     ctx.sync()
     barrier()
@@ -358,7 +372,7 @@ def run_b200(args, rank, world, local_rank):
 
     e2e_tts = None
     if not args.no_e2e:
-        e2e_tts = e2e_bench(ctx, host_layers, args, rank, world)
+        e2e_tts = e2e_bench(ctx, host_layers, args, rank, world, gpu_index)
 
     base = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
 
@@ -641,17 +655,21 @@ def decode_bench(ctx, host_layers, args):
 # q 1024->2048 for 16 heads of 128, 2 KV heads) and the generation loop's
 # projections (config 4: FSQ 256, RALM 8 layers of the TSLM width).
 DIT_H, DIT_FFN, DIT_LAYERS, FEAT, PATCH, FSQ_DIM, RALM_LAYERS, ENC_LAYERS = 1024, 4096, 8, 64, 4, 256, 8, 8
+VOCAB = 73448
 SAMPLES_PER_PATCH, SAMPLE_RATE = 7680, 48000
 
 
-def e2e_bench(ctx, host_layers, args, rank, world):
+def e2e_bench(ctx, host_layers, args, rank, world, gpu_index=0):
     """end-to-end synthetic TTS.  args.e2e_utts utterances
     (200 random-token prompts, args.e2e_patches patches of 7680 samples at
     48 kHz each) sharded over the ranks; each rank runs its shard in lockstep
     through vb_gen (prompt, then per patch: mu -> 10-step CFM with CFG-Zero*
     -> LocEnc -> TSLM -> FSQ -> RALM -> stop head).  RTF = max-over-ranks
-    wall time / total audio seconds.  Excluded: text embedding lookup
-    (prompt embeddings are drawn directly) and the AudioVAE decoder."""
+    wall time / total audio seconds.  The timed region starts from token ids
+    in pinned host memory (copied in, looked up in a Q8_0 embedding table of
+    the 73,448-token vocabulary with vb_get_rows) and ends with the patches
+    and stop logits copied back to pinned host memory.  Excluded: the
+    AudioVAE decoder."""
     import torch
     import vcpm_b200 as vb
     rng = np.random.default_rng(11 + rank)
@@ -698,22 +716,35 @@ def e2e_bench(ctx, host_layers, args, rank, world):
                  enc_special=torch.from_numpy(small(DIT_H, 0.5)).cuda(), enc_norm=torch.from_numpy(norm(DIT_H)).cuda(),
                  feat_dim=FEAT, patch=PATCH, fsq_scale=9.0, eps=1e-5, cfm_steps=10, cfg_value=2.0)
     gen = vb.Gen(ctx, parts, B, T + NP + 8)
-    emb = (torch.randn(B, T, HIDDEN, device="cuda") * 0.5).to(torch.bfloat16).float()
+    embed = ctx.weight(vb.TYPE_Q8_0, HIDDEN, VOCAB, q8(VOCAB, HIDDEN))
+    ids_h = torch.from_numpy(rng.integers(0, VOCAB, (B, T)).astype(np.int32)).pin_memory()
+    ids = torch.zeros(B, T, dtype=torch.int32, device="cuda")
+    emb = torch.zeros(B, T, HIDDEN, device="cuda")
     patches = torch.zeros(NP, B, PATCH, FEAT, device="cuda")
     stops = torch.zeros(NP, B, 2, device="cuda")
+    patches_h = torch.zeros(NP, B, PATCH, FEAT).pin_memory()
+    stops_h = torch.zeros(NP, B, 2).pin_memory()
     ev = [ctx.event() for _ in range(3)]
+    torch.cuda.synchronize()
     ctx.sync()
+    clocks = ClockSampler(gpu_index)
+    clocks.start()
     if world > 1:
         torch.distributed.barrier()
     t0 = time.time()
     ctx.record(ev[0])
+    ctx.memcpy_h2d(ids, ids_h, ids_h.numel() * 4)
+    ctx.get_rows(embed, ids, B * T, emb)
     gen.prefill(T, emb)
     ctx.record(ev[1])
     for s in range(NP):
         gen.step(1000 + rank * B, patches[s], stops[s])
+    ctx.memcpy_d2h(patches_h, patches, patches.numel() * 4)
+    ctx.memcpy_d2h(stops_h, stops, stops.numel() * 4)
     ctx.record(ev[2])
     ctx.sync()
     wall = time.time() - t0
+    ck = clocks.stop()
     pre_ms, steps_ms = ctx.elapsed_ms(ev[0], ev[1]), ctx.elapsed_ms(ev[1], ev[2])
     rc, derr = ctx.device_status()
     finite = bool(torch.isfinite(patches).all().item())
@@ -723,6 +754,7 @@ def e2e_bench(ctx, host_layers, args, rank, world):
     total_ms = float(tt[0])
     audio_s = B * world * NP * SAMPLES_PER_PATCH / SAMPLE_RATE
     gen.close()
+    embed.release()
     for w in ws.values():
         w.release()
     for o in (tslm, ralm, enc):
@@ -732,10 +764,12 @@ def e2e_bench(ctx, host_layers, args, rank, world):
             "unit": "s/s", "higher_is_better": False, "utterances": B * world, "utterances_per_gpu": B,
             "patches": NP, "prompt_tokens": T, "audio_s": audio_s, "wall_ms_max_over_ranks": total_ms,
             "prefill_ms": float(tt[1]), "steps_ms": float(tt[2]), "per_patch_ms": float(tt[2]) / NP,
-            "host_wall_s_rank0": wall, "device_error": derr, "patches_finite": finite,
-            "pipeline": "vb_gen: prompt (TSLM 28L, RALM 8L) then per patch mu -> CFM (9 LocDiT evals, CFG batch) "
-                        "-> LocEnc 8L -> TSLM step -> FSQ -> RALM step -> stop head",
-            "excluded": "text embedding lookup; AudioVAE decode (runs on the host CPU in the reference, not built)"}
+            "host_wall_s_rank0": wall, "device_error": derr, "patches_finite": finite, "clocks": ck,
+            "pipeline": "token ids H2D -> vb_get_rows (Q8_0 embedding 73448 x 2048) -> vb_gen: prompt (TSLM 28L, "
+                        "RALM 8L) then per patch mu -> CFM (9 LocDiT evals, CFG batch) -> LocEnc 8L -> TSLM step "
+                        "-> FSQ -> RALM step -> stop head -> patches and stop logits D2H",
+            "h2d_bytes": int(ids_h.numel() * 4), "d2h_bytes": int((patches_h.numel() + stops_h.numel()) * 4),
+            "excluded": "AudioVAE decode (runs on the host CPU in the reference)"}
 
 
 def main():

@@ -175,6 +175,15 @@ int vb_quantize_q8_0(vb_ctx *ctx, const float *x, int64_t K, int64_t M,
  * src/gen_prompt.c:106-125), n values. */
 int vb_dequantize_q8_0(vb_ctx *ctx, const void *blocks, int64_t n, float *y);
 
+/* Embedding lookup (gen_forward_text, src/gen_prompt.c:67-131): y row i =
+ * row ids[i] of a registered Q8_0 / F16 / F32 table [N rows][K] as F32
+ * (Q8_0: (float)qs * d exactly); an id outside [0, N) reads row 0, as the
+ * reference does.  ids: device int32 [n]; y: device F32 [n][K], 16-byte
+ * aligned; K a multiple of 8.  Replaces the host loop over the F32 copy of
+ * embed_tokens made at src/gen_init.c:370-421. */
+int vb_get_rows(vb_ctx *ctx, vb_weight table, const int32_t *ids, int64_t n,
+                float *y);
+
 /* vcpm_rms_norm (src/minicpm4.c:132-152): with w != NULL and VB_OUT_BF16,
  * y = bf16(bf16(rms_norm(x)) * w); with w == NULL and flags == 0 the plain
  * ggml_rms_norm.  rows of n floats. */

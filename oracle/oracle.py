@@ -114,6 +114,7 @@ def _declare(L):
         "vo_quantize_q8_0": (None, [P, P, I64, I]),
         "vo_dequantize_q8_0": (None, [P, P, I64]),
         "vo_row_bytes": (C.c_size_t, [I, I64]),
+        "vo_get_rows": (I, [I, P, I64, I64, P, I64, P]),
         "vo_matmul": (I, [I, P, I64, I64, P, I64, P, I, I]),
         "vo_rms_norm": (None, [P, P, I64, I64, F]),
         "vo_rms_norm_bf16": (None, [P, P, P, I64, I64, F]),
@@ -208,6 +209,17 @@ def weight_as_f32(wtype, w, K):
     if wtype == TYPE_F16:
         return w.view(np.float16).astype(np.float32)
     return w
+
+
+def get_rows(wtype, table, K, n_rows, ids):
+    """Embedding lookup of gen_forward_text -> float32 [len(ids), K]."""
+    table = np.ascontiguousarray(table)
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    out = np.zeros((ids.size, K), dtype=np.float32)
+    rc = lib().vo_get_rows(wtype, _p(table), K, n_rows, _p(ids), ids.size, _p(out))
+    if rc:
+        raise ValueError("vo_get_rows: unsupported type %d" % wtype)
+    return out
 
 
 # ------------------------------------------------------------------- norms

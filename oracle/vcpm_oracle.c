@@ -158,6 +158,31 @@ void vo_dequantize_q8_0(const void *blocks, float *y, int64_t n) {
     }
 }
 
+/* Embedding lookup of gen_forward_text (src/gen_prompt.c:67-131): out row
+ * i = table row ids[i] as F32, an id outside [0, n_rows) reading row 0.
+ * Q8_0 values are qs * fp16->fp32(d) (:106-125), F16 the exact widening
+ * (:88-95), F32 a copy (:96-103).  Returns -1 for an unknown type. */
+int vo_get_rows(int type, const void *table, int64_t K, int64_t n_rows, const int32_t *ids, int64_t n,
+                float *out) {
+    const size_t rb = vo_row_bytes(type, K);
+    if (rb == 0) return -1;
+    for (int64_t i = 0; i < n; i++) {
+        int64_t id = ids[i];
+        if (id < 0 || id >= n_rows) id = 0;
+        const uint8_t *row = (const uint8_t *)table + (size_t)id * rb;
+        float *y = out + i * K;
+        if (type == VO_TYPE_Q8_0) {
+            vo_dequantize_q8_0(row, y, K);
+        } else if (type == VO_TYPE_F16) {
+            const uint16_t *h = (const uint16_t *)row;
+            for (int64_t k = 0; k < K; k++) y[k] = vo_fp16_to_fp32(h[k]);
+        } else {
+            memcpy(y, row, (size_t)K * 4u);
+        }
+    }
+    return 0;
+}
+
 size_t vo_row_bytes(int type, int64_t K) {
     switch (type) {
     case VO_TYPE_F32: return (size_t)K * 4u;

@@ -63,6 +63,8 @@ void     vo_bf16_round_array(float *x, int64_t n);
 void vo_quantize_q8_0(const float *x, void *blocks, int64_t n, int rule);
 void vo_dequantize_q8_0(const void *blocks, float *y, int64_t n);
 size_t vo_row_bytes(int type, int64_t K);
+int vo_get_rows(int type, const void *table, int64_t K, int64_t n_rows, const int32_t *ids, int64_t n,
+                float *out);
 
 /* y[m*N+n] = sum_k W[n,k]*x[m*K+k] with ggml-CPU operand conversion:
  * Q8_0 weights quantize x rows to Q8_0 (rule), F16 weights round x to fp16,

@@ -71,6 +71,42 @@ def test_dequantize_q8_0_bit_exact(ctx):
     assert np.array_equal(host(y), O.dequantize_q8_0(w, 2048).ravel())
 
 
+@pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_F16, O.TYPE_F32])
+def test_get_rows_bit_exact(ctx, wtype):
+    """Embedding lookup (src/gen_prompt.c:67-131): random, repeated,
+    negative and out-of-range ids (which read row 0)."""
+    K, N = 2048, 3001
+    table = S.weight(wtype, N, K)
+    w = ctx.weight(wtype, K, N, table)
+    rng = np.random.default_rng(5)
+    ids = rng.integers(0, N, 200).astype(np.int32)
+    ids[:6] = [0, N - 1, -1, N, 2 ** 31 - 1, 7]
+    ids[6:10] = ids[10]
+    y = torch.full((ids.size, K), float("nan"), dtype=torch.float32, device="cuda")
+    idd = dev(ids)
+    run(ctx, lambda: ctx.get_rows(w, idd, ids.size, y))
+    ref = O.get_rows(wtype, table, K, N, ids)
+    assert np.array_equal(host(y).view(np.uint32), ref.view(np.uint32))
+    run(ctx, lambda: ctx.get_rows(w, idd, 0, y))        # empty lookup
+    w.release()
+
+
+def test_get_rows_rejects_bad_arguments(ctx):
+    table = S.weight(O.TYPE_F32, 16, 12)
+    w = ctx.weight(O.TYPE_F32, 12, 16, table)                # K % 8 != 0
+    ids = torch.zeros(4, dtype=torch.int32, device="cuda")
+    y = torch.zeros((4, 16), dtype=torch.float32, device="cuda")
+    with pytest.raises(vb.VBError) as e:
+        ctx.get_rows(w, ids, 4, y)
+    assert e.value.code == vb.VB_ERR_INVALID_ARG
+    w.release()
+    w = ctx.weight(O.TYPE_Q8_0, 64, 16, S.weight(O.TYPE_Q8_0, 16, 64))
+    with pytest.raises(vb.VBError) as e:
+        ctx.get_rows(w, ids, 2, y.data_ptr() + 4)            # misaligned output
+    assert e.value.code == vb.VB_ERR_INVALID_ARG
+    w.release()
+
+
 # ------------------------------------------------------------------ matmul
 SHAPES = [(2048, 2048), (2048, 256), (2048, 6144), (6144, 2048), (1024, 2048), (64, 1024), (1024, 64)]
 

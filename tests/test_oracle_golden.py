@@ -178,6 +178,27 @@ def test_q8_0_weight_quantizer_matches_gguf_py():
     assert np.array_equal(O.dequantize_q8_0(ours, 2048), deq.astype(np.float32))
 
 
+@pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_F16, O.TYPE_F32])
+def test_get_rows_restates_prompt_embedding(wtype):
+    """Oracle embedding lookup (src/gen_prompt.c:67-131) against an
+    independent numpy dequantization; out-of-range ids read row 0."""
+    K, N = 256, 40
+    w = _rng_weights(N * K, seed=4).reshape(N, K)
+    table = O.make_weight(wtype, w, O.QRULE_REF)
+    if wtype == O.TYPE_Q8_0:
+        blk = table.reshape(N, K // 32, 34)
+        d = blk[..., :2].copy().view(np.float16).astype(np.float32)
+        full = (blk[..., 2:].view(np.int8).astype(np.float32) * d).reshape(N, K)
+    elif wtype == O.TYPE_F16:
+        full = table.view(np.float16).astype(np.float32).reshape(N, K)
+    else:
+        full = table.reshape(N, K)
+    ids = np.array([3, 0, N - 1, -5, N, 3, 17], np.int32)
+    got = O.get_rows(wtype, table, K, N, ids)
+    want = full[np.where((ids >= 0) & (ids < N), ids, 0)]
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 def _np_quant_x86(x):
     """Independent numpy statement of the x86 activation rule."""
     b = x.reshape(-1, 32).astype(np.float32)

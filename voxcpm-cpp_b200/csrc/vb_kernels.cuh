@@ -41,6 +41,7 @@ void gemm_free(vb_ctx *ctx);
 
 int launch_quantize_q8_0(vb_ctx *ctx, const float *x, int64_t K, int64_t M, void *blocks, int rule);
 int launch_dequantize_q8_0(vb_ctx *ctx, const void *blocks, int64_t n, float *y);
+int launch_get_rows(vb_ctx *ctx, vb_weight w, const int32_t *ids, int64_t n, float *y);
 
 // elementwise (vb_elem.cu)
 int launch_rms_norm(vb_ctx *ctx, const float *x, const float *w, float *y, int64_t n, int64_t rows, float eps,

@@ -54,6 +54,11 @@ extern "C" int vb_dequantize_q8_0(vb_ctx *ctx, const void *blocks, int64_t n, fl
     return launch_dequantize_q8_0(ctx, blocks, n, y);
 }
 
+extern "C" int vb_get_rows(vb_ctx *ctx, vb_weight table, const int32_t *ids, int64_t n, float *y) {
+    VB_REQUIRE(ctx, table && ids && y && n >= 0, "vb_get_rows: bad argument");
+    return launch_get_rows(ctx, table, ids, n, y);
+}
+
 extern "C" int vb_rms_norm(vb_ctx *ctx, const float *x, const float *w, float *y, int64_t n, int64_t rows, float eps,
                            unsigned flags) {
     VB_REQUIRE(ctx, x && y && n > 0 && rows >= 0, "vb_rms_norm: bad argument");

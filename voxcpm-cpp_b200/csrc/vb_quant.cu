@@ -145,4 +145,63 @@ int launch_dequantize_q8_0(vb_ctx *ctx, const void *blocks, int64_t n, float *y)
     return VB_OK;
 }
 
+// Embedding lookup (gen_forward_text, src/gen_prompt.c:67-131): row i of y
+// is table row ids[i] as F32; an id outside [0, N) reads row 0, as the
+// reference clamps it.  Q8_0 rows are (float)qs * fp16->fp32(d), one exact
+// product per value; F16 rows are the exact widening; F32 rows are copied.
+// One CTA per output row, 8 values per thread per pass.
+template <int TYPE>
+__global__ void get_rows_kernel(const void *__restrict__ data, const uint16_t *__restrict__ scales, int64_t K,
+                                int64_t N, const int32_t *__restrict__ ids, float *__restrict__ y) {
+    const int64_t i = blockIdx.x;
+    int64_t id = ids[i];
+    if (id < 0 || id >= N) id = 0;
+    float *yr = y + i * K;
+    for (int64_t k = (int64_t)threadIdx.x * 8; k < K; k += (int64_t)blockDim.x * 8) {
+        float v[8];
+        if (TYPE == VB_TYPE_Q8_0) {
+            const int2 q = __ldg(reinterpret_cast<const int2 *>(static_cast<const int8_t *>(data) + id * K + k));
+            const float d = h2f(__ldg(scales + id * (K / QK) + k / QK));
+            const int8_t *qb = reinterpret_cast<const int8_t *>(&q);
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = __fmul_rn((float)qb[e], d);
+        } else if (TYPE == VB_TYPE_F16) {
+            const int4 h = __ldg(reinterpret_cast<const int4 *>(static_cast<const uint16_t *>(data) + id * K + k));
+            const uint16_t *hb = reinterpret_cast<const uint16_t *>(&h);
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[e] = h2f(hb[e]);
+        } else {
+            const float4 *src = reinterpret_cast<const float4 *>(static_cast<const float *>(data) + id * K + k);
+            const float4 a = __ldg(src), b = __ldg(src + 1);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+            v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        }
+        reinterpret_cast<float4 *>(yr + k)[0] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4 *>(yr + k)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+}
+
+int launch_get_rows(vb_ctx *ctx, vb_weight w, const int32_t *ids, int64_t n, float *y) {
+    if (w->K % 8)
+        return set_error(ctx, VB_ERR_INVALID_ARG, "get_rows: row width K=%lld is not a multiple of 8", (long long)w->K);
+    if (reinterpret_cast<uintptr_t>(y) % 16)
+        return set_error(ctx, VB_ERR_INVALID_ARG, "get_rows: output is not 16-byte aligned");
+    if (n > 0x7fffffffLL) return set_error(ctx, VB_ERR_INVALID_ARG, "get_rows: too many rows");
+    if (n == 0) return VB_OK;
+    const int threads = (int)std::min<int64_t>(256, (w->K / 8 + 31) / 32 * 32);
+    switch (w->type) {
+        case VB_TYPE_Q8_0:
+            get_rows_kernel<VB_TYPE_Q8_0><<<(unsigned)n, threads, 0, ctx->stream>>>(w->data, w->scales, w->K, w->N, ids, y);
+            break;
+        case VB_TYPE_F16:
+            get_rows_kernel<VB_TYPE_F16><<<(unsigned)n, threads, 0, ctx->stream>>>(w->data, nullptr, w->K, w->N, ids, y);
+            break;
+        default:
+            get_rows_kernel<VB_TYPE_F32><<<(unsigned)n, threads, 0, ctx->stream>>>(w->data, nullptr, w->K, w->N, ids, y);
+            break;
+    }
+    VB_LAUNCH_CHECK(ctx, "get_rows");
+    return VB_OK;
+}
+
 }  // namespace vb

@@ -106,6 +106,7 @@ SIGNATURES = {
     "vb_program_destroy": (None, [_P]),
     "vb_quantize_q8_0": (_I, [_P, _P, _I64, _I64, _P, _I]),
     "vb_dequantize_q8_0": (_I, [_P, _P, _I64, _P]),
+    "vb_get_rows": (_I, [_P, _P, _P, _I64, _P]),
     "vb_rms_norm": (_I, [_P, _P, _P, _P, _I64, _I64, _F, _U]),
     "vb_bf16_round": (_I, [_P, _P, _I64]),
     "vb_residual_add": (_I, [_P, _P, _P, _F, _P, _I64, _U]),
@@ -277,6 +278,9 @@ class Context:
 
     def dequantize_q8_0(self, blocks, n, y):
         self.check(self.L.vb_dequantize_q8_0(self.h, _addr(blocks), n, _addr(y)))
+
+    def get_rows(self, table, ids, n, y):
+        self.check(self.L.vb_get_rows(self.h, table.h, _addr(ids), n, _addr(y)))
 
     def rms_norm(self, x, w, y, n, rows, eps, flags=0):
         self.check(self.L.vb_rms_norm(self.h, _addr(x), _addr(w), _addr(y), n, rows, eps, flags))
