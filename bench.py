@@ -82,8 +82,9 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index):
+    def __init__(self, gpu_index, period_ms=20):
         self.gpu = gpu_index
+        self.period_ms = int(period_ms)
         self.proc = None
         self.lines = []
         self.t = None
@@ -94,7 +95,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", str(self.period_ms)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except (OSError, ValueError):
@@ -657,6 +658,57 @@ def decode_bench(ctx, host_layers, args):
 DIT_H, DIT_FFN, DIT_LAYERS, FEAT, PATCH, FSQ_DIM, RALM_LAYERS, ENC_LAYERS = 1024, 4096, 8, 64, 4, 256, 8, 8
 VOCAB = 73448
 SAMPLES_PER_PATCH, SAMPLE_RATE = 7680, 48000
+VAE_LATENT, VAE_DIM, VAE_RATES = 64, 2048, (8, 6, 5, 2, 2, 2)
+VAE_SLOTS = 145
+FP32_SIMT_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12   # FMA lanes x 2 x max SM clock
+
+
+def vae_slot_block(b, part):
+    return 4 + 23 * b + part
+
+
+def vae_slot_res(b, u, part):
+    return 4 + 23 * b + 5 + 6 * u + part
+
+
+def synth_vae(rng, dim=VAE_DIM, latent=VAE_LATENT, rates=VAE_RATES):
+    """F32 AudioVAE V2 decoder tensors in the C ABI's slot order: conv
+    weights N(0, 1/fan_in), Snake alphas in [0.5, 1.5), small biases."""
+    t = [None] * VAE_SLOTS
+
+    def w(shape, fan):
+        return (rng.standard_normal(shape) / np.sqrt(fan)).astype(np.float32)
+
+    def vec(n, std=0.02):
+        return (std * rng.standard_normal(n)).astype(np.float32)
+
+    def alpha(n):
+        return (0.5 + rng.random(n)).astype(np.float32)
+
+    t[0], t[1], t[2], t[3] = w((latent, 7), 7), vec(latent), w((dim, latent), latent), vec(dim)
+    for b in range(6):
+        ci, co, s = dim >> b, dim >> (b + 1), rates[b]
+        t[vae_slot_block(b, 2)], t[vae_slot_block(b, 3)] = alpha(ci), w((ci, co, 2 * s), 2 * ci)
+        t[vae_slot_block(b, 4)] = vec(co)
+        for u in range(3):
+            t[vae_slot_res(b, u, 0)], t[vae_slot_res(b, u, 1)] = alpha(co), w((co, 7), 7)
+            t[vae_slot_res(b, u, 2)], t[vae_slot_res(b, u, 3)] = vec(co), alpha(co)
+            t[vae_slot_res(b, u, 4)], t[vae_slot_res(b, u, 5)] = w((co, co), 4 * co), vec(co)
+    cl = dim >> 6
+    t[142], t[143], t[144] = alpha(cl), w((cl, 7), 7 * cl) * np.float32(0.15), vec(1)
+    return t
+
+
+def vae_flops(frames, dim=VAE_DIM, latent=VAE_LATENT, rates=VAE_RATES):
+    """Multiply-add flops of decoding `frames` latent frames (2 per MAC)."""
+    f = 2 * frames * (7 * latent + latent * dim)
+    T = frames
+    for b in range(6):
+        ci, co, s = dim >> b, dim >> (b + 1), rates[b]
+        f += 2 * T * (2 * ci) * (s * co)           # transposed conv as [x(q-1)|x(q)] x [2Ci][s*Co]
+        T *= s
+        f += 3 * 2 * T * (7 * co + co * co)        # residual units: depthwise k7 + pointwise
+    return f + 2 * T * 7 * (dim >> 6)
 
 
 def e2e_bench(ctx, host_layers, args, rank, world, gpu_index=0):
@@ -667,9 +719,9 @@ def e2e_bench(ctx, host_layers, args, rank, world, gpu_index=0):
     -> LocEnc -> TSLM -> FSQ -> RALM -> stop head).  RTF = max-over-ranks
     wall time / total audio seconds.  The timed region starts from token ids
     in pinned host memory (copied in, looked up in a Q8_0 embedding table of
-    the 73,448-token vocabulary with vb_get_rows) and ends with the patches
-    and stop logits copied back to pinned host memory.  Excluded: the
-    AudioVAE decoder."""
+    the 73,448-token vocabulary with vb_get_rows); every patch is decoded to
+    PCM by the AudioVAE V2 streaming decoder (vb_vae), and the region ends
+    with the PCM and stop logits copied back to pinned host memory."""
     import torch
     import vcpm_b200 as vb
     rng = np.random.default_rng(11 + rank)
@@ -715,19 +767,35 @@ def e2e_bench(ctx, host_layers, args, rank, world, gpu_index=0):
     parts = dict(tslm=tslm, ralm=ralm, enc=enc, dit=dit, **ws, **bs,
                  enc_special=torch.from_numpy(small(DIT_H, 0.5)).cuda(), enc_norm=torch.from_numpy(norm(DIT_H)).cuda(),
                  feat_dim=FEAT, patch=PATCH, fsq_scale=9.0, eps=1e-5, cfm_steps=10, cfg_value=2.0)
-    gen = vb.Gen(ctx, parts, B, T + NP + 8)
     embed = ctx.weight(vb.TYPE_Q8_0, HIDDEN, VOCAB, q8(VOCAB, HIDDEN))
+    vae = vb.VAE(ctx, vb.VAEConfig(VAE_LATENT, VAE_DIM, VAE_RATES, vb.TYPE_F32), synth_vae(rng))
+    vst = vae.stream(B, PATCH)
+    audio = torch.zeros(NP, B, SAMPLES_PER_PATCH, device="cuda")
+    audio_h = torch.zeros(NP, B, SAMPLES_PER_PATCH).pin_memory()
     ids_h = torch.from_numpy(rng.integers(0, VOCAB, (B, T)).astype(np.int32)).pin_memory()
     ids = torch.zeros(B, T, dtype=torch.int32, device="cuda")
     emb = torch.zeros(B, T, HIDDEN, device="cuda")
     patches = torch.zeros(NP, B, PATCH, FEAT, device="cuda")
     stops = torch.zeros(NP, B, 2, device="cuda")
-    patches_h = torch.zeros(NP, B, PATCH, FEAT).pin_memory()
     stops_h = torch.zeros(NP, B, 2).pin_memory()
     ev = [ctx.event() for _ in range(3)]
+    # Untimed warm-up of the whole pipeline on a throw-away generator: the
+    # context's scratch arenas, kernel attributes and the decoder's
+    # activation buffers reach their steady-state sizes here.
+    warm = vb.Gen(ctx, parts, B, T + 8)
+    ctx.memcpy_h2d(ids, ids_h, ids_h.numel() * 4)
+    ctx.get_rows(embed, ids, B * T, emb)
+    warm.prefill(T, emb)
+    for s in range(2):
+        warm.step(7, patches[s], stops[s])
+        vst.decode(patches[s], PATCH, audio[s])
+    ctx.sync()
+    warm.close()
+    vst.reset()
+    gen = vb.Gen(ctx, parts, B, T + NP + 8)
     torch.cuda.synchronize()
     ctx.sync()
-    clocks = ClockSampler(gpu_index)
+    clocks = ClockSampler(gpu_index, args.e2e_clock_ms)
     clocks.start()
     if world > 1:
         torch.distributed.barrier()
@@ -739,7 +807,8 @@ def e2e_bench(ctx, host_layers, args, rank, world, gpu_index=0):
     ctx.record(ev[1])
     for s in range(NP):
         gen.step(1000 + rank * B, patches[s], stops[s])
-    ctx.memcpy_d2h(patches_h, patches, patches.numel() * 4)
+        vst.decode(patches[s], PATCH, audio[s])
+    ctx.memcpy_d2h(audio_h, audio, audio.numel() * 4)
     ctx.memcpy_d2h(stops_h, stops, stops.numel() * 4)
     ctx.record(ev[2])
     ctx.sync()
@@ -747,7 +816,18 @@ def e2e_bench(ctx, host_layers, args, rank, world, gpu_index=0):
     ck = clocks.stop()
     pre_ms, steps_ms = ctx.elapsed_ms(ev[0], ev[1]), ctx.elapsed_ms(ev[1], ev[2])
     rc, derr = ctx.device_status()
-    finite = bool(torch.isfinite(patches).all().item())
+    finite = bool(torch.isfinite(patches).all().item()) and bool(torch.isfinite(audio).all().item())
+    # the decoder alone, continuing the same streams: 10 more patches
+    vev = [ctx.event() for _ in range(2)]
+    ctx.record(vev[0])
+    for s in range(10):
+        vst.decode(patches[s], PATCH, audio[s])
+    ctx.record(vev[1])
+    ctx.sync()
+    vae_ms = ctx.elapsed_ms(vev[0], vev[1]) / 10
+    vae_tflops = vae_flops(B * PATCH) / (vae_ms * 1e-3) / 1e12
+    vst.close()
+    vae.close()
     tt = torch.tensor([pre_ms + steps_ms, pre_ms, steps_ms], dtype=torch.float64, device="cuda")
     if world > 1:
         torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
@@ -765,11 +845,16 @@ def e2e_bench(ctx, host_layers, args, rank, world, gpu_index=0):
             "patches": NP, "prompt_tokens": T, "audio_s": audio_s, "wall_ms_max_over_ranks": total_ms,
             "prefill_ms": float(tt[1]), "steps_ms": float(tt[2]), "per_patch_ms": float(tt[2]) / NP,
             "host_wall_s_rank0": wall, "device_error": derr, "patches_finite": finite, "clocks": ck,
+            "warmup": "one untimed prompt + 2 patches on a separate generator (same context)",
             "pipeline": "token ids H2D -> vb_get_rows (Q8_0 embedding 73448 x 2048) -> vb_gen: prompt (TSLM 28L, "
                         "RALM 8L) then per patch mu -> CFM (9 LocDiT evals, CFG batch) -> LocEnc 8L -> TSLM step "
-                        "-> FSQ -> RALM step -> stop head -> patches and stop logits D2H",
-            "h2d_bytes": int(ids_h.numel() * 4), "d2h_bytes": int((patches_h.numel() + stops_h.numel()) * 4),
-            "excluded": "AudioVAE decode (runs on the host CPU in the reference)"}
+                        "-> FSQ -> RALM step -> stop head -> AudioVAE V2 streaming decode (F32, 7680 samples) "
+                        "-> PCM and stop logits D2H",
+            "h2d_bytes": int(ids_h.numel() * 4), "d2h_bytes": int((audio_h.numel() + stops_h.numel()) * 4),
+            "vae": {"ms_per_patch": vae_ms, "streams": B, "gflop_per_patch": vae_flops(B * PATCH) / 1e9,
+                    "tflops": vae_tflops, "fp32_simt_nominal_tflops": FP32_SIMT_NOMINAL_TFLOPS,
+                    "frac_of_nominal": vae_tflops / FP32_SIMT_NOMINAL_TFLOPS},
+            "excluded": "none of the synthetic pipeline (tokenizer and WAV writing are host I/O)"}
 
 
 def main():
@@ -785,6 +870,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-utts", type=int, default=64)
     ap.add_argument("--e2e-patches", type=int, default=100)
+    ap.add_argument("--e2e-clock-ms", type=int, default=500, help="nvidia-smi sampling period during the e2e run")
     ap.add_argument("--mode", default="full", choices=["full", "config1", "gemm", "decode"],
                     help="config1 / gemm / decode: small profiling cases (config-1 streaming program, one "
                          "tensor-core mat-mul shape, the single-launch decode step)")

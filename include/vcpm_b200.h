@@ -402,6 +402,74 @@ int vb_gen_prefill(vb_ctx *ctx, vb_gen g, int T, const float *embeds);
 int vb_gen_step(vb_ctx *ctx, vb_gen g, uint64_t seed, float *patches, float *stop_logits);
 void vb_gen_destroy(vb_ctx *ctx, vb_gen g);
 
+/* ---- AudioVAE V2 decoder -------------------------------------------------
+ * Latent patches -> 48 kHz PCM, streaming, for a batch of independent
+ * utterances decoded in lockstep.  Replaces vcpm_vae_stream_create / _reset
+ * / _decode / _free (src/audio_vae_stream.h, src/audio_vae_stream.c:80-619)
+ * and the whole-utterance vcpm_vae_v2_decode (src/audio_vae_v2_decoder.c:
+ * 149-282, which equals a stream decoded from reset state). */
+typedef struct vb_vae_config {
+    int latent_dim;     /* latent channels (64) */
+    int decoder_dim;    /* 2048: block b maps decoder_dim>>b to decoder_dim>>(b+1)
+                         * channels (src/audio_vae_v2.c:40-43); multiple of 256 */
+    int rates[6];       /* upsampling strides, transposed-conv kernel 2*rate (8,6,5,2,2,2) */
+    int weight_type;    /* storage of the conv weights: VB_TYPE_F32 or VB_TYPE_F16 */
+} vb_vae_config;
+
+/* Tensor slots of vb_vae_create, host pointers in GGUF element order.  Conv
+ * weights are in cfg.weight_type; biases, Snake alphas and the sr_cond
+ * vectors are F32 per channel.  A NULL alpha skips that Snake and a NULL
+ * bias adds none (as a missing tensor does in the reference); the sr_cond
+ * pair of a block is the bucket row the caller selected (the reference's
+ * vcpm_vae_sr_cond_embedding_extract, src/audio_vae_v2.c:652-708) or
+ * NULL for none. */
+enum {
+    VB_VAE_IN_DW_W = 0,    /* audio_vae.decoder.model.0.weight.weight [latent][7] (depthwise) */
+    VB_VAE_IN_DW_B = 1,    /* model.0.bias [latent]                                        */
+    VB_VAE_IN_PW_W = 2,    /* model.1.weight.weight [D][latent]                             */
+    VB_VAE_IN_PW_B = 3,    /* model.1.bias [D]                                              */
+    VB_VAE_BLOCK0 = 4,     /* model.(2+b) starts at slot BLOCK0 + b*BLOCK_SLOTS             */
+    VB_VAE_BLOCK_SLOTS = 23,
+    VB_VAE_B_SR_SCALE = 0, /* sr_cond_model.(2+b).scale_embed row [Ci]                      */
+    VB_VAE_B_SR_BIAS = 1,  /* sr_cond_model.(2+b).bias_embed row [Ci]                       */
+    VB_VAE_B_ALPHA = 2,    /* model.(2+b).block.0.alpha [Ci]                                */
+    VB_VAE_B_UP_W = 3,     /* model.(2+b).block.1.weight.weight [Ci][Co][2*rate]            */
+    VB_VAE_B_UP_B = 4,     /* model.(2+b).block.1.bias [Co]                                 */
+    VB_VAE_B_RES0 = 5,     /* residual unit u = block.(2+u) at B_RES0 + u*RES_SLOTS         */
+    VB_VAE_RES_SLOTS = 6,
+    VB_VAE_R_ALPHA0 = 0,   /* block.(2+u).block.0.alpha [Co]                                */
+    VB_VAE_R_DW_W = 1,     /* block.(2+u).block.1.weight.weight [Co][7] (depthwise, dilation 1/3/9) */
+    VB_VAE_R_DW_B = 2,     /* block.(2+u).block.1.bias [Co]                                 */
+    VB_VAE_R_ALPHA2 = 3,   /* block.(2+u).block.2.alpha [Co]                                */
+    VB_VAE_R_PW_W = 4,     /* block.(2+u).block.3.weight.weight [Co][Co]                    */
+    VB_VAE_R_PW_B = 5,     /* block.(2+u).block.3.bias [Co]                                 */
+    VB_VAE_OUT_ALPHA = 142, /* model.8.alpha [D>>6]                                         */
+    VB_VAE_OUT_W = 143,     /* model.9.weight.weight [D>>6][7]                              */
+    VB_VAE_OUT_B = 144,     /* model.9.bias [1]                                             */
+    VB_VAE_N_SLOTS = 145
+};
+
+typedef struct vb_vae_s *vb_vae;
+typedef struct vb_vae_stream_s *vb_vae_stream;
+/* Uploads the decoder (one-time repack to F32 device layouts). */
+int vb_vae_create(vb_ctx *ctx, const vb_vae_config *cfg, const void *const *tensors, vb_vae *out);
+void vb_vae_destroy(vb_ctx *ctx, vb_vae v);
+size_t vb_vae_device_bytes(vb_vae v);
+/* History caches of n_streams utterances, zeroed (vcpm_vae_stream_create;
+ * patch_size only sets vb_vae_stream_patch_samples). */
+int vb_vae_stream_create(vb_ctx *ctx, vb_vae v, int n_streams, int patch_size, vb_vae_stream *out);
+int vb_vae_stream_reset(vb_ctx *ctx, vb_vae_stream s);
+/* latent: device [n_streams][n_timesteps][latent_dim] (time-major, as
+ * vcpm_vae_stream_decode takes it); audio: device [n_streams][n_timesteps *
+ * prod(rates)] in (-1, 1).  Both 16-byte aligned.  Enqueued on the context
+ * stream; the caches advance by n_timesteps. */
+int vb_vae_stream_decode(vb_ctx *ctx, vb_vae_stream s, const float *latent, int n_timesteps, float *audio);
+void vb_vae_stream_destroy(vb_ctx *ctx, vb_vae_stream s);
+int vb_vae_stream_conv_cache_count(vb_vae_stream s);     /* 20 */
+int vb_vae_stream_upconv_cache_count(vb_vae_stream s);   /* 6  */
+int vb_vae_stream_patch_samples(vb_vae_stream s);        /* patch_size * prod(rates) */
+size_t vb_vae_stream_state_bytes(vb_vae_stream s);       /* device bytes of the caches */
+
 /* Host helpers restated from the reference for its callers. */
 float vb_cfm_sway_t_bf16(int step, int n_steps);   /* src/cfm_solver.c:27-37 */
 int vb_cfm_zero_star_steps(int n_steps);           /* src/gen_step.c:50-54 */

@@ -32,7 +32,7 @@ _f32acc = None
 def build(force: bool = False) -> str:
     """Compile liboracle.so (and its fp32-accumulation twin) with the
     committed Makefile."""
-    src = os.path.getmtime(os.path.join(HERE, "vcpm_oracle.c"))
+    src = max(os.path.getmtime(os.path.join(HERE, f)) for f in ("vcpm_oracle.c", "vcpm_oracle_vae.c", "vcpm_oracle.h"))
     stale = any(not os.path.exists(p) or os.path.getmtime(p) < src for p in (LIB_PATH, LIB_F32ACC_PATH))
     if force or stale:
         subprocess.check_call(["make", "-s", "-B" if force else "all", "-C", HERE])
@@ -137,6 +137,12 @@ def _declare(L):
         "vo_cfm_solve": (I, [P, P, P, P, P, I, F, P]),
         "vo_round_cache_capacity": (I, [I, I]),
         "vo_fill_normal": (None, [U64, F, F, P, I64]),
+        "vo_vae_check_config": (I, [P]),
+        "vo_vae_upsample": (I, [P]),
+        "vo_vae_stream_create": (P, [P, P]),
+        "vo_vae_stream_free": (None, [P]),
+        "vo_vae_stream_decode": (I, [P, P, I, P]),
+        "vo_vae_decode": (I, [P, P, P, I, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -411,3 +417,73 @@ def fill_normal(seed, mean, std, n):
 
 def round_cache_capacity(required, model_max):
     return lib().vo_round_cache_capacity(required, model_max)
+
+
+# ------------------------------------------------------------ AudioVAE V2
+VAE_IN_DW_W, VAE_IN_DW_B, VAE_IN_PW_W, VAE_IN_PW_B, VAE_BLOCK0, VAE_BLOCK_SLOTS = 0, 1, 2, 3, 4, 23
+VAE_B_SR_SCALE, VAE_B_SR_BIAS, VAE_B_ALPHA, VAE_B_UP_W, VAE_B_UP_B, VAE_B_RES0, VAE_RES_SLOTS = 0, 1, 2, 3, 4, 5, 6
+VAE_R_ALPHA0, VAE_R_DW_W, VAE_R_DW_B, VAE_R_ALPHA2, VAE_R_PW_W, VAE_R_PW_B = 0, 1, 2, 3, 4, 5
+VAE_OUT_ALPHA, VAE_OUT_W, VAE_OUT_B, VAE_N_SLOTS = 142, 143, 144, 145
+
+
+def vae_block_slot(b, part):
+    return VAE_BLOCK0 + b * VAE_BLOCK_SLOTS + part
+
+
+def vae_res_slot(b, u, part):
+    return VAE_BLOCK0 + b * VAE_BLOCK_SLOTS + VAE_B_RES0 + u * VAE_RES_SLOTS + part
+
+
+class VAEConfig(C.Structure):
+    _fields_ = [("latent_dim", C.c_int), ("decoder_dim", C.c_int), ("rates", C.c_int * 6)]
+
+    def __init__(self, latent_dim=64, decoder_dim=2048, rates=(8, 6, 5, 2, 2, 2)):
+        super().__init__(latent_dim, decoder_dim, (C.c_int * 6)(*rates))
+
+    def upsample(self):
+        return int(np.prod(list(self.rates)))
+
+
+class _VAETensors:
+    """Keeps F32 copies of the slot tensors alive behind a pointer table."""
+
+    def __init__(self, tensors):
+        assert len(tensors) == VAE_N_SLOTS
+        self.arrays = [None if t is None else f32(t).copy() for t in tensors]
+        self.table = (C.c_void_p * VAE_N_SLOTS)(*[None if a is None else a.ctypes.data for a in self.arrays])
+
+
+class VAEStream:
+    """Streaming AudioVAE V2 decoder (vcpm_vae_stream_*), zeroed history."""
+
+    def __init__(self, cfg: VAEConfig, tensors):
+        self.cfg = cfg
+        self.t = _VAETensors(tensors)
+        self.h = lib().vo_vae_stream_create(C.byref(cfg), self.t.table)
+        assert self.h, "vo_vae_stream_create failed"
+        self.L = lib()
+
+    def decode(self, latent):
+        latent = f32(latent).reshape(-1, self.cfg.latent_dim)
+        n = latent.shape[0]
+        audio = np.zeros(n * self.cfg.upsample(), np.float32)
+        assert self.L.vo_vae_stream_decode(self.h, _p(latent), n, _p(audio)) == 0
+        return audio
+
+    def close(self):
+        if self.h:
+            self.L.vo_vae_stream_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+
+def vae_decode(cfg: VAEConfig, tensors, latent):
+    """Whole-utterance decode (vcpm_vae_v2_decode): latent [n][latent_dim]."""
+    t = _VAETensors(tensors)
+    latent = f32(latent).reshape(-1, cfg.latent_dim)
+    n = latent.shape[0]
+    audio = np.zeros(n * cfg.upsample(), np.float32)
+    assert lib().vo_vae_decode(C.byref(cfg), t.table, _p(latent), n, _p(audio)) == 0
+    return audio

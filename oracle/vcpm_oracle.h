@@ -184,6 +184,58 @@ int vo_round_cache_capacity(int required, int model_max);
 void vo_fill_normal(uint64_t seed, float mean, float stddev, float *x,
                     int64_t n);
 
+/* ---- AudioVAE V2 decoder (vcpm_oracle_vae.c) ------------------------- */
+/* Decoder geometry: latent channels, decoder_dim D (block b maps D>>b to
+ * D>>(b+1) channels, src/audio_vae_v2.c:40-43) and the six upsampling
+ * strides (transposed-conv kernel 2*stride). */
+typedef struct vo_vae_config {
+    int latent_dim;
+    int decoder_dim;
+    int rates[6];
+} vo_vae_config;
+
+/* Tensor slots of the decoder, all F32 in GGUF element order; biases,
+ * Snake alphas and sr_cond vectors are per channel.  Slot names follow
+ * audio_vae.decoder.* in src/audio_vae_stream.c:362-561. */
+enum {
+    VO_VAE_IN_DW_W = 0,    /* model.0.weight.weight  [latent][7] depthwise  */
+    VO_VAE_IN_DW_B = 1,    /* model.0.bias                                    */
+    VO_VAE_IN_PW_W = 2,    /* model.1.weight.weight  [D][latent]             */
+    VO_VAE_IN_PW_B = 3,    /* model.1.bias                                    */
+    VO_VAE_BLOCK0 = 4,     /* first slot of model.2; model.(2+b) at BLOCK0 + b*BLOCK_SLOTS */
+    VO_VAE_BLOCK_SLOTS = 23,
+    VO_VAE_B_SR_SCALE = 0, /* sr_cond_model.(2+b) scale vector [Ci] or NULL   */
+    VO_VAE_B_SR_BIAS = 1,  /* sr_cond_model.(2+b) bias vector  [Ci] or NULL   */
+    VO_VAE_B_ALPHA = 2,    /* block.0.alpha [Ci]                              */
+    VO_VAE_B_UP_W = 3,     /* block.1.weight.weight [Ci][Co][2*stride]        */
+    VO_VAE_B_UP_B = 4,     /* block.1.bias [Co]                               */
+    VO_VAE_B_RES0 = 5,     /* residual unit u (block.(2+u)) at B_RES0 + u*RES_SLOTS */
+    VO_VAE_RES_SLOTS = 6,
+    VO_VAE_R_ALPHA0 = 0,   /* block.0.alpha [Co]                              */
+    VO_VAE_R_DW_W = 1,     /* block.1.weight.weight [Co][7] depthwise         */
+    VO_VAE_R_DW_B = 2,
+    VO_VAE_R_ALPHA2 = 3,   /* block.2.alpha [Co]                              */
+    VO_VAE_R_PW_W = 4,     /* block.3.weight.weight [Co][Co]                  */
+    VO_VAE_R_PW_B = 5,
+    VO_VAE_OUT_ALPHA = 142, /* model.8.alpha [D>>6]                           */
+    VO_VAE_OUT_W = 143,     /* model.9.weight.weight [D>>6][7]               */
+    VO_VAE_OUT_B = 144,     /* model.9.bias [1]                               */
+    VO_VAE_N_SLOTS = 145
+};
+
+typedef struct vo_vae_stream vo_vae_stream;
+int vo_vae_check_config(const vo_vae_config *cfg);
+int vo_vae_upsample(const vo_vae_config *cfg);
+/* Streaming decoder state with zeroed history (vcpm_vae_stream_create);
+ * `w` (VO_VAE_N_SLOTS pointers) must outlive it. */
+vo_vae_stream *vo_vae_stream_create(const vo_vae_config *cfg, const float *const *w);
+void vo_vae_stream_free(vo_vae_stream *s);
+/* latent [n][latent_dim] time-major -> audio [n * upsample] in (-1, 1)
+ * (vcpm_vae_stream_decode, src/audio_vae_stream.c:563-619). */
+int vo_vae_stream_decode(vo_vae_stream *s, const float *latent, int n, float *audio);
+/* Whole-utterance decode (vcpm_vae_v2_decode) = streaming from zero state. */
+int vo_vae_decode(const vo_vae_config *cfg, const float *const *w, const float *latent, int n, float *audio);
+
 #ifdef __cplusplus
 }
 #endif

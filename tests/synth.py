@@ -111,3 +111,40 @@ def assert_layer_close(y, r, tol=1e-3):
     bound = np.abs(r) * 2.0 ** -7 + tol * rms
     worst = float((np.abs(y - r) - bound).max())
     assert worst <= 0, f"element beyond one bf16 ulp: excess {worst:.3e}"
+
+
+def vae_tensors(cfg, sr_cond=False):
+    """Random AudioVAE V2 decoder tensors (oracle slot order, F32, GGUF
+    element order).  Conv weights are scaled by 1/sqrt(fan-in) so the
+    activations keep unit scale through the six blocks; Snake alphas are
+    drawn in [0.5, 1.5] (the activation divides by them)."""
+    L, D, rates = cfg.latent_dim, cfg.decoder_dim, list(cfg.rates)
+    t = [None] * O.VAE_N_SLOTS
+
+    def conv(shape, fan_in):
+        return normal(shape, 1.0 / np.sqrt(fan_in))
+
+    def alpha(n):
+        return (0.5 + np.abs(normal(n, 0.3)) % 1.0).astype(np.float32)
+
+    t[O.VAE_IN_DW_W], t[O.VAE_IN_DW_B] = conv((L, 7), 7), normal(L, 0.02)
+    t[O.VAE_IN_PW_W], t[O.VAE_IN_PW_B] = conv((D, L), L), normal(D, 0.02)
+    for b in range(6):
+        ci, co, s = D >> b, D >> (b + 1), rates[b]
+        if sr_cond:
+            t[O.vae_block_slot(b, O.VAE_B_SR_SCALE)] = normal(ci, 0.1, 1.0)
+            t[O.vae_block_slot(b, O.VAE_B_SR_BIAS)] = normal(ci, 0.05)
+        t[O.vae_block_slot(b, O.VAE_B_ALPHA)] = alpha(ci)
+        t[O.vae_block_slot(b, O.VAE_B_UP_W)] = conv((ci, co, 2 * s), 2 * ci)
+        t[O.vae_block_slot(b, O.VAE_B_UP_B)] = normal(co, 0.02)
+        for u in range(3):
+            t[O.vae_res_slot(b, u, O.VAE_R_ALPHA0)] = alpha(co)
+            t[O.vae_res_slot(b, u, O.VAE_R_DW_W)] = conv((co, 7), 7)
+            t[O.vae_res_slot(b, u, O.VAE_R_DW_B)] = normal(co, 0.02)
+            t[O.vae_res_slot(b, u, O.VAE_R_ALPHA2)] = alpha(co)
+            t[O.vae_res_slot(b, u, O.VAE_R_PW_W)] = conv((co, co), 4 * co)
+            t[O.vae_res_slot(b, u, O.VAE_R_PW_B)] = normal(co, 0.02)
+    cl = D >> 6
+    # output conv scaled down so that tanh stays mostly out of saturation
+    t[O.VAE_OUT_ALPHA], t[O.VAE_OUT_W], t[O.VAE_OUT_B] = alpha(cl), normal((cl, 7), 0.15 / np.sqrt(7 * cl)), normal(1, 0.02)
+    return t

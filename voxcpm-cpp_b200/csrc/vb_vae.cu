@@ -1,0 +1,641 @@
+// vb_vae.cu -- AudioVAE V2 decoder (latent patches -> 48 kHz PCM) as CUDA
+// kernels, streaming over a batch of independent utterances.
+//
+// Reference: the streaming decoder graph of src/audio_vae_stream.c:184-619
+// (per-layer history caches, vcpm_vae_stream_create/reset/decode) and the
+// layer helpers of src/audio_vae_v2.c (causal depthwise / pointwise conv
+// :214-407, transposed conv with causal trim :409-441, Snake :483-503,
+// residual unit :567-636, block table :40-43).
+//
+// Layout: activations are time-major [stream][time][channels] in F32, so a
+// pointwise conv is a GEMM with M = streams x time and K = input channels,
+// and a transposed conv of stride s (kernel 2s) is one GEMM as well: output
+// times q*s .. q*s+s-1 of all channels form one row of s*Co values, computed
+// from the concatenated input rows [x(q-1) | x(q)] (x(-1) = the history
+// cache) against a repacked weight [2*Ci][s*Co].  The GEMM is an fp32 SIMT
+// kernel (the reference decodes in F32; a tensor-core format would not meet
+// the parity bar), with the bias, residual skip, sr_cond scale/bias and the
+// next layer's Snake fused into its epilogue.  Depthwise k7 convs and the
+// final k7 -> tanh conv are bandwidth-bound direct kernels that also roll
+// their history caches (double-buffered, so no launch reads a cache row that
+// the same launch rewrites).
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "vb_common.cuh"
+
+using namespace vb;
+
+namespace {
+
+constexpr int VAE_DIL[3] = {1, 3, 9};
+
+// snake(x, a) = x + sin(a*x)^2 / a, one fp32 op at a time as ggml's
+// mul / sin / sqr / div / add nodes (src/audio_vae_v2.c:483-503).
+__device__ __forceinline__ float snake_f(float x, float a) {
+    const float t = __fmul_rn(x, a);
+    const float st = sinf(t);
+    const float sq = __fmul_rn(st, st);
+    return __fadd_rn(x, __fdiv_rn(sq, a));
+}
+
+__device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ void st4(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
+
+// ----------------------------------------------------------------- GEMM
+struct VaeGemm {
+    const float *A;       // [M][Ka] rows
+    int Ka;
+    const float *prev;    // non-null: K = 2*Ka, k < Ka reads the previous row (prev[stream] for a stream's first row)
+    int T_in;             // rows per stream (for the previous-row rule)
+    const float *B;       // [K][N]
+    int M, N, K;
+    const float *bias;    // [Cb], index n % Cb
+    int Cb;
+    const float *skip;    // [M][N] residual added after the bias (may alias out_h)
+    float *out_h;         // [M][N] value
+    float *out_x;         // [M][N] next layer's input: snake(alpha)(sr(value))
+    const float *alpha, *sr_scale, *sr_bias;   // [Cb] each, optional
+};
+
+constexpr int G_BM = 128, G_BK = 8, G_THREADS = 256;
+
+// Epilogue of one value: bias, skip, then the outputs.
+__device__ __forceinline__ void gemm_out(const VaeGemm &g, int64_t m, int n, float acc) {
+    const int c = n % g.Cb;
+    float v = acc;
+    if (g.bias) v = __fadd_rn(v, g.bias[c]);
+    const int64_t at = m * g.N + n;
+    if (g.skip) v = __fadd_rn(g.skip[at], v);
+    if (g.out_h) g.out_h[at] = v;
+    if (g.out_x) {
+        float u = v;
+        if (g.sr_scale) u = __fadd_rn(__fmul_rn(u, g.sr_scale[c]), g.sr_bias[c]);
+        if (g.alpha) u = snake_f(u, g.alpha[c]);
+        g.out_x[at] = u;
+    }
+}
+
+// The two source rows of logical A row m: columns k < Ka come from `lo`,
+// the rest from `hi` (one row when there is no previous-row part).
+struct ARow {
+    const float *lo, *hi;
+    int split;
+    bool valid;
+};
+
+__device__ __forceinline__ ARow gemm_a_row(const VaeGemm &g, int64_t m) {
+    ARow r;
+    r.valid = m < g.M;
+    const float *cur = g.A + (r.valid ? m : 0) * g.Ka;
+    if (!g.prev) {
+        r.lo = r.hi = cur;
+        r.split = g.K;
+    } else {
+        const int64_t t = r.valid ? m % g.T_in : 0;
+        r.lo = t ? cur - g.Ka : g.prev + (r.valid ? m / g.T_in : 0) * g.Ka;
+        r.hi = cur - g.Ka;      // indexed from k = Ka
+        r.split = g.Ka;
+    }
+    return r;
+}
+
+// A float4 of row r at columns k..k+3 (k % 4 == 0).
+__device__ __forceinline__ float4 gemm_load_a(const VaeGemm &g, const ARow &r, int k) {
+    if (!r.valid || k >= g.K) return make_float4(0.f, 0.f, 0.f, 0.f);
+    return ld4((k < r.split ? r.lo : r.hi) + k);
+}
+
+// C[M][N] = A[M][K] . B[K][N] with the fused epilogue.  128 x BN tile,
+// 256 threads, TM x TN outputs per thread; A staged transposed in shared
+// memory, both operands double-buffered through registers.
+template <int BN, int TM, int TN>
+__global__ void __launch_bounds__(G_THREADS) vae_gemm_kernel(const VaeGemm g) {
+    static_assert((G_BM / TM) * (BN / TN) == G_THREADS, "thread tiling");
+    __shared__ __align__(16) float As[2][G_BK][G_BM + 4];
+    __shared__ __align__(16) float Bs[2][G_BK][BN];
+    const int tid = threadIdx.x;
+    const int tx = tid % (BN / TN), ty = tid / (BN / TN);
+    const int64_t m0 = (int64_t)blockIdx.x * G_BM;
+    const int n0 = blockIdx.y * BN;
+    // loaders: A row tid/2, k quad (tid%2)*4; B k-row tid/(BN/4), column quad
+    const int ar = tid >> 1, ak = (tid & 1) * 4;
+    const bool bload = tid < 2 * BN;
+    const int bk = tid / (BN / 4), bn = (tid % (BN / 4)) * 4;
+
+    float acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; i++)
+#pragma unroll
+        for (int j = 0; j < TN; j++) acc[i][j] = 0.f;
+
+    auto load_b = [&](int k0) -> float4 {
+        const int k = k0 + bk, n = n0 + bn;
+        if (!bload || k >= g.K || n >= g.N) return make_float4(0.f, 0.f, 0.f, 0.f);
+        return ld4(g.B + (int64_t)k * g.N + n);
+    };
+    const ARow arow = gemm_a_row(g, m0 + ar);
+    float4 ra = gemm_load_a(g, arow, ak);
+    float4 rb = load_b(0);
+    const int nk = (g.K + G_BK - 1) / G_BK;
+    int buf = 0;
+    As[0][ak + 0][ar] = ra.x; As[0][ak + 1][ar] = ra.y; As[0][ak + 2][ar] = ra.z; As[0][ak + 3][ar] = ra.w;
+    if (bload) st4(&Bs[0][bk][bn], rb);
+    __syncthreads();
+    for (int kt = 0; kt < nk; kt++) {
+        const bool more = kt + 1 < nk;
+        if (more) {
+            ra = gemm_load_a(g, arow, (kt + 1) * G_BK + ak);
+            rb = load_b((kt + 1) * G_BK);
+        }
+#pragma unroll
+        for (int k = 0; k < G_BK; k++) {
+            float a[TM], b[TN];
+#pragma unroll
+            for (int i = 0; i < TM; i += 4) {
+                const float4 v = *reinterpret_cast<const float4 *>(&As[buf][k][ty * TM + i]);
+                a[i] = v.x; a[i + 1] = v.y; a[i + 2] = v.z; a[i + 3] = v.w;
+            }
+#pragma unroll
+            for (int j = 0; j < TN; j += 4) {
+                const float4 v = *reinterpret_cast<const float4 *>(&Bs[buf][k][tx * TN + j]);
+                b[j] = v.x; b[j + 1] = v.y; b[j + 2] = v.z; b[j + 3] = v.w;
+            }
+#pragma unroll
+            for (int i = 0; i < TM; i++)
+#pragma unroll
+                for (int j = 0; j < TN; j++) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        if (more) {
+            const int nb = buf ^ 1;
+            As[nb][ak + 0][ar] = ra.x; As[nb][ak + 1][ar] = ra.y; As[nb][ak + 2][ar] = ra.z; As[nb][ak + 3][ar] = ra.w;
+            if (bload) st4(&Bs[nb][bk][bn], rb);
+            __syncthreads();
+            buf = nb;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < TM; i++) {
+        const int64_t m = m0 + ty * TM + i;
+        if (m >= g.M) continue;
+#pragma unroll
+        for (int j = 0; j < TN; j++) {
+            const int n = n0 + tx * TN + j;
+            if (n < g.N) gemm_out(g, m, n, acc[i][j]);
+        }
+    }
+}
+
+// ------------------------------------------------------ depthwise conv k7
+// y[b][t][c] = snake(alpha)(sum_j w[j][c] * comb[t + j*d][c] + bias[c]),
+// comb = [history (6d rows); x (T rows)]; rows T .. T+6d-1 of the grid
+// write the new history (the last 6d rows of comb) into cnew.
+__global__ void vae_dw7_kernel(const float *__restrict__ x, const float *__restrict__ cold, float *__restrict__ cnew,
+                               const float *__restrict__ w, const float *__restrict__ bias,
+                               const float *__restrict__ alpha, float *__restrict__ y, int T, int C, int d) {
+    const int C4 = C / 4, L = 6 * d, b = blockIdx.y;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (int64_t)(T + L) * C4) return;
+    const int row = (int)(idx / C4), c = (int)(idx % C4) * 4;
+    const float *xb = x + (int64_t)b * T * C;
+    const float *hb = cold + (int64_t)b * L * C;
+    auto comb = [&](int i) -> const float * { return i < L ? hb + (int64_t)i * C : xb + (int64_t)(i - L) * C; };
+    if (row >= T) {
+        const int r = row - T;
+        st4(cnew + ((int64_t)b * L + r) * C + c, ld4(comb(T + r) + c));
+        return;
+    }
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < 7; j++) {
+        const float4 v = ld4(comb(row + j * d) + c), k = ld4(w + j * C + c);
+        acc.x = fmaf(k.x, v.x, acc.x);
+        acc.y = fmaf(k.y, v.y, acc.y);
+        acc.z = fmaf(k.z, v.z, acc.z);
+        acc.w = fmaf(k.w, v.w, acc.w);
+    }
+    if (bias) {
+        const float4 bb = ld4(bias + c);
+        acc.x = __fadd_rn(acc.x, bb.x); acc.y = __fadd_rn(acc.y, bb.y);
+        acc.z = __fadd_rn(acc.z, bb.z); acc.w = __fadd_rn(acc.w, bb.w);
+    }
+    if (alpha) {
+        const float4 a = ld4(alpha + c);
+        acc.x = snake_f(acc.x, a.x); acc.y = snake_f(acc.y, a.y);
+        acc.z = snake_f(acc.z, a.z); acc.w = snake_f(acc.w, a.w);
+    }
+    st4(y + ((int64_t)b * T + row) * C + c, acc);
+}
+
+// ------------------------------------------- output conv k7, C -> 1, tanh
+// audio[b][t] = tanh(sum_{i,j} w[i][j] * comb[t + j][i] + bias), summed
+// channel-major / tap-minor (im2col order); rows T .. T+5 roll the history.
+__global__ void vae_out7_kernel(const float *__restrict__ x, const float *__restrict__ cold, float *__restrict__ cnew,
+                                const float *__restrict__ w, const float *__restrict__ bias, float *__restrict__ audio,
+                                int T, int C) {
+    const int L = 6, b = blockIdx.y;
+    const int row = blockIdx.x * blockDim.x + threadIdx.x;
+    const float *xb = x + (int64_t)b * T * C;
+    const float *hb = cold + (int64_t)b * L * C;
+    auto comb = [&](int i) -> const float * { return i < L ? hb + (int64_t)i * C : xb + (int64_t)(i - L) * C; };
+    if (row >= T) {
+        if (row < T + L) {
+            const int r = row - T;
+            for (int c = 0; c < C; c += 4) st4(cnew + ((int64_t)b * L + r) * C + c, ld4(comb(T + r) + c));
+        }
+        return;
+    }
+    float acc = 0.f;
+    for (int i = 0; i < C; i++)
+#pragma unroll
+        for (int j = 0; j < 7; j++) acc = fmaf(w[i * 7 + j], comb(row + j)[i], acc);
+    float v = acc;
+    if (bias) v = __fadd_rn(v, bias[0]);
+    audio[(int64_t)b * T + row] = tanhf(v);
+}
+
+// ------------------------------------------------------------ host side
+float host_h2f(uint16_t h) {
+    __half_raw r;
+    r.x = h;
+    return __half2float(__half(r));
+}
+
+}  // namespace
+
+struct VaeResUnit {
+    float *alpha0 = nullptr, *dw_w = nullptr, *dw_b = nullptr, *alpha2 = nullptr, *pw_w = nullptr, *pw_b = nullptr;
+};
+struct VaeBlock {
+    int ci = 0, co = 0, s = 0;
+    float *sr_scale = nullptr, *sr_bias = nullptr, *alpha = nullptr, *up_w = nullptr, *up_b = nullptr;
+    VaeResUnit res[3];
+};
+
+struct vb_vae_s {
+    vb_vae_config cfg{};
+    float *in_dw_w = nullptr, *in_dw_b = nullptr, *in_pw_w = nullptr, *in_pw_b = nullptr;
+    VaeBlock blk[6];
+    float *out_alpha = nullptr, *out_w = nullptr, *out_b = nullptr;
+    std::vector<void *> allocs;
+    size_t device_bytes = 0;
+};
+
+struct vb_vae_stream_s {
+    vb_vae vae = nullptr;
+    int n = 0;                    // streams (utterances) decoded in lockstep
+    int patch_size = 0;
+    int parity = 0;               // which half of each double-buffered history is current
+    float *cache_in[2] = {};      // [n][6][latent]
+    float *cache_up[6] = {};      // [n][Ci]
+    float *cache_res[6][3][2] = {};   // [n][6d][Co]
+    float *cache_out[2] = {};     // [n][6][C_last]
+    std::vector<void *> allocs;
+    size_t state_bytes = 0;
+    float *work = nullptr;        // activations: X0, XA, XB, TB, H
+    size_t work_floats = 0;       // per buffer
+    int work_T = 0;               // latent frames the buffers hold
+};
+
+namespace {
+
+int vae_upsample(const vb_vae_config &c) {
+    int f = 1;
+    for (int i = 0; i < 6; i++) f *= c.rates[i];
+    return f;
+}
+
+// Copies a host tensor of `n` elements (F32, or F16 when `f16`) to F32.
+void to_f32(const void *src, bool f16, size_t n, std::vector<float> &out) {
+    out.resize(n);
+    if (f16) {
+        const uint16_t *h = static_cast<const uint16_t *>(src);
+        for (size_t i = 0; i < n; i++) out[i] = host_h2f(h[i]);
+    } else {
+        memcpy(out.data(), src, n * sizeof(float));
+    }
+}
+
+int upload(vb_ctx *ctx, vb_vae v, const std::vector<float> &h, float **dst) {
+    *dst = nullptr;
+    if (h.empty()) return VB_OK;
+    void *p = nullptr;
+    if (cudaMalloc(&p, h.size() * sizeof(float)) != cudaSuccess)
+        return set_error(ctx, VB_ERR_OOM, "vb_vae_create: device allocation of %zu bytes failed", h.size() * 4);
+    v->allocs.push_back(p);
+    v->device_bytes += h.size() * sizeof(float);
+    VB_CHECK(ctx, cudaMemcpy(p, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice));
+    *dst = static_cast<float *>(p);
+    return VB_OK;
+}
+
+template <int BN, int TM, int TN>
+int launch_gemm_bn(vb_ctx *ctx, const VaeGemm &g) {
+    dim3 grid((unsigned)((g.M + G_BM - 1) / G_BM), (unsigned)((g.N + BN - 1) / BN));
+    vae_gemm_kernel<BN, TM, TN><<<grid, G_THREADS, 0, ctx->stream>>>(g);
+    VB_LAUNCH_CHECK(ctx, "vae_gemm");
+    return VB_OK;
+}
+
+int launch_vae_gemm(vb_ctx *ctx, const VaeGemm &g) {
+    if (g.M <= 0) return VB_OK;
+    if (g.N >= 128) return launch_gemm_bn<128, 8, 8>(ctx, g);
+    if (g.N >= 64) return launch_gemm_bn<64, 8, 4>(ctx, g);
+    return launch_gemm_bn<32, 4, 4>(ctx, g);
+}
+
+int launch_dw7(vb_ctx *ctx, const float *x, const float *cold, float *cnew, const float *w, const float *bias,
+               const float *alpha, float *y, int n, int T, int C, int d) {
+    const int64_t items = (int64_t)(T + 6 * d) * (C / 4);
+    dim3 grid((unsigned)((items + 255) / 256), (unsigned)n);
+    vae_dw7_kernel<<<grid, 256, 0, ctx->stream>>>(x, cold, cnew, w, bias, alpha, y, T, C, d);
+    VB_LAUNCH_CHECK(ctx, "vae_dw7");
+    return VB_OK;
+}
+
+}  // namespace
+
+extern "C" int vb_vae_create(vb_ctx *ctx, const vb_vae_config *cfg, const void *const *t, vb_vae *out) {
+    if (!ctx || !cfg || !t || !out) return VB_ERR_INVALID_ARG;
+    *out = nullptr;
+    const vb_vae_config &c = *cfg;
+    if (c.latent_dim <= 0 || c.latent_dim % 4 || c.decoder_dim <= 0 || c.decoder_dim % 256)
+        return set_error(ctx, VB_ERR_INVALID_ARG,
+                         "vb_vae_create: latent_dim must be a multiple of 4 and decoder_dim of 256");
+    for (int i = 0; i < 6; i++)
+        if (c.rates[i] <= 0 || c.rates[i] > 64) return set_error(ctx, VB_ERR_INVALID_ARG, "vb_vae_create: bad rate");
+    if (c.weight_type != VB_TYPE_F32 && c.weight_type != VB_TYPE_F16)
+        return set_error(ctx, VB_ERR_INVALID_ARG, "vb_vae_create: conv weights must be F32 or F16");
+    if (!t[VB_VAE_IN_DW_W] || !t[VB_VAE_IN_PW_W] || !t[VB_VAE_OUT_W])
+        return set_error(ctx, VB_ERR_INVALID_ARG, "vb_vae_create: missing model.0 / model.1 / model.9 weight");
+    for (int b = 0; b < 6; b++) {
+        const int base = VB_VAE_BLOCK0 + b * VB_VAE_BLOCK_SLOTS;
+        if (!t[base + VB_VAE_B_UP_W])
+            return set_error(ctx, VB_ERR_INVALID_ARG, "vb_vae_create: missing upsample weight of block %d", b);
+        if (!t[base + VB_VAE_B_SR_SCALE] != !t[base + VB_VAE_B_SR_BIAS])
+            return set_error(ctx, VB_ERR_INVALID_ARG, "vb_vae_create: sr_cond scale and bias go together");
+        for (int u = 0; u < 3; u++) {
+            const int rb = base + VB_VAE_B_RES0 + u * VB_VAE_RES_SLOTS;
+            if (!t[rb + VB_VAE_R_DW_W] || !t[rb + VB_VAE_R_PW_W])
+                return set_error(ctx, VB_ERR_INVALID_ARG, "vb_vae_create: missing residual conv of block %d", b);
+        }
+    }
+    if (fault_injected("alloc")) return set_error(ctx, VB_ERR_OOM, "vb_vae_create: injected allocation fault");
+    VB_CHECK(ctx, cudaSetDevice(ctx->device));
+    vb_vae v = new vb_vae_s();
+    v->cfg = c;
+    const bool f16 = c.weight_type == VB_TYPE_F16;
+    const int L = c.latent_dim, D = c.decoder_dim;
+    std::vector<float> a, r;
+    auto vec = [&](const void *p, size_t n, float **dst) -> int {   // per-channel F32 vectors
+        if (!p) { *dst = nullptr; return VB_OK; }
+        to_f32(p, false, n, a);
+        return upload(ctx, v, a, dst);
+    };
+    // depthwise [C][7] -> [7][C]
+    auto dw = [&](const void *p, int C, float **dst) -> int {
+        to_f32(p, f16, (size_t)C * 7, a);
+        r.assign((size_t)C * 7, 0.f);
+        for (int ch = 0; ch < C; ch++)
+            for (int j = 0; j < 7; j++) r[(size_t)j * C + ch] = a[(size_t)ch * 7 + j];
+        return upload(ctx, v, r, dst);
+    };
+    // pointwise [Co][Ci] -> B operand [Ci][Co]
+    auto pw = [&](const void *p, int ci, int co, float **dst) -> int {
+        to_f32(p, f16, (size_t)ci * co, a);
+        r.assign((size_t)ci * co, 0.f);
+        for (int o = 0; o < co; o++)
+            for (int i = 0; i < ci; i++) r[(size_t)i * co + o] = a[(size_t)o * ci + i];
+        return upload(ctx, v, r, dst);
+    };
+    int rc = VB_OK;
+    if (!rc) rc = dw(t[VB_VAE_IN_DW_W], L, &v->in_dw_w);
+    if (!rc) rc = vec(t[VB_VAE_IN_DW_B], L, &v->in_dw_b);
+    if (!rc) rc = pw(t[VB_VAE_IN_PW_W], L, D, &v->in_pw_w);
+    if (!rc) rc = vec(t[VB_VAE_IN_PW_B], D, &v->in_pw_b);
+    for (int b = 0; b < 6 && !rc; b++) {
+        VaeBlock &B = v->blk[b];
+        B.ci = D >> b;
+        B.co = D >> (b + 1);
+        B.s = c.rates[b];
+        const int base = VB_VAE_BLOCK0 + b * VB_VAE_BLOCK_SLOTS, ci = B.ci, co = B.co, s = B.s;
+        rc = vec(t[base + VB_VAE_B_SR_SCALE], ci, &B.sr_scale);
+        if (!rc) rc = vec(t[base + VB_VAE_B_SR_BIAS], ci, &B.sr_bias);
+        if (!rc) rc = vec(t[base + VB_VAE_B_ALPHA], ci, &B.alpha);
+        if (!rc) rc = vec(t[base + VB_VAE_B_UP_B], co, &B.up_b);
+        if (!rc) {
+            // [Ci][Co][2s] -> [2*Ci][s*Co]: rows 0..Ci-1 take the previous
+            // input through taps s..2s-1, rows Ci.. the current one through 0..s-1
+            to_f32(t[base + VB_VAE_B_UP_W], f16, (size_t)ci * co * 2 * s, a);
+            r.assign((size_t)2 * ci * s * co, 0.f);
+            for (int i = 0; i < ci; i++)
+                for (int o = 0; o < co; o++)
+                    for (int q = 0; q < s; q++) {
+                        const size_t src = ((size_t)i * co + o) * 2 * s;
+                        r[(size_t)i * s * co + (size_t)q * co + o] = a[src + s + q];
+                        r[(size_t)(ci + i) * s * co + (size_t)q * co + o] = a[src + q];
+                    }
+            rc = upload(ctx, v, r, &B.up_w);
+        }
+        for (int u = 0; u < 3 && !rc; u++) {
+            const int rb = base + VB_VAE_B_RES0 + u * VB_VAE_RES_SLOTS;
+            VaeResUnit &R = B.res[u];
+            rc = vec(t[rb + VB_VAE_R_ALPHA0], co, &R.alpha0);
+            if (!rc) rc = dw(t[rb + VB_VAE_R_DW_W], co, &R.dw_w);
+            if (!rc) rc = vec(t[rb + VB_VAE_R_DW_B], co, &R.dw_b);
+            if (!rc) rc = vec(t[rb + VB_VAE_R_ALPHA2], co, &R.alpha2);
+            if (!rc) rc = pw(t[rb + VB_VAE_R_PW_W], co, co, &R.pw_w);
+            if (!rc) rc = vec(t[rb + VB_VAE_R_PW_B], co, &R.pw_b);
+        }
+    }
+    const int cl = D >> 6;
+    if (!rc) rc = vec(t[VB_VAE_OUT_ALPHA], cl, &v->out_alpha);
+    if (!rc) {
+        to_f32(t[VB_VAE_OUT_W], f16, (size_t)cl * 7, a);
+        rc = upload(ctx, v, a, &v->out_w);
+    }
+    if (!rc) rc = vec(t[VB_VAE_OUT_B], 1, &v->out_b);
+    if (rc) {
+        vb_vae_destroy(ctx, v);
+        return rc;
+    }
+    *out = v;
+    return VB_OK;
+}
+
+extern "C" void vb_vae_destroy(vb_ctx *ctx, vb_vae v) {
+    if (!v) return;
+    if (ctx) cudaStreamSynchronize(ctx->stream);
+    for (void *p : v->allocs) cudaFree(p);
+    delete v;
+}
+
+extern "C" size_t vb_vae_device_bytes(vb_vae v) { return v ? v->device_bytes : 0; }
+
+extern "C" int vb_vae_stream_create(vb_ctx *ctx, vb_vae v, int n_streams, int patch_size, vb_vae_stream *out) {
+    if (!ctx || !v || !out || n_streams <= 0 || patch_size <= 0) return VB_ERR_INVALID_ARG;
+    *out = nullptr;
+    if (fault_injected("alloc")) return set_error(ctx, VB_ERR_OOM, "vb_vae_stream_create: injected allocation fault");
+    vb_vae_stream s = new vb_vae_stream_s();
+    s->vae = v;
+    s->n = n_streams;
+    s->patch_size = patch_size;
+    const vb_vae_config &c = v->cfg;
+    const int D = c.decoder_dim;
+    auto alloc = [&](size_t floats, float **dst) -> bool {
+        void *p = nullptr;
+        if (cudaMalloc(&p, floats * sizeof(float)) != cudaSuccess) return false;
+        s->allocs.push_back(p);
+        s->state_bytes += floats * sizeof(float);
+        *dst = static_cast<float *>(p);
+        return true;
+    };
+    bool ok = true;
+    for (int h = 0; h < 2; h++) ok = ok && alloc((size_t)n_streams * 6 * c.latent_dim, &s->cache_in[h]);
+    for (int b = 0; b < 6 && ok; b++) {
+        ok = alloc((size_t)n_streams * (D >> b), &s->cache_up[b]);
+        for (int u = 0; u < 3 && ok; u++)
+            for (int h = 0; h < 2 && ok; h++)
+                ok = alloc((size_t)n_streams * 6 * VAE_DIL[u] * (D >> (b + 1)), &s->cache_res[b][u][h]);
+    }
+    for (int h = 0; h < 2 && ok; h++) ok = alloc((size_t)n_streams * 6 * (D >> 6), &s->cache_out[h]);
+    if (!ok) {
+        vb_vae_stream_destroy(ctx, s);
+        return set_error(ctx, VB_ERR_OOM, "vb_vae_stream_create: history allocation failed");
+    }
+    const int rc = vb_vae_stream_reset(ctx, s);
+    if (rc) {
+        vb_vae_stream_destroy(ctx, s);
+        return rc;
+    }
+    *out = s;
+    return VB_OK;
+}
+
+extern "C" int vb_vae_stream_reset(vb_ctx *ctx, vb_vae_stream s) {
+    if (!ctx || !s) return VB_ERR_INVALID_ARG;
+    const vb_vae_config &c = s->vae->cfg;
+    const int D = c.decoder_dim, n = s->n;
+    for (int h = 0; h < 2; h++) {
+        VB_CHECK(ctx, cudaMemsetAsync(s->cache_in[h], 0, sizeof(float) * n * 6 * c.latent_dim, ctx->stream));
+        VB_CHECK(ctx, cudaMemsetAsync(s->cache_out[h], 0, sizeof(float) * n * 6 * (D >> 6), ctx->stream));
+    }
+    for (int b = 0; b < 6; b++) {
+        VB_CHECK(ctx, cudaMemsetAsync(s->cache_up[b], 0, sizeof(float) * n * (D >> b), ctx->stream));
+        for (int u = 0; u < 3; u++)
+            for (int h = 0; h < 2; h++)
+                VB_CHECK(ctx, cudaMemsetAsync(s->cache_res[b][u][h], 0,
+                                              sizeof(float) * n * 6 * VAE_DIL[u] * (D >> (b + 1)), ctx->stream));
+    }
+    s->parity = 0;
+    return VB_OK;
+}
+
+extern "C" void vb_vae_stream_destroy(vb_ctx *ctx, vb_vae_stream s) {
+    if (!s) return;
+    if (ctx) cudaStreamSynchronize(ctx->stream);
+    for (void *p : s->allocs) cudaFree(p);
+    if (s->work) cudaFree(s->work);
+    delete s;
+}
+
+extern "C" int vb_vae_stream_conv_cache_count(vb_vae_stream s) { return s ? 20 : 0; }
+extern "C" int vb_vae_stream_upconv_cache_count(vb_vae_stream s) { return s ? 6 : 0; }
+extern "C" int vb_vae_stream_patch_samples(vb_vae_stream s) {
+    return s ? s->patch_size * vae_upsample(s->vae->cfg) : 0;
+}
+extern "C" size_t vb_vae_stream_state_bytes(vb_vae_stream s) { return s ? s->state_bytes : 0; }
+
+extern "C" int vb_vae_stream_decode(vb_ctx *ctx, vb_vae_stream s, const float *latent, int n_timesteps,
+                                    float *audio) {
+    if (!ctx || !s || !latent || !audio || n_timesteps <= 0) return VB_ERR_INVALID_ARG;
+    if ((reinterpret_cast<uintptr_t>(latent) | reinterpret_cast<uintptr_t>(audio)) % 16)
+        return set_error(ctx, VB_ERR_INVALID_ARG, "vb_vae_stream_decode: latent and audio must be 16-byte aligned");
+    const vb_vae v = s->vae;
+    const vb_vae_config &c = v->cfg;
+    const int n = s->n, L = c.latent_dim, D = c.decoder_dim;
+    // largest activation of one level, per buffer
+    size_t need = (size_t)n * n_timesteps * std::max(L, D);
+    {
+        size_t T = (size_t)n_timesteps;
+        for (int b = 0; b < 6; b++) {
+            T *= c.rates[b];
+            need = std::max(need, (size_t)n * T * (D >> (b + 1)));
+        }
+        if (T * (size_t)n > 0x7fffffffULL) return set_error(ctx, VB_ERR_INVALID_ARG, "vb_vae_stream_decode: too long");
+    }
+    if (need > s->work_floats) {
+        if (s->work) {
+            VB_CHECK(ctx, cudaStreamSynchronize(ctx->stream));
+            cudaFree(s->work);
+            s->work = nullptr;
+            s->work_floats = 0;
+        }
+        void *p = nullptr;
+        if (cudaMalloc(&p, need * 5 * sizeof(float)) != cudaSuccess)
+            return set_error(ctx, VB_ERR_OOM, "vb_vae_stream_decode: %zu bytes of activations", need * 20);
+        s->work = static_cast<float *>(p);
+        s->work_floats = need;
+    }
+    float *X0 = s->work, *XA = X0 + need, *XB = XA + need, *TB = XB + need, *H = TB + need;
+    const int p = s->parity, q = p ^ 1;
+    int rc;
+    // model.0: depthwise k7 over the latent (no Snake before model.1)
+    rc = launch_dw7(ctx, latent, s->cache_in[p], s->cache_in[q], v->in_dw_w, v->in_dw_b, nullptr, X0, n,
+                    n_timesteps, L, 1);
+    if (rc) return rc;
+    // model.1: pointwise L -> D; emits block 0's input: snake(alpha)(sr(h))
+    {
+        VaeGemm g{};
+        g.A = X0; g.Ka = L; g.B = v->in_pw_w; g.M = n * n_timesteps; g.N = D; g.K = L;
+        g.bias = v->in_pw_b; g.Cb = D; g.out_x = XA;
+        g.alpha = v->blk[0].alpha; g.sr_scale = v->blk[0].sr_scale; g.sr_bias = v->blk[0].sr_bias;
+        if ((rc = launch_vae_gemm(ctx, g))) return rc;
+    }
+    int T = n_timesteps;
+    for (int b = 0; b < 6; b++) {
+        const VaeBlock &B = v->blk[b];
+        // transposed conv: rows [x(q-1) | x(q)] -> s output times of Co
+        {
+            VaeGemm g{};
+            g.A = XA; g.Ka = B.ci; g.prev = s->cache_up[b]; g.T_in = T;
+            g.B = B.up_w; g.M = n * T; g.N = B.s * B.co; g.K = 2 * B.ci;
+            g.bias = B.up_b; g.Cb = B.co; g.out_h = H; g.out_x = XB; g.alpha = B.res[0].alpha0;
+            if ((rc = launch_vae_gemm(ctx, g))) return rc;
+        }
+        // its history: the last (Snake-activated) input row of every stream
+        VB_CHECK(ctx, cudaMemcpy2DAsync(s->cache_up[b], sizeof(float) * B.ci, XA + (size_t)(T - 1) * B.ci,
+                                        sizeof(float) * T * B.ci, sizeof(float) * B.ci, n, cudaMemcpyDeviceToDevice,
+                                        ctx->stream));
+        T *= B.s;
+        for (int u = 0; u < 3; u++) {
+            const VaeResUnit &R = B.res[u];
+            rc = launch_dw7(ctx, XB, s->cache_res[b][u][p], s->cache_res[b][u][q], R.dw_w, R.dw_b, R.alpha2, TB, n,
+                            T, B.co, VAE_DIL[u]);
+            if (rc) return rc;
+            VaeGemm g{};
+            g.A = TB; g.Ka = B.co; g.B = R.pw_w; g.M = n * T; g.N = B.co; g.K = B.co;
+            g.bias = R.pw_b; g.Cb = B.co; g.skip = H;
+            if (u < 2) {            // skip of the next unit, and its Snake input
+                g.out_h = H; g.out_x = XB; g.alpha = B.res[u + 1].alpha0;
+            } else if (b < 5) {     // next block's sr_cond + Snake input
+                g.out_x = XA; g.alpha = v->blk[b + 1].alpha;
+                g.sr_scale = v->blk[b + 1].sr_scale; g.sr_bias = v->blk[b + 1].sr_bias;
+            } else {                // model.8 Snake before the output conv
+                g.out_x = XA; g.alpha = v->out_alpha;
+            }
+            if ((rc = launch_vae_gemm(ctx, g))) return rc;
+        }
+    }
+    // model.9 + tanh
+    {
+        const int C = D >> 6;
+        dim3 grid((unsigned)((T + 6 + 127) / 128), (unsigned)n);
+        vae_out7_kernel<<<grid, 128, 0, ctx->stream>>>(XA, s->cache_out[p], s->cache_out[q], v->out_w, v->out_b, audio,
+                                                       T, C);
+        VB_LAUNCH_CHECK(ctx, "vae_out7");
+    }
+    s->parity = q;
+    return VB_OK;
+}

@@ -13,6 +13,8 @@ from __future__ import annotations
 import ctypes as C
 import os
 
+import numpy as np
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libvcpm_b200.so")
 
@@ -138,6 +140,17 @@ SIGNATURES = {
     "vb_gen_prefill": (_I, [_P, _P, _I, _P]),
     "vb_gen_step": (_I, [_P, _P, C.c_uint64, _P, _P]),
     "vb_gen_destroy": (None, [_P, _P]),
+    "vb_vae_create": (_I, [_P, _P, _P, C.POINTER(_P)]),
+    "vb_vae_destroy": (None, [_P, _P]),
+    "vb_vae_device_bytes": (_SZ, [_P]),
+    "vb_vae_stream_create": (_I, [_P, _P, _I, _I, C.POINTER(_P)]),
+    "vb_vae_stream_reset": (_I, [_P, _P]),
+    "vb_vae_stream_decode": (_I, [_P, _P, _P, _I, _P]),
+    "vb_vae_stream_destroy": (None, [_P, _P]),
+    "vb_vae_stream_conv_cache_count": (_I, [_P]),
+    "vb_vae_stream_upconv_cache_count": (_I, [_P]),
+    "vb_vae_stream_patch_samples": (_I, [_P]),
+    "vb_vae_stream_state_bytes": (_SZ, [_P]),
     "vb_cfm_sway_t_bf16": (_F, [_I, _I]),
     "vb_cfm_zero_star_steps": (_I, [_I]),
     "vb_cfm_noise": (None, [C.c_uint64, _I, _P, _I]),
@@ -467,6 +480,77 @@ class Gen:
     def close(self):
         if self.h:
             self.ctx.L.vb_gen_destroy(self.ctx.h, self.h)
+            self.h = C.c_void_p()
+
+
+class VAEConfig(C.Structure):
+    """vb_vae_config: latent channels, decoder width, six strides, conv weight type."""
+    _fields_ = [("latent_dim", C.c_int), ("decoder_dim", C.c_int), ("rates", C.c_int * 6), ("weight_type", C.c_int)]
+
+    def __init__(self, latent_dim=64, decoder_dim=2048, rates=(8, 6, 5, 2, 2, 2), weight_type=TYPE_F32):
+        super().__init__(latent_dim, decoder_dim, (C.c_int * 6)(*rates), weight_type)
+
+    def upsample(self):
+        f = 1
+        for r in self.rates:
+            f *= r
+        return f
+
+
+VAE_N_SLOTS = 145
+
+
+class VAE:
+    """AudioVAE V2 decoder (vb_vae): tensors = list of VAE_N_SLOTS host
+    numpy arrays (or None) in GGUF element order, conv weights as float32
+    or float16 per cfg.weight_type, the rest float32."""
+
+    def __init__(self, ctx: Context, cfg: VAEConfig, tensors):
+        assert len(tensors) == VAE_N_SLOTS
+        self.ctx, self.cfg = ctx, cfg
+        self._keep = [None if t is None else np.ascontiguousarray(t) for t in tensors]
+        table = (C.c_void_p * VAE_N_SLOTS)(*[None if t is None else t.ctypes.data for t in self._keep])
+        self.h = C.c_void_p()
+        ctx.check(ctx.L.vb_vae_create(ctx.h, C.byref(cfg), table, C.byref(self.h)))
+        self._keep = None      # uploaded
+
+    def device_bytes(self):
+        return self.ctx.L.vb_vae_device_bytes(self.h)
+
+    def stream(self, n_streams, patch_size=4):
+        return VAEStream(self, n_streams, patch_size)
+
+    def close(self):
+        if self.h:
+            self.ctx.L.vb_vae_destroy(self.ctx.h, self.h)
+            self.h = C.c_void_p()
+
+
+class VAEStream:
+    """History caches of n_streams utterances (vb_vae_stream)."""
+
+    def __init__(self, vae: VAE, n_streams, patch_size=4):
+        self.ctx, self.vae, self.n = vae.ctx, vae, n_streams
+        self.h = C.c_void_p()
+        self.ctx.check(self.ctx.L.vb_vae_stream_create(self.ctx.h, vae.h, n_streams, patch_size, C.byref(self.h)))
+
+    def decode(self, latent, n_timesteps, audio):
+        """latent: device [n][T][latent_dim]; audio: device [n][T * upsample]."""
+        self.ctx.check(self.ctx.L.vb_vae_stream_decode(self.ctx.h, self.h, _addr(latent), n_timesteps, _addr(audio)))
+
+    def reset(self):
+        self.ctx.check(self.ctx.L.vb_vae_stream_reset(self.ctx.h, self.h))
+
+    def info(self):
+        L = self.ctx.L
+        return dict(conv_caches=L.vb_vae_stream_conv_cache_count(self.h),
+                    upconv_caches=L.vb_vae_stream_upconv_cache_count(self.h),
+                    patch_samples=L.vb_vae_stream_patch_samples(self.h),
+                    state_bytes=L.vb_vae_stream_state_bytes(self.h))
+
+    def close(self):
+        if self.h:
+            self.ctx.L.vb_vae_stream_destroy(self.ctx.h, self.h)
             self.h = C.c_void_p()
 
 
