@@ -547,6 +547,39 @@ def run_gemm_case(args, local_rank):
     return 0 if rc == 0 else 1
 
 
+def run_vae_case(args, local_rank):
+    """Profiling case: the AudioVAE V2 streaming decoder alone (vb_vae) on
+    e2e_utts streams, one 4-frame patch per decode; warmup + steps patches.
+    Prints ms per patch and the fp32 flop rate."""
+    import torch
+    import vcpm_b200 as vb
+    torch.cuda.set_device(local_rank)
+    ctx = vb.Context(local_rank)
+    rng = np.random.default_rng(9)
+    B = args.e2e_utts
+    vae = vb.VAE(ctx, vb.VAEConfig(VAE_LATENT, VAE_DIM, VAE_RATES, vb.TYPE_F32), synth_vae(rng))
+    st = vae.stream(B, PATCH)
+    lat = torch.randn(B, PATCH, VAE_LATENT, device="cuda")
+    audio = torch.zeros(B, SAMPLES_PER_PATCH, device="cuda")
+    for _ in range(args.warmup):
+        st.decode(lat, PATCH, audio)
+    ev0, ev1 = ctx.event(), ctx.event()
+    ctx.record(ev0)
+    for _ in range(args.steps):
+        st.decode(lat, PATCH, audio)
+    ctx.record(ev1)
+    ctx.sync()
+    ms = ctx.elapsed_ms(ev0, ev1) / args.steps
+    tf = vae_flops(B * PATCH) / (ms * 1e-3) / 1e12
+    print(json.dumps({"mode": "vae", "streams": B, "ms_per_patch": ms, "tflops": tf,
+                      "frac_of_fp32_nominal": tf / FP32_SIMT_NOMINAL_TFLOPS,
+                      "finite": bool(torch.isfinite(audio).all().item())}), flush=True)
+    st.close()
+    vae.close()
+    ctx.close()
+    return 0
+
+
 def run_decode_case(args, local_rank):
     """Profiling case: the 28-layer decode step (vb_decoder_step, one
     persistent launch per token) after a 256-token prefill; warmup + steps
@@ -821,7 +854,7 @@ def e2e_bench(ctx, host_layers, args, rank, world, gpu_index=0):
     vev = [ctx.event() for _ in range(2)]
     ctx.record(vev[0])
     for s in range(10):
-        vst.decode(patches[s], PATCH, audio[s])
+        vst.decode(patches[s % NP], PATCH, audio[s % NP])
     ctx.record(vev[1])
     ctx.sync()
     vae_ms = ctx.elapsed_ms(vev[0], vev[1]) / 10
@@ -871,7 +904,7 @@ def main():
     ap.add_argument("--e2e-utts", type=int, default=64)
     ap.add_argument("--e2e-patches", type=int, default=100)
     ap.add_argument("--e2e-clock-ms", type=int, default=500, help="nvidia-smi sampling period during the e2e run")
-    ap.add_argument("--mode", default="full", choices=["full", "config1", "gemm", "decode"],
+    ap.add_argument("--mode", default="full", choices=["full", "config1", "gemm", "decode", "vae"],
                     help="config1 / gemm / decode: small profiling cases (config-1 streaming program, one "
                          "tensor-core mat-mul shape, the single-launch decode step)")
     ap.add_argument("--gemm-shape", default="1408,1024,8192")
@@ -889,6 +922,8 @@ def main():
         return run_config1(args, local_rank)
     if args.mode == "gemm":
         return run_gemm_case(args, local_rank)
+    if args.mode == "vae":
+        return run_vae_case(args, local_rank)
     if args.mode == "decode":
         return run_decode_case(args, local_rank)
     if world > 1:

@@ -59,25 +59,41 @@ struct VaeGemm {
     const float *alpha, *sr_scale, *sr_bias;   // [Cb] each, optional
 };
 
-constexpr int G_BM = 128, G_BK = 8, G_THREADS = 256;
+constexpr int G_BK = 8, G_THREADS = 256;
 
-// Epilogue of one value: bias, skip, then the outputs.
-__device__ __forceinline__ void gemm_out(const VaeGemm &g, int64_t m, int n, float acc) {
+// Epilogue of four consecutive values (n % 4 == 0, N % 4 == 0, Cb % 4 == 0):
+// bias, skip, then the outputs; every op one fp32 rounding, as ggml's nodes.
+__device__ __forceinline__ void gemm_out4(const VaeGemm &g, int64_t m, int n, float4 acc) {
     const int c = n % g.Cb;
-    float v = acc;
-    if (g.bias) v = __fadd_rn(v, g.bias[c]);
+    float v[4] = {acc.x, acc.y, acc.z, acc.w};
+    if (g.bias) {
+        const float4 b = ld4(g.bias + c);
+        v[0] = __fadd_rn(v[0], b.x); v[1] = __fadd_rn(v[1], b.y);
+        v[2] = __fadd_rn(v[2], b.z); v[3] = __fadd_rn(v[3], b.w);
+    }
     const int64_t at = m * g.N + n;
-    if (g.skip) v = __fadd_rn(g.skip[at], v);
-    if (g.out_h) g.out_h[at] = v;
+    if (g.skip) {
+        const float4 k = ld4(g.skip + at);
+        v[0] = __fadd_rn(k.x, v[0]); v[1] = __fadd_rn(k.y, v[1]);
+        v[2] = __fadd_rn(k.z, v[2]); v[3] = __fadd_rn(k.w, v[3]);
+    }
+    if (g.out_h) st4(g.out_h + at, make_float4(v[0], v[1], v[2], v[3]));
     if (g.out_x) {
-        float u = v;
-        if (g.sr_scale) u = __fadd_rn(__fmul_rn(u, g.sr_scale[c]), g.sr_bias[c]);
-        if (g.alpha) u = snake_f(u, g.alpha[c]);
-        g.out_x[at] = u;
+        if (g.sr_scale) {
+            const float4 a = ld4(g.sr_scale + c), b = ld4(g.sr_bias + c);
+            v[0] = __fadd_rn(__fmul_rn(v[0], a.x), b.x); v[1] = __fadd_rn(__fmul_rn(v[1], a.y), b.y);
+            v[2] = __fadd_rn(__fmul_rn(v[2], a.z), b.z); v[3] = __fadd_rn(__fmul_rn(v[3], a.w), b.w);
+        }
+        if (g.alpha) {
+            const float4 a = ld4(g.alpha + c);
+            v[0] = snake_f(v[0], a.x); v[1] = snake_f(v[1], a.y);
+            v[2] = snake_f(v[2], a.z); v[3] = snake_f(v[3], a.w);
+        }
+        st4(g.out_x + at, make_float4(v[0], v[1], v[2], v[3]));
     }
 }
 
-// The two source rows of logical A row m: columns k < Ka come from `lo`,
+// The two source rows of logical A row m: columns k < split come from `lo`,
 // the rest from `hi` (one row when there is no previous-row part).
 struct ARow {
     const float *lo, *hi;
@@ -107,22 +123,30 @@ __device__ __forceinline__ float4 gemm_load_a(const VaeGemm &g, const ARow &r, i
     return ld4((k < r.split ? r.lo : r.hi) + k);
 }
 
-// C[M][N] = A[M][K] . B[K][N] with the fused epilogue.  128 x BN tile,
-// 256 threads, TM x TN outputs per thread; A staged transposed in shared
-// memory, both operands double-buffered through registers.
-template <int BN, int TM, int TN>
-__global__ void __launch_bounds__(G_THREADS) vae_gemm_kernel(const VaeGemm g) {
-    static_assert((G_BM / TM) * (BN / TN) == G_THREADS, "thread tiling");
-    __shared__ __align__(16) float As[2][G_BK][G_BM + 4];
+// C[M][N] = A[M][K] . B[K][N] with the fused epilogue.  BM x BN tile, 256
+// threads, TM x TN outputs per thread: rows ty*TM.., columns in TN/4 groups
+// of four at g*(BN/G) + tx*4, so that a quarter-warp's shared-memory reads
+// and global stores of B / C cover one contiguous span.  A is staged
+// transposed in shared memory; both operands are double-buffered through
+// registers.  Each output accumulates over k in order with fmaf.
+template <int BM, int BN, int TM, int TN>
+__global__ void __launch_bounds__(G_THREADS, 2) vae_gemm_kernel(const VaeGemm g) {
+    constexpr int TX = BN / (TN / 4) / 4;     // threads along N per column group
+    constexpr int G = TN / 4;                 // column groups per thread
+    static_assert((BM / TM) * TX == G_THREADS, "thread tiling");
+    static_assert(TM % 4 == 0 && TN % 4 == 0, "vector widths");
+    __shared__ __align__(16) float As[2][G_BK][BM + 4];
     __shared__ __align__(16) float Bs[2][G_BK][BN];
     const int tid = threadIdx.x;
-    const int tx = tid % (BN / TN), ty = tid / (BN / TN);
-    const int64_t m0 = (int64_t)blockIdx.x * G_BM;
+    const int tx = tid % TX, ty = tid / TX;
+    const int64_t m0 = (int64_t)blockIdx.x * BM;
     const int n0 = blockIdx.y * BN;
-    // loaders: A row tid/2, k quad (tid%2)*4; B k-row tid/(BN/4), column quad
-    const int ar = tid >> 1, ak = (tid & 1) * 4;
+    // loaders: A row tid/2, k quad (tid%2)*4 (BM*2 threads); B k-row
+    // tid/(BN/4), column quad (BN*2 threads)
+    const bool aload = tid < BM * 2;
+    const int ar = (tid >> 1) % BM, ak = (tid & 1) * 4;
     const bool bload = tid < 2 * BN;
-    const int bk = tid / (BN / 4), bn = (tid % (BN / 4)) * 4;
+    const int bk = (tid / (BN / 4)) % G_BK, bn = (tid % (BN / 4)) * 4;
 
     float acc[TM][TN];
 #pragma unroll
@@ -136,17 +160,19 @@ __global__ void __launch_bounds__(G_THREADS) vae_gemm_kernel(const VaeGemm g) {
         return ld4(g.B + (int64_t)k * g.N + n);
     };
     const ARow arow = gemm_a_row(g, m0 + ar);
-    float4 ra = gemm_load_a(g, arow, ak);
+    float4 ra = aload ? gemm_load_a(g, arow, ak) : make_float4(0.f, 0.f, 0.f, 0.f);
     float4 rb = load_b(0);
     const int nk = (g.K + G_BK - 1) / G_BK;
     int buf = 0;
-    As[0][ak + 0][ar] = ra.x; As[0][ak + 1][ar] = ra.y; As[0][ak + 2][ar] = ra.z; As[0][ak + 3][ar] = ra.w;
+    if (aload) {
+        As[0][ak + 0][ar] = ra.x; As[0][ak + 1][ar] = ra.y; As[0][ak + 2][ar] = ra.z; As[0][ak + 3][ar] = ra.w;
+    }
     if (bload) st4(&Bs[0][bk][bn], rb);
     __syncthreads();
     for (int kt = 0; kt < nk; kt++) {
         const bool more = kt + 1 < nk;
         if (more) {
-            ra = gemm_load_a(g, arow, (kt + 1) * G_BK + ak);
+            if (aload) ra = gemm_load_a(g, arow, (kt + 1) * G_BK + ak);
             rb = load_b((kt + 1) * G_BK);
         }
 #pragma unroll
@@ -158,9 +184,9 @@ __global__ void __launch_bounds__(G_THREADS) vae_gemm_kernel(const VaeGemm g) {
                 a[i] = v.x; a[i + 1] = v.y; a[i + 2] = v.z; a[i + 3] = v.w;
             }
 #pragma unroll
-            for (int j = 0; j < TN; j += 4) {
-                const float4 v = *reinterpret_cast<const float4 *>(&Bs[buf][k][tx * TN + j]);
-                b[j] = v.x; b[j + 1] = v.y; b[j + 2] = v.z; b[j + 3] = v.w;
+            for (int q = 0; q < G; q++) {
+                const float4 v = *reinterpret_cast<const float4 *>(&Bs[buf][k][q * (BN / G) + tx * 4]);
+                b[4 * q] = v.x; b[4 * q + 1] = v.y; b[4 * q + 2] = v.z; b[4 * q + 3] = v.w;
             }
 #pragma unroll
             for (int i = 0; i < TM; i++)
@@ -169,7 +195,9 @@ __global__ void __launch_bounds__(G_THREADS) vae_gemm_kernel(const VaeGemm g) {
         }
         if (more) {
             const int nb = buf ^ 1;
-            As[nb][ak + 0][ar] = ra.x; As[nb][ak + 1][ar] = ra.y; As[nb][ak + 2][ar] = ra.z; As[nb][ak + 3][ar] = ra.w;
+            if (aload) {
+                As[nb][ak + 0][ar] = ra.x; As[nb][ak + 1][ar] = ra.y; As[nb][ak + 2][ar] = ra.z; As[nb][ak + 3][ar] = ra.w;
+            }
             if (bload) st4(&Bs[nb][bk][bn], rb);
             __syncthreads();
             buf = nb;
@@ -180,9 +208,10 @@ __global__ void __launch_bounds__(G_THREADS) vae_gemm_kernel(const VaeGemm g) {
         const int64_t m = m0 + ty * TM + i;
         if (m >= g.M) continue;
 #pragma unroll
-        for (int j = 0; j < TN; j++) {
-            const int n = n0 + tx * TN + j;
-            if (n < g.N) gemm_out(g, m, n, acc[i][j]);
+        for (int q = 0; q < G; q++) {
+            const int n = n0 + q * (BN / G) + tx * 4;
+            if (n < g.N)
+                gemm_out4(g, m, n, make_float4(acc[i][4 * q], acc[i][4 * q + 1], acc[i][4 * q + 2], acc[i][4 * q + 3]));
         }
     }
 }
@@ -230,29 +259,47 @@ __global__ void vae_dw7_kernel(const float *__restrict__ x, const float *__restr
 
 // ------------------------------------------- output conv k7, C -> 1, tanh
 // audio[b][t] = tanh(sum_{i,j} w[i][j] * comb[t + j][i] + bias), summed
-// channel-major / tap-minor (im2col order); rows T .. T+5 roll the history.
-__global__ void vae_out7_kernel(const float *__restrict__ x, const float *__restrict__ cold, float *__restrict__ cnew,
-                                const float *__restrict__ w, const float *__restrict__ bias, float *__restrict__ audio,
-                                int T, int C) {
-    const int L = 6, b = blockIdx.y;
-    const int row = blockIdx.x * blockDim.x + threadIdx.x;
+// channel-major / tap-minor (im2col order).  A CTA stages the OUT7_T + 6
+// history/input rows it needs in shared memory (row stride C + 1: the
+// per-thread row reads then hit distinct banks) and each thread computes
+// one sample; the CTA holding the stream's last samples also rolls the
+// history (the last 6 rows of comb).
+constexpr int OUT7_T = 128;
+
+__global__ void __launch_bounds__(OUT7_T) vae_out7_kernel(const float *__restrict__ x, const float *__restrict__ cold,
+                                                           float *__restrict__ cnew, const float *__restrict__ w,
+                                                           const float *__restrict__ bias, float *__restrict__ audio,
+                                                           int T, int C) {
+    extern __shared__ float o7[];          // [OUT7_T + 6][C + 1], then w [C][7]
+    const int L = 6, b = blockIdx.y, t0 = blockIdx.x * OUT7_T;
+    const int CS = C + 1;
+    float *ws = o7 + (OUT7_T + L) * CS;
     const float *xb = x + (int64_t)b * T * C;
     const float *hb = cold + (int64_t)b * L * C;
     auto comb = [&](int i) -> const float * { return i < L ? hb + (int64_t)i * C : xb + (int64_t)(i - L) * C; };
-    if (row >= T) {
-        if (row < T + L) {
-            const int r = row - T;
-            for (int c = 0; c < C; c += 4) st4(cnew + ((int64_t)b * L + r) * C + c, ld4(comb(T + r) + c));
-        }
-        return;
+    const int rows = min(OUT7_T + L, T + L - t0);
+    for (int e = threadIdx.x; e < rows * C; e += OUT7_T) {
+        const int r = e / C, c = e - r * C;
+        o7[r * CS + c] = comb(t0 + r)[c];
     }
-    float acc = 0.f;
-    for (int i = 0; i < C; i++)
+    for (int e = threadIdx.x; e < C * 7; e += OUT7_T) ws[e] = w[e];
+    __syncthreads();
+    const int t = t0 + threadIdx.x;
+    if (t < T) {
+        float acc = 0.f;
+        for (int i = 0; i < C; i++)
 #pragma unroll
-        for (int j = 0; j < 7; j++) acc = fmaf(w[i * 7 + j], comb(row + j)[i], acc);
-    float v = acc;
-    if (bias) v = __fadd_rn(v, bias[0]);
-    audio[(int64_t)b * T + row] = tanhf(v);
+            for (int j = 0; j < 7; j++) acc = fmaf(ws[i * 7 + j], o7[(threadIdx.x + j) * CS + i], acc);
+        float v = acc;
+        if (bias) v = __fadd_rn(v, bias[0]);
+        audio[(int64_t)b * T + t] = tanhf(v);
+    }
+    if (t0 + OUT7_T >= T) {        // this CTA covers the stream's end: new history = comb[T .. T+5]
+        for (int e = threadIdx.x; e < L * C; e += OUT7_T) {
+            const int r = e / C, c = e - r * C;
+            cnew[((int64_t)b * L + r) * C + c] = comb(T + r)[c];
+        }
+    }
 }
 
 // ------------------------------------------------------------ host side
@@ -330,19 +377,24 @@ int upload(vb_ctx *ctx, vb_vae v, const std::vector<float> &h, float **dst) {
     return VB_OK;
 }
 
-template <int BN, int TM, int TN>
-int launch_gemm_bn(vb_ctx *ctx, const VaeGemm &g) {
-    dim3 grid((unsigned)((g.M + G_BM - 1) / G_BM), (unsigned)((g.N + BN - 1) / BN));
-    vae_gemm_kernel<BN, TM, TN><<<grid, G_THREADS, 0, ctx->stream>>>(g);
+template <int BM, int BN, int TM, int TN>
+int launch_gemm_tile(vb_ctx *ctx, const VaeGemm &g) {
+    dim3 grid((unsigned)((g.M + BM - 1) / BM), (unsigned)((g.N + BN - 1) / BN));
+    vae_gemm_kernel<BM, BN, TM, TN><<<grid, G_THREADS, 0, ctx->stream>>>(g);
     VB_LAUNCH_CHECK(ctx, "vae_gemm");
     return VB_OK;
 }
 
+// Widest N tile the shape fills; 64-row tiles when 128-row ones would give
+// fewer than two CTAs per SM.
 int launch_vae_gemm(vb_ctx *ctx, const VaeGemm &g) {
     if (g.M <= 0) return VB_OK;
-    if (g.N >= 128) return launch_gemm_bn<128, 8, 8>(ctx, g);
-    if (g.N >= 64) return launch_gemm_bn<64, 8, 4>(ctx, g);
-    return launch_gemm_bn<32, 4, 4>(ctx, g);
+    const int64_t bn = g.N >= 128 ? 128 : (g.N >= 64 ? 64 : 32);
+    const int64_t tiles128 = (g.M + 127) / 128 * ((g.N + bn - 1) / bn);
+    const bool small = tiles128 < 2 * (int64_t)ctx->sm_count;
+    if (bn == 128) return small ? launch_gemm_tile<64, 128, 4, 8>(ctx, g) : launch_gemm_tile<128, 128, 8, 8>(ctx, g);
+    if (bn == 64) return small ? launch_gemm_tile<64, 64, 4, 4>(ctx, g) : launch_gemm_tile<128, 64, 8, 4>(ctx, g);
+    return launch_gemm_tile<128, 32, 4, 4>(ctx, g);
 }
 
 int launch_dw7(vb_ctx *ctx, const float *x, const float *cold, float *cnew, const float *w, const float *bias,
@@ -631,9 +683,11 @@ extern "C" int vb_vae_stream_decode(vb_ctx *ctx, vb_vae_stream s, const float *l
     // model.9 + tanh
     {
         const int C = D >> 6;
-        dim3 grid((unsigned)((T + 6 + 127) / 128), (unsigned)n);
-        vae_out7_kernel<<<grid, 128, 0, ctx->stream>>>(XA, s->cache_out[p], s->cache_out[q], v->out_w, v->out_b, audio,
-                                                       T, C);
+        const size_t smem = sizeof(float) * ((size_t)(OUT7_T + 6) * (C + 1) + (size_t)C * 7);
+        if (smem > 48 * 1024) return set_error(ctx, VB_ERR_INVALID_ARG, "vb_vae_stream_decode: output conv too wide");
+        dim3 grid((unsigned)((T + OUT7_T - 1) / OUT7_T), (unsigned)n);
+        vae_out7_kernel<<<grid, OUT7_T, smem, ctx->stream>>>(XA, s->cache_out[p], s->cache_out[q], v->out_w, v->out_b,
+                                                             audio, T, C);
         VB_LAUNCH_CHECK(ctx, "vae_out7");
     }
     s->parity = q;
