@@ -83,7 +83,11 @@ def vb_cfg(cfg, wtype=vb.TYPE_F32):
 
 
 @pytest.mark.parametrize("sr_cond", [False, True])
-def test_vae_small_streaming_matches_oracle(ctx, sr_cond):
+@pytest.mark.parametrize("tf32", ["1", "0"])
+def test_vae_small_streaming_matches_oracle(ctx, sr_cond, tf32, monkeypatch):
+    """tf32 "1": the 128+-channel convs on the tensor cores (three tf32
+    products), the rest SIMT; "0": fp32 SIMT everywhere (VB_VAE_TF32=0)."""
+    monkeypatch.setenv("VB_VAE_TF32", tf32)
     cfg = O.VAEConfig(**SMALL)
     t = S.vae_tensors(cfg, sr_cond)
     vae = vb.VAE(ctx, vb_cfg(cfg), t)
@@ -99,9 +103,11 @@ def test_vae_small_streaming_matches_oracle(ctx, sr_cond):
     vae.close()
 
 
-def test_vae_full_width_patch_matches_oracle(ctx):
+@pytest.mark.parametrize("tf32", ["1", "0"])
+def test_vae_full_width_patch_matches_oracle(ctx, tf32, monkeypatch):
     """The VoxCPM2 decoder geometry (2048 -> 32 channels, strides 8,6,5,2,2,2):
     two utterances, two 4-frame patches each (7680 samples per patch)."""
+    monkeypatch.setenv("VB_VAE_TF32", tf32)
     cfg = O.VAEConfig()
     t = S.vae_tensors(cfg)
     vae = vb.VAE(ctx, vb_cfg(cfg), t)

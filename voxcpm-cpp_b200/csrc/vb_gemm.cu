@@ -50,6 +50,8 @@ constexpr int GM_SMEM_BUDGET = 220 * 1024;
 
 struct GemmArgs {
     int q8;                 // 1: Q8_0 weights (hi/lo split), 0: F16 weights
+    int tf32;               // 1: fp32 operands pre-split into tf32 hi/lo, three kind::tf32 MMAs
+    int bk;                 // k elements per stage (64 fp16 / 32 tf32: one 128-byte swizzle row)
     int K, N, M, BN;
     int kt_total, kt_per_split, splits, tiles_m, tiles_n;
     int n_tma, n_conv;      // pipeline depths
@@ -66,6 +68,13 @@ struct GemmArgs {
     int Mp;                 // tiles_m * BN
     unsigned *cnt;          // per-tile arrival counters (self-resetting)
     int *err;
+    // AudioVAE epilogue (vae != 0): v = acc + bias[n % cb] (+ skip); y = v
+    // (if y); out_x = snake(alpha)(sr(v)) (if out_x)
+    int vae, cb;
+    uint32_t small_off;     // tf32: TMEM column offset of the cross-term accumulator (hi*lo + lo*hi)
+    const float *skip;
+    float *out_x;
+    const float *alpha, *sr_scale, *sr_bias;
 };
 
 __device__ __forceinline__ uint64_t sw128_desc(const void *p) {
@@ -89,6 +98,14 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem, uint64_t a, uint64_t b, 
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
         "l"(a), "l"(b), "r"(idesc), "r"(acc)
         : "memory");
 }
@@ -150,9 +167,58 @@ __device__ __forceinline__ void gm_store16(const GemmArgs &a, int m0, int n, con
     }
 }
 
+// snake(x, a) = x + sin(a*x)^2 / a, one fp32 op at a time (the AudioVAE
+// activation, src/audio_vae_v2.c:483-503).
+__device__ __forceinline__ float gm_snake(float x, float al) {
+    const float t = __fmul_rn(x, al);
+    const float st = sinf(t);
+    return __fadd_rn(x, __fdiv_rn(__fmul_rn(st, st), al));
+}
+
+// AudioVAE epilogue of 16 outputs (activation rows m0 .. m0+15, output
+// channel n): bias, residual skip, the value, and the next layer's input.
+// Every skip row is loaded before any store (the skip may alias y).
+__device__ __forceinline__ void gm_store16_vae(const GemmArgs &a, int m0, int n, const float *acc) {
+    const int c = n % a.cb;
+    float r[16];
+    if (a.skip) {
+#pragma unroll
+        for (int cc = 0; cc < 16; cc++) r[cc] = __ldcg(a.skip + (int64_t)min(m0 + cc, a.M - 1) * a.ldy + n);
+    }
+    const float b = a.bias ? a.bias[c] : 0.0f;
+    const float al = a.alpha ? a.alpha[c] : 1.0f;
+    const float ss = a.sr_scale ? a.sr_scale[c] : 1.0f, sb = a.sr_scale ? a.sr_bias[c] : 0.0f;
+#pragma unroll
+    for (int cc = 0; cc < 16; cc++) {
+        if (m0 + cc >= a.M) break;
+        float v = acc[cc];
+        if (a.bias) v = __fadd_rn(v, b);
+        if (a.skip) v = __fadd_rn(r[cc], v);
+        const int64_t at = (int64_t)(m0 + cc) * a.ldy + n;
+        if (a.y) a.y[at] = v;
+        if (a.out_x) {
+            float u = v;
+            if (a.sr_scale) u = __fadd_rn(__fmul_rn(u, ss), sb);
+            if (a.alpha) u = gm_snake(u, al);
+            a.out_x[at] = u;
+        }
+    }
+}
+
+template <bool TF32>
+__device__ __forceinline__ void gm_store(const GemmArgs &a, int m0, int n, const float *acc) {
+    if constexpr (TF32) gm_store16_vae(a, m0, n, acc);
+    else gm_store16(a, m0, n, acc);
+}
+
+// TF32 = false: F16 / Q8_0 weights (a.q8) with the ggml epilogue;
+// TF32 = true: tf32 hi/lo operands with the AudioVAE epilogue.  Two
+// instantiations, so neither pays the other's registers.
+template <bool TF32>
 __global__ void __launch_bounds__(GM_THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_bh,
-                const __grid_constant__ CUtensorMap tm_bl, const GemmArgs a) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_wl,
+                const __grid_constant__ CUtensorMap tm_bh, const __grid_constant__ CUtensorMap tm_bl,
+                const GemmArgs a) {
     extern __shared__ uint8_t gsm_raw[];
     uint8_t *gsm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~(uintptr_t)1023);
     __shared__ uint64_t bars[4 * GM_MAX_STAGES + 4];
@@ -163,9 +229,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int BN = a.BN;
-    const uint32_t a_bytes = a.q8 ? GM_BM * GM_BK : GM_BM * GM_BK * 2;   // raw int8 or fp16 tile
+    // stage: weight tile (raw int8, fp16, or tf32 hi then lo), activation
+    // tile(s) (hi, then lo for Q8_0 / tf32); every row one 128-byte
+    // swizzle row
+    const uint32_t a_bytes = a.q8 ? GM_BM * GM_BK : GM_BM * 128;
+    const uint32_t a_parts = TF32 ? 2u : 1u;
     const uint32_t b_bytes = (uint32_t)BN * 128;
-    const uint32_t stage_bytes = a_bytes + b_bytes * (a.q8 ? 2 : 1);
+    const uint32_t stage_bytes = a_bytes * a_parts + b_bytes * ((a.q8 || TF32) ? 2 : 1);
     uint8_t *conv = gsm + (size_t)a.n_tma * stage_bytes;                 // converted A: [n_conv][hi 16K | lo 16K]
     const int n_tiles = a.tiles_n * a.tiles_m * a.splits;
     const uint32_t acc_cols = a.tmem_cols >> 1;                         // two accumulators
@@ -219,10 +289,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                     if (!gm_wait(&empty[s], ph ^ 1u)) { atomicCAS(a.err, 0, 11); ok = false; break; }
                     uint8_t *st = gsm + (size_t)s * stage_bytes;
                     mbar_arrive_expect_tx(&full[s], stage_bytes);
-                    const int kx = (kt0 + i) * GM_BK;
+                    const int kx = (kt0 + i) * a.bk;
                     tma_load_2d(st, &tm_w, kx, n0, &full[s]);
-                    tma_load_2d(st + a_bytes, &tm_bh, kx, m0, &full[s]);
-                    if (a.q8) tma_load_2d(st + a_bytes + b_bytes, &tm_bl, kx, m0, &full[s]);
+                    if (TF32) tma_load_2d(st + a_bytes, &tm_wl, kx, n0, &full[s]);
+                    uint8_t *sb = st + a_bytes * a_parts;
+                    tma_load_2d(sb, &tm_bh, kx, m0, &full[s]);
+                    if (a.q8 || TF32) tma_load_2d(sb + b_bytes, &tm_bl, kx, m0, &full[s]);
                 }
             }
             // every issued copy has landed before the CTA can finish
@@ -234,7 +306,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     } else if (warp == 1) {
         // ---------------------------------------------------------- MMA
         if (lane == 0) {
-            const uint32_t idesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(GM_BM >> 4) << 24);
+            // D f32 (bits 4-5 = 1); A/B f16 (0) or tf32 (2) in bits 7-9 / 10-12;
+            // K-major both; N >> 3 at bit 17, M >> 4 at bit 24
+            const uint32_t fmt = TF32 ? 2u : 0u;
+            const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                   ((uint32_t)(GM_BM >> 4) << 24);
             int it = 0, tc = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, tc++) {
@@ -258,18 +334,34 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                     uint8_t *st = gsm + (size_t)s * stage_bytes;
                     const uint8_t *ahi = a.q8 ? conv + (size_t)c * 32768 : st;
                     const uint8_t *alo = ahi + 16384;
-                    const uint8_t *bhi = st + a_bytes, *blo = bhi + b_bytes;
+                    const uint8_t *bhi = st + a_bytes * a_parts, *blo = bhi + b_bytes;
+                    if constexpr (TF32) {
+                        // four k-steps of 8 tf32 (32 bytes) per stage: hi*hi + hi*lo + lo*hi
 #pragma unroll
-                    for (int k = 0; k < GM_BK / 16; k++) {
-                        const uint32_t acc = (i | k) != 0;
-                        umma_f16(acc_t, sw128_desc(ahi + 32 * k), sw128_desc(bhi + 32 * k), idesc, acc);
-                        if (a.q8) {
-                            umma_f16(acc_t, sw128_desc(ahi + 32 * k), sw128_desc(blo + 32 * k), idesc, 1u);
-                            umma_f16(acc_t, sw128_desc(alo + 32 * k), sw128_desc(bhi + 32 * k), idesc, 1u);
+                        // hi*hi accumulates apart from the two cross terms, which
+                        // are 2^-11 smaller: the accumulator's own rounding then
+                        // acts on the large sum once per k-step, not three times
+                        for (int k = 0; k < 4; k++) {
+                            const uint32_t acc = (i | k) != 0;
+                            const uint32_t acc_s = acc_t + a.small_off;
+                            umma_tf32(acc_t, sw128_desc(st + 32 * k), sw128_desc(bhi + 32 * k), idesc, acc);
+                            umma_tf32(acc_s, sw128_desc(st + 32 * k), sw128_desc(blo + 32 * k), idesc, acc);
+                            umma_tf32(acc_s, sw128_desc(st + a_bytes + 32 * k), sw128_desc(bhi + 32 * k), idesc, 1u);
                         }
+                        umma_commit(&empty[s]);
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < GM_BK / 16; k++) {
+                            const uint32_t acc = (i | k) != 0;
+                            umma_f16(acc_t, sw128_desc(ahi + 32 * k), sw128_desc(bhi + 32 * k), idesc, acc);
+                            if (a.q8) {
+                                umma_f16(acc_t, sw128_desc(ahi + 32 * k), sw128_desc(blo + 32 * k), idesc, 1u);
+                                umma_f16(acc_t, sw128_desc(alo + 32 * k), sw128_desc(bhi + 32 * k), idesc, 1u);
+                            }
+                        }
+                        umma_commit(&empty[s]);
+                        if (a.q8) umma_commit(&cempty[c]);
                     }
-                    umma_commit(&empty[s]);
-                    if (a.q8) umma_commit(&cempty[c]);
                 }
                 umma_commit(&tfull[buf]);   // fires once this tile's MMAs have completed
             }
@@ -372,7 +464,15 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             if (!okt) atomicCAS(a.err, 0, 14);
             for (int j = 0; okt && j * 16 < BN; j++) {
                 uint32_t v[16];
-                tmem_ld16(tmem + (uint32_t)buf * acc_cols + ((uint32_t)(q * 32) << 16) + (uint32_t)(j * 16), v);
+                const uint32_t ta = tmem + (uint32_t)buf * acc_cols + ((uint32_t)(q * 32) << 16) + (uint32_t)(j * 16);
+                tmem_ld16(ta, v);
+                if constexpr (TF32) {
+                    uint32_t w[16];
+                    tmem_ld16(ta + a.small_off, w);
+#pragma unroll
+                    for (int e = 0; e < 16; e++)
+                        v[e] = __float_as_uint(__fadd_rn(__uint_as_float(v[e]), __uint_as_float(w[e])));
+                }
                 if (n < a.N) {
                     if (split_k) {
                         // partials [split][N][Mp], this thread's 16 columns contiguous
@@ -383,7 +483,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                             pw[q4] = make_float4(__uint_as_float(v[4 * q4]), __uint_as_float(v[4 * q4 + 1]),
                                                  __uint_as_float(v[4 * q4 + 2]), __uint_as_float(v[4 * q4 + 3]));
                     } else {
-                        gm_store16(a, m0 + j * 16, n, reinterpret_cast<const float *>(v));
+                        gm_store<TF32>(a, m0 + j * 16, n, reinterpret_cast<const float *>(v));
                     }
                 }
             }
@@ -434,7 +534,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                                         acc[q4].w = __fadd_rn(acc[q4].w, vv[u][q4].w);
                                     }
                         }
-                        gm_store16(a, m0 + j * 16, n, reinterpret_cast<const float *>(acc));
+                        gm_store<TF32>(a, m0 + j * 16, n, reinterpret_cast<const float *>(acc));
                     }
                 }
                 asm volatile("bar.sync 2, %0;" ::"r"(GM_EPI_THREADS) : "memory");   // s_last reused next tile
@@ -551,6 +651,7 @@ static bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, i
 struct ActMaps {                // TMA descriptors of one activation buffer shape
     const void *bh = nullptr, *bl = nullptr;
     int K = 0, M = 0, BN = 0;
+    bool tf32 = false;
     CUtensorMap th, tl;
 };
 
@@ -593,7 +694,10 @@ void gemm_free(vb_ctx *ctx) {
 }
 
 int init_gemm(vb_ctx *ctx) {
-    VB_CHECK(ctx, cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GM_SMEM_BUDGET + 1024));
+    VB_CHECK(ctx, cudaFuncSetAttribute(gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       GM_SMEM_BUDGET + 1024));
+    VB_CHECK(ctx, cudaFuncSetAttribute(gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       GM_SMEM_BUDGET + 1024));
     return VB_OK;
 }
 
@@ -687,7 +791,7 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
     const void *blp = q8 ? (const void *)bl : (const void *)bh;
     ActMaps *am = nullptr;
     for (ActMaps &c : gs->cache)
-        if (c.bh == bh && c.bl == blp && c.K == K && c.M == (int)M && c.BN == BN) am = &c;
+        if (c.bh == bh && c.bl == blp && c.K == K && c.M == (int)M && c.BN == BN && !c.tf32) am = &c;
     if (!am) {
         am = &gs->cache[gs->next];
         gs->next = (gs->next + 1) % 8;
@@ -700,10 +804,12 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
         am->K = K;
         am->M = (int)M;
         am->BN = BN;
+        am->tf32 = false;
     }
 
     GemmArgs g{};
     g.q8 = q8;
+    g.bk = GM_BK;
     g.K = K;
     g.N = N;
     g.M = (int)M;
@@ -736,9 +842,125 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
         g.ws = (float *)gs->part.ptr;
     }
     const int n_work = tiles * splits;
-    gemm_kernel<<<(unsigned)std::min(n_work, ctx->sm_count), GM_THREADS, smem, ctx->stream>>>(
-        *reinterpret_cast<const CUtensorMap *>(w->tmap), am->th, am->tl, g);
+    const CUtensorMap &twm = *reinterpret_cast<const CUtensorMap *>(w->tmap);
+    gemm_kernel<false><<<(unsigned)std::min(n_work, ctx->sm_count), GM_THREADS, smem, ctx->stream>>>(twm, twm, am->th,
+                                                                                                  am->tl, g);
     VB_LAUNCH_CHECK(ctx, "gemm");
+    return VB_OK;
+}
+
+// fp32 GEMM as three tf32 products (the AudioVAE convolutions):
+// y[m][n] = sum_k W[n][k] * A[m][k] with both operands given as tf32 hi/lo
+// splits (hi = tf32(v), lo = tf32(v - hi), each stored as fp32 with the low
+// 13 mantissa bits clear): hi*hi + hi*lo + lo*hi in fp32, so every product
+// carries ~22 significant bits, as an fp32 multiply-add's does to within a
+// few units of 2^-22.  The AudioVAE epilogue (bias period cb, residual skip,
+// sr_cond, Snake) is fused.
+int launch_gemm_tf32(vb_ctx *ctx, Tf32Weight &w, const float *a_hi, const float *a_lo, int64_t M,
+                     const GemmEpi &e) {
+    GemmState *gs = gemm_state(ctx);
+    if (!gs) return set_error(ctx, VB_ERR_OOM, "gemm: state allocation failed");
+    const int K = w.K, N = w.N, BK = 32;
+    if (K % BK || M < 1 || !encode_fn())
+        return set_error(ctx, VB_ERR_INVALID_ARG, "gemm_tf32: K must be a multiple of 32");
+    if (((uintptr_t)a_hi | (uintptr_t)a_lo) % 16)
+        return set_error(ctx, VB_ERR_INVALID_ARG, "gemm_tf32: operands must be 16-byte aligned");
+    const int tiles_n = (N + GM_BM - 1) / GM_BM;
+    const int mr = (int)((M + 15) / 16 * 16);
+    const int kt_total = K / BK;
+    // the widest tile that still gives about one tile per SM, a K split
+    // when tiles are scarce (as the F16 path)
+    // (BN <= 128: each accumulator buffer holds the hi*hi and the cross-term
+    // sums side by side, two buffers -> 4 x 128 TMEM columns)
+    int BN = std::min(128, mr), splits = 1;
+    for (int cand : {128, 64}) {
+        if (cand > mr) continue;
+        BN = cand;
+        if ((int64_t)tiles_n * ((M + cand - 1) / cand) * 5 >= (int64_t)ctx->sm_count * 4) break;
+    }
+    const int64_t tiles0 = (int64_t)tiles_n * ((M + BN - 1) / BN);
+    if (tiles0 * 5 < (int64_t)ctx->sm_count * 4)
+        splits = (int)std::min<int64_t>(std::max<int64_t>(1, ctx->sm_count / tiles0), std::max(1, kt_total / 2));
+    // at most 1024 k per accumulation: longer sums are finished by the
+    // split-K reduction (fp32, round to nearest, split order)
+    splits = std::max(splits, (K + 1023) / 1024);
+    const int tiles_m = (int)((M + BN - 1) / BN);
+    const int tiles = tiles_m * tiles_n;
+    const int kt_per_split = (kt_total + splits - 1) / splits;
+    splits = (kt_total + kt_per_split - 1) / kt_per_split;
+    if (tiles > 65536) return set_error(ctx, VB_ERR_INVALID_ARG, "gemm_tf32: too many tiles");
+    const uint32_t stage = 2u * GM_BM * 128 + 2u * (uint32_t)BN * 128;
+    const int n_tma = (int)std::min<size_t>(GM_MAX_STAGES, (size_t)GM_SMEM_BUDGET / stage);
+    if (n_tma < 2) return set_error(ctx, VB_ERR_INVALID_ARG, "gemm_tf32: tile does not fit shared memory");
+    const size_t smem = (size_t)n_tma * stage + 1024;
+    uint32_t pcols = 32;
+    while (pcols < (uint32_t)BN) pcols <<= 1;
+    const uint32_t cols = 4 * pcols;      // 2 buffers x (hi*hi, cross terms)
+    if (!w.maps_ok) {
+        w.maps_ok = make_map(reinterpret_cast<CUtensorMap *>(w.map_hi), w.hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, K, N,
+                             BK, GM_BM, true) &&
+                    make_map(reinterpret_cast<CUtensorMap *>(w.map_lo), w.lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, K, N,
+                             BK, GM_BM, true);
+        if (!w.maps_ok) return set_error(ctx, VB_ERR_BACKEND, "gemm_tf32: weight tensor map encoding failed");
+    }
+    ActMaps *am = nullptr;
+    for (ActMaps &c : gs->cache)
+        if (c.bh == a_hi && c.bl == a_lo && c.K == K && c.M == (int)M && c.BN == BN && c.tf32) am = &c;
+    if (!am) {
+        am = &gs->cache[gs->next];
+        gs->next = (gs->next + 1) % 8;
+        am->bh = nullptr;
+        if (!make_map(&am->th, a_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, K, M, BK, BN, true) ||
+            !make_map(&am->tl, a_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, K, M, BK, BN, true))
+            return set_error(ctx, VB_ERR_BACKEND, "gemm_tf32: activation tensor map encoding failed");
+        am->bh = a_hi;
+        am->bl = a_lo;
+        am->K = K;
+        am->M = (int)M;
+        am->BN = BN;
+        am->tf32 = true;
+    }
+    GemmArgs g{};
+    g.tf32 = 1;
+    g.bk = BK;
+    g.K = K;
+    g.N = N;
+    g.M = (int)M;
+    g.BN = BN;
+    g.kt_total = kt_total;
+    g.kt_per_split = kt_per_split;
+    g.splits = splits;
+    g.tiles_m = tiles_m;
+    g.tiles_n = tiles_n;
+    g.n_tma = n_tma;
+    g.n_conv = 1;
+    g.tmem_cols = cols;
+    g.y = e.y;
+    g.bias = e.bias;
+    g.ldy = N;
+    g.seg = M;
+    g.seg_plain = 1;
+    g.cnt = gs->cnt;
+    g.err = gs->err;
+    g.vae = 1;
+    g.small_off = pcols;
+    g.cb = e.cb > 0 ? e.cb : N;
+    g.skip = e.skip;
+    g.out_x = e.out_x;
+    g.alpha = e.alpha;
+    g.sr_scale = e.sr_scale;
+    g.sr_bias = e.sr_bias;
+    if (splits > 1) {
+        g.Mp = tiles_m * BN;
+        const int rc = arena_reserve(ctx, gs->part, (size_t)splits * N * g.Mp * 4);
+        if (rc) return rc;
+        g.ws = (float *)gs->part.ptr;
+    }
+    const int n_work = tiles * splits;
+    gemm_kernel<true><<<(unsigned)std::min(n_work, ctx->sm_count), GM_THREADS, smem, ctx->stream>>>(
+        *reinterpret_cast<const CUtensorMap *>(w.map_hi), *reinterpret_cast<const CUtensorMap *>(w.map_lo), am->th,
+        am->tl, g);
+    VB_LAUNCH_CHECK(ctx, "gemm_tf32");
     return VB_OK;
 }
 

@@ -43,6 +43,28 @@ int launch_quantize_q8_0(vb_ctx *ctx, const float *x, int64_t K, int64_t M, void
 int launch_dequantize_q8_0(vb_ctx *ctx, const void *blocks, int64_t n, float *y);
 int launch_get_rows(vb_ctx *ctx, vb_weight w, const int32_t *ids, int64_t n, float *y);
 
+// fp32 GEMM through three tf32 tensor-core products (vb_gemm.cu).  Weights
+// [N][K] pre-split into tf32 hi/lo (fp32 storage, low 13 mantissa bits
+// clear); the TMA descriptors are encoded on first use.
+struct Tf32Weight {
+    float *hi = nullptr, *lo = nullptr;
+    int K = 0, N = 0;
+    alignas(64) unsigned char map_hi[128];
+    alignas(64) unsigned char map_lo[128];
+    bool maps_ok = false;
+};
+// AudioVAE epilogue: v = acc + bias[n % cb] (+ skip[m][n]); y[m][n] = v
+// (if y); out_x[m][n] = snake(alpha)(v * sr_scale + sr_bias) (if out_x).
+struct GemmEpi {
+    float *y = nullptr;
+    const float *bias = nullptr;
+    int cb = 0;
+    const float *skip = nullptr;
+    float *out_x = nullptr;
+    const float *alpha = nullptr, *sr_scale = nullptr, *sr_bias = nullptr;
+};
+int launch_gemm_tf32(vb_ctx *ctx, Tf32Weight &w, const float *a_hi, const float *a_lo, int64_t M, const GemmEpi &e);
+
 // elementwise (vb_elem.cu)
 int launch_rms_norm(vb_ctx *ctx, const float *x, const float *w, float *y, int64_t n, int64_t rows, float eps,
                     unsigned flags, int64_t ldx = 0, int64_t ldy = 0);

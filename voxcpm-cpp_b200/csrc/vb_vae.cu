@@ -13,17 +13,19 @@
 // times q*s .. q*s+s-1 of all channels form one row of s*Co values, computed
 // from the concatenated input rows [x(q-1) | x(q)] (x(-1) = the history
 // cache) against a repacked weight [2*Ci][s*Co].  The GEMM is an fp32 SIMT
-// kernel (the reference decodes in F32; a tensor-core format would not meet
-// the parity bar), with the bias, residual skip, sr_cond scale/bias and the
-// next layer's Snake fused into its epilogue.  Depthwise k7 convs and the
-// final k7 -> tanh conv are bandwidth-bound direct kernels that also roll
-// their history caches (double-buffered, so no launch reads a cache row that
-// the same launch rewrites).
+// kernel, or for the wide layers the tcgen05 GEMM with both operands split
+// into tf32 hi/lo (three products, fp32-class accuracy; a single tf32 or
+// bf16 product would move PCM by ~1e-3), with the bias, residual skip,
+// sr_cond scale/bias and the next layer's Snake fused into its epilogue.
+// Depthwise k7 convs and the final k7 -> tanh conv are bandwidth-bound
+// direct kernels that also roll their history caches (double-buffered, so
+// no launch reads a cache row that the same launch rewrites).
 #include <algorithm>
 #include <cstring>
 #include <vector>
 
 #include "vb_common.cuh"
+#include "vb_kernels.cuh"
 
 using namespace vb;
 
@@ -42,6 +44,27 @@ __device__ __forceinline__ float snake_f(float x, float a) {
 
 __device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
 __device__ __forceinline__ void st4(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
+
+// tf32 of x with round-to-nearest-even (fp32 storage, low 13 mantissa bits
+// clear, as the tensor core reads it); finite inputs.
+__host__ __device__ __forceinline__ uint32_t tf32_bits(uint32_t u) {
+    if ((u & 0x7f800000u) == 0x7f800000u) return u;
+    u += 0xfffu + ((u >> 13) & 1u);
+    return u & 0xffffe000u;
+}
+
+// x = hi + lo: hi = tf32(x), lo = tf32(x - hi) (the difference is exact).
+__device__ __forceinline__ void split4(float4 v, float *hi, float *lo) {
+    const float x[4] = {v.x, v.y, v.z, v.w};
+    float h[4], l[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        h[e] = __uint_as_float(tf32_bits(__float_as_uint(x[e])));
+        l[e] = __uint_as_float(tf32_bits(__float_as_uint(__fsub_rn(x[e], h[e]))));
+    }
+    st4(hi, make_float4(h[0], h[1], h[2], h[3]));
+    st4(lo, make_float4(l[0], l[1], l[2], l[3]));
+}
 
 // ----------------------------------------------------------------- GEMM
 struct VaeGemm {
@@ -222,7 +245,8 @@ __global__ void __launch_bounds__(G_THREADS, 2) vae_gemm_kernel(const VaeGemm g)
 // write the new history (the last 6d rows of comb) into cnew.
 __global__ void vae_dw7_kernel(const float *__restrict__ x, const float *__restrict__ cold, float *__restrict__ cnew,
                                const float *__restrict__ w, const float *__restrict__ bias,
-                               const float *__restrict__ alpha, float *__restrict__ y, int T, int C, int d) {
+                               const float *__restrict__ alpha, float *__restrict__ y, float *__restrict__ ylo, int T,
+                               int C, int d) {
     const int C4 = C / 4, L = 6 * d, b = blockIdx.y;
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (int64_t)(T + L) * C4) return;
@@ -254,7 +278,24 @@ __global__ void vae_dw7_kernel(const float *__restrict__ x, const float *__restr
         acc.x = snake_f(acc.x, a.x); acc.y = snake_f(acc.y, a.y);
         acc.z = snake_f(acc.z, a.z); acc.w = snake_f(acc.w, a.w);
     }
-    st4(y + ((int64_t)b * T + row) * C + c, acc);
+    const int64_t at = ((int64_t)b * T + row) * C + c;
+    if (ylo) split4(acc, y + at, ylo + at);     // tf32 hi/lo operand of the next GEMM
+    else st4(y + at, acc);
+}
+
+// The transposed conv's GEMM operand as tf32 hi/lo rows [x(q-1) | x(q)] of
+// 2C values (x(-1) = the stream's history row).
+__global__ void vae_split_prev_kernel(const float *__restrict__ x, const float *__restrict__ hist,
+                                      float *__restrict__ ah, float *__restrict__ al, int64_t M, int T, int C) {
+    const int C4 = C / 4;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= M * 2 * C4) return;
+    const int64_t m = idx / (2 * C4);
+    const int q = (int)(idx % (2 * C4)), half = q / C4, c = (q % C4) * 4;
+    const int64_t t = m % T;
+    const float *src = half ? x + m * C : (t ? x + (m - 1) * C : hist + (m / T) * C);
+    const int64_t at = m * 2 * C + (int64_t)half * C + c;
+    split4(ld4(src + c), ah + at, al + at);
 }
 
 // ------------------------------------------- output conv k7, C -> 1, tanh
@@ -313,16 +354,20 @@ float host_h2f(uint16_t h) {
 
 struct VaeResUnit {
     float *alpha0 = nullptr, *dw_w = nullptr, *dw_b = nullptr, *alpha2 = nullptr, *pw_w = nullptr, *pw_b = nullptr;
+    Tf32Weight pw_t;              // tensor-core operand of pw_w ([Co][Co], hi/lo), if used
 };
 struct VaeBlock {
     int ci = 0, co = 0, s = 0;
     float *sr_scale = nullptr, *sr_bias = nullptr, *alpha = nullptr, *up_w = nullptr, *up_b = nullptr;
+    Tf32Weight up_t;              // [s*Co][2*Ci] hi/lo, if used
     VaeResUnit res[3];
 };
 
 struct vb_vae_s {
     vb_vae_config cfg{};
+    bool tf32 = true;             // tensor-core path for the wide convs (VB_VAE_TF32=0: fp32 SIMT everywhere)
     float *in_dw_w = nullptr, *in_dw_b = nullptr, *in_pw_w = nullptr, *in_pw_b = nullptr;
+    Tf32Weight in_pw_t;           // [D][latent] hi/lo, if used
     VaeBlock blk[6];
     float *out_alpha = nullptr, *out_w = nullptr, *out_b = nullptr;
     std::vector<void *> allocs;
@@ -340,7 +385,7 @@ struct vb_vae_stream_s {
     float *cache_out[2] = {};     // [n][6][C_last]
     std::vector<void *> allocs;
     size_t state_bytes = 0;
-    float *work = nullptr;        // activations: X0, XA, XB, TB, H
+    float *work = nullptr;        // activations: X0, XA, XB, TB, H, then the tf32 operand AH, AL (2x each)
     size_t work_floats = 0;       // per buffer
     int work_T = 0;               // latent frames the buffers hold
 };
@@ -362,6 +407,37 @@ void to_f32(const void *src, bool f16, size_t n, std::vector<float> &out) {
     } else {
         memcpy(out.data(), src, n * sizeof(float));
     }
+}
+
+float host_tf32(float x) {
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    u = tf32_bits(u);
+    float r;
+    memcpy(&r, &u, 4);
+    return r;
+}
+
+// Wide convs (N >= 128 output values per row, K >= 256 and a multiple of
+// 32) run on the tensor cores as three tf32 products; the rest on the SIMT
+// kernel (measured on B200: below K = 256 the tensor-core tiles wait on
+// their epilogue and the SIMT kernel is as fast).
+bool use_tf32(const vb_vae_s *v, int N, int K) { return v->tf32 && N >= 128 && K >= 256 && K % 32 == 0; }
+
+int upload(vb_ctx *ctx, vb_vae v, const std::vector<float> &h, float **dst);
+
+// K-major [N][K] weight -> tf32 hi/lo device copies.
+int upload_tf32(vb_ctx *ctx, vb_vae v, const std::vector<float> &wk, int N, int K, Tf32Weight &t) {
+    std::vector<float> hi(wk.size()), lo(wk.size());
+    for (size_t i = 0; i < wk.size(); i++) {
+        hi[i] = host_tf32(wk[i]);
+        lo[i] = host_tf32(wk[i] - hi[i]);
+    }
+    t.N = N;
+    t.K = K;
+    int rc = upload(ctx, v, hi, &t.hi);
+    if (!rc) rc = upload(ctx, v, lo, &t.lo);
+    return rc;
 }
 
 int upload(vb_ctx *ctx, vb_vae v, const std::vector<float> &h, float **dst) {
@@ -397,11 +473,12 @@ int launch_vae_gemm(vb_ctx *ctx, const VaeGemm &g) {
     return launch_gemm_tile<128, 32, 4, 4>(ctx, g);
 }
 
+// y_lo non-null: y and y_lo receive the tf32 hi/lo split of the output.
 int launch_dw7(vb_ctx *ctx, const float *x, const float *cold, float *cnew, const float *w, const float *bias,
-               const float *alpha, float *y, int n, int T, int C, int d) {
+               const float *alpha, float *y, float *y_lo, int n, int T, int C, int d) {
     const int64_t items = (int64_t)(T + 6 * d) * (C / 4);
     dim3 grid((unsigned)((items + 255) / 256), (unsigned)n);
-    vae_dw7_kernel<<<grid, 256, 0, ctx->stream>>>(x, cold, cnew, w, bias, alpha, y, T, C, d);
+    vae_dw7_kernel<<<grid, 256, 0, ctx->stream>>>(x, cold, cnew, w, bias, alpha, y, y_lo, T, C, d);
     VB_LAUNCH_CHECK(ctx, "vae_dw7");
     return VB_OK;
 }
@@ -437,6 +514,10 @@ extern "C" int vb_vae_create(vb_ctx *ctx, const vb_vae_config *cfg, const void *
     VB_CHECK(ctx, cudaSetDevice(ctx->device));
     vb_vae v = new vb_vae_s();
     v->cfg = c;
+    {
+        const char *e = getenv("VB_VAE_TF32");
+        v->tf32 = !(e && e[0] == '0');
+    }
     const bool f16 = c.weight_type == VB_TYPE_F16;
     const int L = c.latent_dim, D = c.decoder_dim;
     std::vector<float> a, r;
@@ -453,18 +534,21 @@ extern "C" int vb_vae_create(vb_ctx *ctx, const vb_vae_config *cfg, const void *
             for (int j = 0; j < 7; j++) r[(size_t)j * C + ch] = a[(size_t)ch * 7 + j];
         return upload(ctx, v, r, dst);
     };
-    // pointwise [Co][Ci] -> B operand [Ci][Co]
-    auto pw = [&](const void *p, int ci, int co, float **dst) -> int {
+    // pointwise [Co][Ci] -> B operand [Ci][Co] (SIMT), and the [Co][Ci]
+    // tf32 hi/lo pair when the layer runs on the tensor cores
+    auto pw = [&](const void *p, int ci, int co, float **dst, Tf32Weight *tw) -> int {
         to_f32(p, f16, (size_t)ci * co, a);
         r.assign((size_t)ci * co, 0.f);
         for (int o = 0; o < co; o++)
             for (int i = 0; i < ci; i++) r[(size_t)i * co + o] = a[(size_t)o * ci + i];
-        return upload(ctx, v, r, dst);
+        int rc2 = upload(ctx, v, r, dst);
+        if (!rc2 && use_tf32(v, co, ci)) rc2 = upload_tf32(ctx, v, a, co, ci, *tw);
+        return rc2;
     };
     int rc = VB_OK;
     if (!rc) rc = dw(t[VB_VAE_IN_DW_W], L, &v->in_dw_w);
     if (!rc) rc = vec(t[VB_VAE_IN_DW_B], L, &v->in_dw_b);
-    if (!rc) rc = pw(t[VB_VAE_IN_PW_W], L, D, &v->in_pw_w);
+    if (!rc) rc = pw(t[VB_VAE_IN_PW_W], L, D, &v->in_pw_w, &v->in_pw_t);
     if (!rc) rc = vec(t[VB_VAE_IN_PW_B], D, &v->in_pw_b);
     for (int b = 0; b < 6 && !rc; b++) {
         VaeBlock &B = v->blk[b];
@@ -489,6 +573,20 @@ extern "C" int vb_vae_create(vb_ctx *ctx, const vb_vae_config *cfg, const void *
                         r[(size_t)(ci + i) * s * co + (size_t)q * co + o] = a[src + q];
                     }
             rc = upload(ctx, v, r, &B.up_w);
+            if (!rc && use_tf32(v, s * co, 2 * ci)) {
+                // K-major [s*Co][2*Ci]: row q*Co + o, previous-row taps then current-row taps
+                std::vector<float> wk((size_t)s * co * 2 * ci);
+                for (int q = 0; q < s; q++)
+                    for (int o = 0; o < co; o++) {
+                        float *row = wk.data() + ((size_t)q * co + o) * 2 * ci;
+                        for (int i = 0; i < ci; i++) {
+                            const size_t src = ((size_t)i * co + o) * 2 * s;
+                            row[i] = a[src + s + q];
+                            row[ci + i] = a[src + q];
+                        }
+                    }
+                rc = upload_tf32(ctx, v, wk, s * co, 2 * ci, B.up_t);
+            }
         }
         for (int u = 0; u < 3 && !rc; u++) {
             const int rb = base + VB_VAE_B_RES0 + u * VB_VAE_RES_SLOTS;
@@ -497,7 +595,7 @@ extern "C" int vb_vae_create(vb_ctx *ctx, const vb_vae_config *cfg, const void *
             if (!rc) rc = dw(t[rb + VB_VAE_R_DW_W], co, &R.dw_w);
             if (!rc) rc = vec(t[rb + VB_VAE_R_DW_B], co, &R.dw_b);
             if (!rc) rc = vec(t[rb + VB_VAE_R_ALPHA2], co, &R.alpha2);
-            if (!rc) rc = pw(t[rb + VB_VAE_R_PW_W], co, co, &R.pw_w);
+            if (!rc) rc = pw(t[rb + VB_VAE_R_PW_W], co, co, &R.pw_w, &R.pw_t);
             if (!rc) rc = vec(t[rb + VB_VAE_R_PW_B], co, &R.pw_b);
         }
     }
@@ -625,17 +723,34 @@ extern "C" int vb_vae_stream_decode(vb_ctx *ctx, vb_vae_stream s, const float *l
             s->work_floats = 0;
         }
         void *p = nullptr;
-        if (cudaMalloc(&p, need * 5 * sizeof(float)) != cudaSuccess)
-            return set_error(ctx, VB_ERR_OOM, "vb_vae_stream_decode: %zu bytes of activations", need * 20);
+        if (cudaMalloc(&p, need * 9 * sizeof(float)) != cudaSuccess)
+            return set_error(ctx, VB_ERR_OOM, "vb_vae_stream_decode: %zu bytes of activations", need * 36);
         s->work = static_cast<float *>(p);
         s->work_floats = need;
     }
     float *X0 = s->work, *XA = X0 + need, *XB = XA + need, *TB = XB + need, *H = TB + need;
+    float *AH = H + need, *AL = AH + 2 * need;     // tf32 hi/lo operand (a transposed conv reads 2 x its input)
     const int p = s->parity, q = p ^ 1;
     int rc;
+    // One conv as a GEMM: on the tensor cores when `tw` holds its tf32
+    // weights (the operand is then already split into AH/AL), else SIMT.
+    auto gemm = [&](const VaeGemm &g, Tf32Weight &tw) -> int {
+        if (!tw.hi) return launch_vae_gemm(ctx, g);
+        GemmEpi e;
+        e.y = g.out_h;
+        e.bias = g.bias;
+        e.cb = g.Cb;
+        e.skip = g.skip;
+        e.out_x = g.out_x;
+        e.alpha = g.alpha;
+        e.sr_scale = g.sr_scale;
+        e.sr_bias = g.sr_bias;
+        return launch_gemm_tf32(ctx, tw, AH, AL, g.M, e);
+    };
     // model.0: depthwise k7 over the latent (no Snake before model.1)
-    rc = launch_dw7(ctx, latent, s->cache_in[p], s->cache_in[q], v->in_dw_w, v->in_dw_b, nullptr, X0, n,
-                    n_timesteps, L, 1);
+    const bool t_in = v->in_pw_t.hi != nullptr;
+    rc = launch_dw7(ctx, latent, s->cache_in[p], s->cache_in[q], v->in_dw_w, v->in_dw_b, nullptr, t_in ? AH : X0,
+                    t_in ? AL : nullptr, n, n_timesteps, L, 1);
     if (rc) return rc;
     // model.1: pointwise L -> D; emits block 0's input: snake(alpha)(sr(h))
     {
@@ -643,18 +758,24 @@ extern "C" int vb_vae_stream_decode(vb_ctx *ctx, vb_vae_stream s, const float *l
         g.A = X0; g.Ka = L; g.B = v->in_pw_w; g.M = n * n_timesteps; g.N = D; g.K = L;
         g.bias = v->in_pw_b; g.Cb = D; g.out_x = XA;
         g.alpha = v->blk[0].alpha; g.sr_scale = v->blk[0].sr_scale; g.sr_bias = v->blk[0].sr_bias;
-        if ((rc = launch_vae_gemm(ctx, g))) return rc;
+        if ((rc = gemm(g, v->in_pw_t))) return rc;
     }
     int T = n_timesteps;
     for (int b = 0; b < 6; b++) {
-        const VaeBlock &B = v->blk[b];
+        VaeBlock &B = v->blk[b];
         // transposed conv: rows [x(q-1) | x(q)] -> s output times of Co
         {
+            if (B.up_t.hi) {
+                const int64_t items = (int64_t)n * T * 2 * (B.ci / 4);
+                vae_split_prev_kernel<<<(unsigned)((items + 255) / 256), 256, 0, ctx->stream>>>(
+                    XA, s->cache_up[b], AH, AL, (int64_t)n * T, T, B.ci);
+                VB_LAUNCH_CHECK(ctx, "vae_split_prev");
+            }
             VaeGemm g{};
             g.A = XA; g.Ka = B.ci; g.prev = s->cache_up[b]; g.T_in = T;
             g.B = B.up_w; g.M = n * T; g.N = B.s * B.co; g.K = 2 * B.ci;
             g.bias = B.up_b; g.Cb = B.co; g.out_h = H; g.out_x = XB; g.alpha = B.res[0].alpha0;
-            if ((rc = launch_vae_gemm(ctx, g))) return rc;
+            if ((rc = gemm(g, B.up_t))) return rc;
         }
         // its history: the last (Snake-activated) input row of every stream
         VB_CHECK(ctx, cudaMemcpy2DAsync(s->cache_up[b], sizeof(float) * B.ci, XA + (size_t)(T - 1) * B.ci,
@@ -662,9 +783,10 @@ extern "C" int vb_vae_stream_decode(vb_ctx *ctx, vb_vae_stream s, const float *l
                                         ctx->stream));
         T *= B.s;
         for (int u = 0; u < 3; u++) {
-            const VaeResUnit &R = B.res[u];
-            rc = launch_dw7(ctx, XB, s->cache_res[b][u][p], s->cache_res[b][u][q], R.dw_w, R.dw_b, R.alpha2, TB, n,
-                            T, B.co, VAE_DIL[u]);
+            VaeResUnit &R = B.res[u];
+            const bool tr = R.pw_t.hi != nullptr;
+            rc = launch_dw7(ctx, XB, s->cache_res[b][u][p], s->cache_res[b][u][q], R.dw_w, R.dw_b, R.alpha2,
+                            tr ? AH : TB, tr ? AL : nullptr, n, T, B.co, VAE_DIL[u]);
             if (rc) return rc;
             VaeGemm g{};
             g.A = TB; g.Ka = B.co; g.B = R.pw_w; g.M = n * T; g.N = B.co; g.K = B.co;
@@ -677,7 +799,7 @@ extern "C" int vb_vae_stream_decode(vb_ctx *ctx, vb_vae_stream s, const float *l
             } else {                // model.8 Snake before the output conv
                 g.out_x = XA; g.alpha = v->out_alpha;
             }
-            if ((rc = launch_vae_gemm(ctx, g))) return rc;
+            if ((rc = gemm(g, R.pw_t))) return rc;
         }
     }
     // model.9 + tanh
