@@ -549,27 +549,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     }
 }
 
-// Activation operand(s): Q8_0 -> (hi, lo) fp16 of the dequantised block
-// values (quantisation bit-exact with the GEMV path's, rule `rule`); F16 ->
-// fp16(x).  One thread per 8 values, four threads per 32-value block (the
-// block maximum is a two-step shuffle); row m reads x row (m % x_mod).
-// vec: x rows are 16-byte aligned (float4 loads).
-__global__ void gemm_act_kernel(const float *x, int64_t ldx, int64_t x_mod, int M, int K, int q8, int rule, int vec,
-                                __half *bh, __half *bl) {
-    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // item of 8 values
-    const int ipr = K >> 3;
-    const bool valid = e < (int64_t)M * ipr;
-    const int m = valid ? (int)(e / ipr) : 0, k0 = valid ? (int)(e - (int64_t)m * ipr) * 8 : 0;
-    const float *xr = x + (int64_t)(m % x_mod) * ldx + k0;
-    float v[8];
-    if (vec) {
-        const float4 a0 = *reinterpret_cast<const float4 *>(xr), a1 = *reinterpret_cast<const float4 *>(xr + 4);
-        v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w; v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
-    } else {
-#pragma unroll
-        for (int j = 0; j < 8; j++) v[j] = xr[j];
-    }
-    const int64_t o = (int64_t)m * K + k0;
+// Emits 8 consecutive activation values (row offset o) as the GEMM operand:
+// Q8_0 -> (hi, lo) fp16 of the dequantised block values (quantisation
+// bit-exact with the GEMV path's, rule `rule`; the four threads of a 32-value
+// block are consecutive lanes and all take part in the shuffles); F16 ->
+// fp16(x).
+__device__ __forceinline__ void act_emit8(const float (&v)[8], bool valid, int64_t o, int q8, int rule, __half *bh,
+                                          __half *bl) {
     if (!q8) {
         if (valid) {
             uint32_t w[4];
@@ -612,6 +598,99 @@ __global__ void gemm_act_kernel(const float *x, int64_t ldx, int64_t x_mod, int 
     if (valid) {
         *reinterpret_cast<uint4 *>(bh + o) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
         *reinterpret_cast<uint4 *>(bl + o) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+    }
+}
+
+__device__ __forceinline__ void load8(const float *p, bool vec, float (&v)[8]) {
+    if (vec) {
+        const float4 a0 = *reinterpret_cast<const float4 *>(p), a1 = *reinterpret_cast<const float4 *>(p + 4);
+        v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w; v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = p[j];
+    }
+}
+
+// Activation operand(s), one thread per 8 values; row m reads x row
+// (m % x_mod).  vec: x rows are 16-byte aligned (float4 loads).  With
+// swiglu_f > 0 the x rows are [gate (F) | up (F)] and the operand is the
+// SwiGLU middle of vcpm_mlp, bf16(bf16(silu(bf16 g)) * bf16 u)
+// (src/minicpm4.c:441-456, the swiglu_rows_kernel formula), so the
+// down-projection reads the gate/up output directly.
+__global__ void gemm_act_kernel(const float *x, int64_t ldx, int64_t x_mod, int M, int K, int q8, int rule, int vec,
+                                int swiglu_f, __half *bh, __half *bl) {
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // item of 8 values
+    const int ipr = K >> 3;
+    const bool valid = e < (int64_t)M * ipr;
+    const int m = valid ? (int)(e / ipr) : 0, k0 = valid ? (int)(e - (int64_t)m * ipr) * 8 : 0;
+    const float *xr = x + (int64_t)(m % x_mod) * ldx + k0;
+    float v[8];
+    load8(xr, vec, v);
+    if (swiglu_f > 0) {
+        float u[8];
+        load8(xr + swiglu_f, vec, u);
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = bf16r(__fmul_rn(bf16r(silu_f(bf16r(v[j]))), bf16r(u[j])));
+    }
+    act_emit8(v, valid, (int64_t)m * K + k0, q8, rule, bh, bl);
+}
+
+// The operand of a mat-mul that follows vcpm_rms_norm with a weight and
+// bf16 rounding (src/minicpm4.c:132-152): one CTA per row computes the row
+// statistic as rms_norm_kernel does (fp32 squares summed in double, mean
+// rounded to fp32, 1/sqrt(mean + eps)), then each value
+// bf16(bf16(x * scale) * w) goes straight into the operand.  K <= 8 * 256 *
+// ACT_NORM_ITEMS.
+constexpr int ACT_NORM_THREADS = 256, ACT_NORM_ITEMS = 4;
+
+__global__ void __launch_bounds__(ACT_NORM_THREADS) gemm_act_norm_kernel(const float *x, int64_t ldx, int64_t x_mod,
+                                                                          int K, int q8, int rule, int vec,
+                                                                          const float *__restrict__ nw, float eps,
+                                                                          __half *bh, __half *bl) {
+    const int m = blockIdx.x;
+    const float *xr = x + (int64_t)(m % x_mod) * ldx;
+    const int ipr = K >> 3;
+    float v[ACT_NORM_ITEMS][8];
+    double s = 0.0;
+#pragma unroll
+    for (int it = 0; it < ACT_NORM_ITEMS; it++) {
+        const int item = it * ACT_NORM_THREADS + threadIdx.x;
+        if (item < ipr) {
+            load8(xr + item * 8, vec, v[it]);
+#pragma unroll
+            for (int j = 0; j < 8; j++) s += (double)__fmul_rn(v[it][j], v[it][j]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[it][j] = 0.0f;
+        }
+    }
+    __shared__ double red[ACT_NORM_THREADS / 32];
+    __shared__ float s_scale;
+    s = warp_sum_d(s);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        double t = threadIdx.x < ACT_NORM_THREADS / 32 ? red[threadIdx.x] : 0.0;
+        t = warp_sum_d(t);
+        if (threadIdx.x == 0) {
+            const float mean = __double2float_rn(__ddiv_rn(t, (double)K));
+            s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+        }
+    }
+    __syncthreads();
+    const float scale = s_scale;
+#pragma unroll
+    for (int it = 0; it < ACT_NORM_ITEMS; it++) {
+        const int item = it * ACT_NORM_THREADS + threadIdx.x;
+        if (it * ACT_NORM_THREADS >= ipr) break;     // uniform over the CTA
+        const bool valid = item < ipr;
+        float y[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const float wv = valid ? __ldg(nw + item * 8 + j) : 0.0f;
+            y[j] = bf16r(__fmul_rn(bf16r(__fmul_rn(v[it][j], scale)), wv));
+        }
+        act_emit8(y, valid, (int64_t)m * K + (int64_t)(valid ? item : 0) * 8, q8, rule, bh, bl);
     }
 }
 
@@ -709,7 +788,7 @@ bool gemm_supported(vb_weight w, int64_t M) {
 }
 
 int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx, int64_t x_mod,
-                const MatmulOut &out) {
+                const MatmulOut &out, const GemmPro *pro) {
     GemmState *gs = gemm_state(ctx);
     if (!gs) return set_error(ctx, VB_ERR_OOM, "gemm: state allocation failed");
     const bool q8 = w->type == VB_TYPE_Q8_0;
@@ -775,10 +854,18 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
     __half *bl = (__half *)((uint8_t *)gs->act.ptr + ((ab + 255) & ~(size_t)255));
     {
         const int64_t items = M * (K / 8);
-        const int64_t lx = ldx ? ldx : K;
+        const int64_t lx = ldx ? ldx : (pro && pro->swiglu_f ? 2 * (int64_t)K : K);
         const int vec = ((uintptr_t)x % 16 == 0) && (lx % 4 == 0);
-        gemm_act_kernel<<<(unsigned)((items + 255) / 256), 256, 0, ctx->stream>>>(
-            x, lx, x_mod > 0 ? x_mod : M, (int)M, K, q8 ? 1 : 0, ctx->qrule, vec, bh, bl);
+        const int64_t xm = x_mod > 0 ? x_mod : M;
+        if (pro && pro->norm_w) {
+            if (K > 8 * ACT_NORM_THREADS * ACT_NORM_ITEMS)
+                return set_error(ctx, VB_ERR_INVALID_ARG, "gemm: fused RMSNorm row of %d values is too wide", K);
+            gemm_act_norm_kernel<<<(unsigned)M, ACT_NORM_THREADS, 0, ctx->stream>>>(
+                x, lx, xm, K, q8 ? 1 : 0, ctx->qrule, vec, pro->norm_w, pro->eps, bh, bl);
+        } else {
+            gemm_act_kernel<<<(unsigned)((items + 255) / 256), 256, 0, ctx->stream>>>(
+                x, lx, xm, (int)M, K, q8 ? 1 : 0, ctx->qrule, vec, pro ? pro->swiglu_f : 0, bh, bl);
+        }
         VB_LAUNCH_CHECK(ctx, "gemm_act");
     }
     // descriptors: the weight's once per weight, the activations' per shape

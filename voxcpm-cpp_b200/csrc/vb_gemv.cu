@@ -263,6 +263,19 @@ int init_gemv(vb_ctx *ctx) {
 
 static size_t q8_smem(int mc, int64_t K) { return (size_t)((mc * K + 15) & ~15) + (size_t)mc * (K / QK) * 4; }
 
+bool matmul_uses_gemm(vb_ctx *ctx, vb_weight w, int64_t M) { return ctx->use_gemm && gemm_supported(w, M); }
+
+int launch_matmul_pro(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx, const GemmPro &pro,
+                      const MatmulOut &out_in) {
+    if (!w || !x || !out_in.y || M < 0) return set_error(ctx, VB_ERR_INVALID_ARG, "matmul: bad argument");
+    if (M == 0) return VB_OK;
+    if (!matmul_uses_gemm(ctx, w, M)) return set_error(ctx, VB_ERR_INVALID_ARG, "matmul: fused prologue needs M >= 16");
+    MatmulOut out = out_in;
+    if (out.ldy == 0) out.ldy = w->N;
+    if (out.seg == 0) { out.seg = M; out.seg_stride = 0; out.seg_off = 0; }
+    return launch_gemm(ctx, w, x, M, ldx, 0, out, &pro);
+}
+
 int launch_matmul(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx, int64_t x_mod,
                   const MatmulOut &out_in) {
     if (!w || !x || !out_in.y || M < 0) return set_error(ctx, VB_ERR_INVALID_ARG, "matmul: bad argument");

@@ -34,8 +34,24 @@ int launch_matmul(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t l
 
 // Tensor-core path for M >= 16 (vb_gemm.cu); launch_matmul dispatches to it.
 bool gemm_supported(vb_weight w, int64_t M);
+// Prologue fused into the tensor-core path's activation operand: norm_w set
+// -> the operand is vcpm_rms_norm(x) with weight norm_w and bf16 rounding;
+// swiglu_f > 0 -> x rows are [gate (F) | up (F)] (ldx 0 means 2F) and the
+// operand is the SwiGLU middle of vcpm_mlp.
+struct GemmPro {
+    const float *norm_w = nullptr;
+    float eps = 0.0f;
+    int swiglu_f = 0;
+};
 int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx, int64_t x_mod,
-                const MatmulOut &out);
+                const MatmulOut &out, const GemmPro *pro = nullptr);
+// True when launch_matmul takes the tensor-core path for this weight and M
+// (so a GemmPro prologue can be fused).
+bool matmul_uses_gemm(vb_ctx *ctx, vb_weight w, int64_t M);
+// launch_matmul through the tensor-core path with a fused prologue; the
+// caller checks matmul_uses_gemm first.
+int launch_matmul_pro(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx, const GemmPro &pro,
+                      const MatmulOut &out);
 int gemm_device_error(vb_ctx *ctx, int *code);
 void gemm_free(vb_ctx *ctx);
 

@@ -339,12 +339,22 @@ static int run_layers(vb_ctx *ctx, vb_lm *lm, int M, float *h, const TokenTables
         uint16_t *kc = kc_base + (size_t)l * kv_layer_elems;
         uint16_t *vc = vc_base + (size_t)l * kv_layer_elems;
         dumpf(ctx, h, H, M, "L%d.in", l);
-        if ((rc = launch_rms_norm(ctx, h, L.attn_norm, xn, H, M, c.eps, VB_OUT_BF16))) return rc;
-        dumpf(ctx, xn, H, M, "L%d.attn_norm", l);
         MatmulOut o;
         o.y = qkv;
         o.flags = VB_OUT_BF16;
-        if ((rc = launch_matmul(ctx, L.qkv, xn, M, 0, 0, o))) return rc;
+        // on the tensor-core path the RMSNorm (and below the SwiGLU) is
+        // computed inside the mat-mul's activation prologue, except when the
+        // stage itself is dumped
+        if (!dumping && matmul_uses_gemm(ctx, L.qkv, M)) {
+            GemmPro pro;
+            pro.norm_w = L.attn_norm;
+            pro.eps = c.eps;
+            if ((rc = launch_matmul_pro(ctx, L.qkv, h, M, 0, pro, o))) return rc;
+        } else {
+            if ((rc = launch_rms_norm(ctx, h, L.attn_norm, xn, H, M, c.eps, VB_OUT_BF16))) return rc;
+            dumpf(ctx, xn, H, M, "L%d.attn_norm", l);
+            if ((rc = launch_matmul(ctx, L.qkv, xn, M, 0, 0, o))) return rc;
+        }
         dumpf(ctx, qkv, QKV, M, "L%d.qkv", l);
         if (!c.no_rope) {
             if ((rc = launch_rope(ctx, qkv, QKV, c.head_dim, c.n_heads, M, tt.pos, cs, VB_OUT_BF16))) return rc;
@@ -374,19 +384,32 @@ static int run_layers(vb_ctx *ctx, vb_lm *lm, int M, float *h, const TokenTables
         dumpf(ctx, a, H, M, "L%d.o", l);
         if (!fuse_res && (rc = launch_residual(ctx, h, a, scale, h, (int64_t)M * H, VB_OUT_BF16))) return rc;
         dumpf(ctx, h, H, M, "L%d.h_attn", l);
-        if ((rc = launch_rms_norm(ctx, h, L.ffn_norm, xn, H, M, c.eps, VB_OUT_BF16))) return rc;
-        dumpf(ctx, xn, H, M, "L%d.ffn_norm", l);
         o.y = gu;
-        if ((rc = launch_matmul(ctx, L.gu, xn, M, 0, 0, o))) return rc;
+        if (!dumping && matmul_uses_gemm(ctx, L.gu, M)) {
+            GemmPro pro;
+            pro.norm_w = L.ffn_norm;
+            pro.eps = c.eps;
+            if ((rc = launch_matmul_pro(ctx, L.gu, h, M, 0, pro, o))) return rc;
+        } else {
+            if ((rc = launch_rms_norm(ctx, h, L.ffn_norm, xn, H, M, c.eps, VB_OUT_BF16))) return rc;
+            dumpf(ctx, xn, H, M, "L%d.ffn_norm", l);
+            if ((rc = launch_matmul(ctx, L.gu, xn, M, 0, 0, o))) return rc;
+        }
         dumpf(ctx, gu, 2 * c.ffn, M, "L%d.gu", l);
-        int64_t ne = (int64_t)M * c.ffn;
-        swiglu_rows_kernel<<<(unsigned)((ne + 255) / 256), 256, 0, ctx->stream>>>(gu, act, M, c.ffn);
-        VB_LAUNCH_CHECK(ctx, "swiglu_rows");
-        dumpf(ctx, act, c.ffn, M, "L%d.act", l);
         o.y = fuse_res ? h : a;
         o.res = fuse_res ? h : nullptr;
         o.res_scale = scale;
-        if ((rc = launch_matmul(ctx, L.down, act, M, 0, 0, o))) return rc;
+        if (!dumping && matmul_uses_gemm(ctx, L.down, M)) {
+            GemmPro pro;
+            pro.swiglu_f = (int)c.ffn;
+            if ((rc = launch_matmul_pro(ctx, L.down, gu, M, 2 * c.ffn, pro, o))) return rc;
+        } else {
+            int64_t ne = (int64_t)M * c.ffn;
+            swiglu_rows_kernel<<<(unsigned)((ne + 255) / 256), 256, 0, ctx->stream>>>(gu, act, M, c.ffn);
+            VB_LAUNCH_CHECK(ctx, "swiglu_rows");
+            dumpf(ctx, act, c.ffn, M, "L%d.act", l);
+            if ((rc = launch_matmul(ctx, L.down, act, M, 0, 0, o))) return rc;
+        }
         o.res = nullptr;
         dumpf(ctx, a, H, M, "L%d.down", l);
         if (!fuse_res && (rc = launch_residual(ctx, h, a, scale, h, (int64_t)M * H, VB_OUT_BF16))) return rc;
