@@ -25,7 +25,6 @@ namespace vb {
 constexpr int ATT_CH = 64;         // K/V rows per CTA
 constexpr int ATT_WARPS = 8;
 constexpr int ATT_HD_MAX = 256;
-constexpr int ATT_SEG_PAIRS = 16;   // (token, head) pairs per segment-attention CTA
 
 struct AttnArgs {
     const float *q;
@@ -148,81 +147,63 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) attn_chunk_kernel(AttnArgs a) 
     }
 }
 
-// Bidirectional segments of T <= 32 tokens (LocDiT, LocEnc): a CTA per
-// (KV group, segment, 16 (token, query head) pairs of the group) stages the
-// segment's K/V rows once for its pairs, one pair per warp at a time.  Per pair the arithmetic is
-// attn_chunk_kernel's with one chunk (same order of every fp32 operation),
-// so the results are identical while K/V are read once per segment instead
-// of once per token.
+// Bidirectional segments of T <= 32 tokens (LocDiT, LocEnc): one CTA per
+// (KV group, segment) stages the segment's K/V rows once (bf16 -> fp32 in
+// shared memory) and its warps take the group's (token, query head) pairs.
+// A lane owns head dimensions lane, lane + 32, ...: each score is the warp
+// sum of the lanes' partial dot products, so all 32 lanes work on every key
+// (T is well below 32 here).  Scores scaled by 1/sqrt(head_dim), softmax
+// with expf in fp32, the output divided by the sum (IEEE division).
+template <int DPL>   // head_dim / 32
 __global__ void __launch_bounds__(ATT_WARPS * 32) attn_segment_kernel(AttnArgs a, int T) {
-    extern __shared__ __align__(16) uint32_t sm[];
+    extern __shared__ __align__(16) float smf[];
+    constexpr int HD = DPL * 32;
     const int g = blockIdx.x, sgi = blockIdx.y;
-    const int HD = a.head_dim, HW = HD >> 1;
-    const int rw = (HW & 1) ? HW : HW + 1;
     const int qpk = a.n_heads / a.n_kv;
-    uint32_t *ks = sm;                                          // [T][rw]
-    uint32_t *vs = ks + 32 * rw;                                // [T][rw]
-    float *qs = reinterpret_cast<float *>(vs + 32 * rw);        // [warps][HD]
-    float *es = qs + ATT_WARPS * HD;                            // [warps][32]
+    float *ks = smf;              // [T][HD]
+    float *vs = ks + T * HD;      // [T][HD]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t base = ((int64_t)g * a.n_rows + (int64_t)sgi * T) * HW;
-    const uint32_t *kg = reinterpret_cast<const uint32_t *>(a.k) + base;
-    const uint32_t *vg = reinterpret_cast<const uint32_t *>(a.v) + base;
-    for (int i = threadIdx.x; i < T * HW; i += blockDim.x) {
-        const int r = i / HW, w = i % HW;
-        ks[r * rw + w] = __ldg(kg + i);
-        vs[r * rw + w] = __ldg(vg + i);
+    const int64_t base = ((int64_t)g * a.n_rows + (int64_t)sgi * T) * HD;
+    for (int i = threadIdx.x; i < T * HD; i += blockDim.x) {
+        ks[i] = bf16_to_f(a.k[base + i]);
+        vs[i] = bf16_to_f(a.v[base + i]);
     }
     __syncthreads();
-    float *qv = qs + warp * HD;
-    float *e = es + warp * 32;
-    const int pr_end = min(T * qpk, (int)(blockIdx.z + 1) * ATT_SEG_PAIRS);
-    for (int pr = blockIdx.z * ATT_SEG_PAIRS + warp; pr < pr_end; pr += ATT_WARPS) {
-        const int t = pr / qpk, j = pr % qpk, h = g * qpk + j;
+    for (int pr = warp; pr < T * qpk; pr += ATT_WARPS) {
+        const int t = pr / qpk, h = g * qpk + pr % qpk;
         const int64_t tok = (int64_t)sgi * T + t;
-        for (int d = lane; d < HD; d += 32) qv[d] = a.q[tok * a.ldq + (int64_t)h * HD + d];
-        __syncwarp();
-        float s = -INFINITY;
-        if (lane < T) {
-            float acc = 0.0f;
-            const uint32_t *kr = ks + lane * rw;
-            for (int w = 0; w < HW; w++) {
-                const uint32_t kk = kr[w];
-                acc = fmaf(__uint_as_float(kk << 16), qv[2 * w], acc);
-                acc = fmaf(__uint_as_float(kk & 0xffff0000u), qv[2 * w + 1], acc);
+        const float *qr = a.q + tok * a.ldq + (int64_t)h * HD;
+        float qv[DPL];
+#pragma unroll
+        for (int u = 0; u < DPL; u++) qv[u] = qr[lane + 32 * u];
+        float sc[32];
+        float mx = -INFINITY;
+#pragma unroll
+        for (int p = 0; p < 32; p++) {
+            if (p < T) {                       // uniform over the warp
+                float part = 0.0f;
+#pragma unroll
+                for (int u = 0; u < DPL; u++) part = fmaf(qv[u], ks[p * HD + lane + 32 * u], part);
+                const float sp = __fmul_rn(warp_sum(part), a.kq_scale);
+                sc[p] = sp;
+                mx = fmaxf(mx, sp);
             }
-            s = __fmul_rn(acc, a.kq_scale);
         }
-        const float mx = warp_max(s);
-        const float ev = (lane < T) ? expf(s - mx) : 0.0f;
-        e[lane] = ev;
-        float l = 0.0f;
-        l += ev;
-        l = warp_sum(l);
-        __syncwarp();
-        float o[ATT_HD_MAX / 32];
+        float l = 0.0f, o[DPL];
 #pragma unroll
-        for (int u = 0; u < ATT_HD_MAX / 32; u++) o[u] = 0.0f;
-        for (int p = 0; p < T; p++) {
-            const float ep = e[p];
-            const uint32_t *vr = vs + p * rw;
+        for (int u = 0; u < DPL; u++) o[u] = 0.0f;
 #pragma unroll
-            for (int u = 0; u < ATT_HD_MAX / 32; u++) {
-                const int d = lane + 32 * u;
-                if (d < HD) {
-                    const uint32_t vv = vr[d >> 1];
-                    const float vf = __uint_as_float((d & 1) ? (vv & 0xffff0000u) : (vv << 16));
-                    o[u] = fmaf(ep, vf, o[u]);
-                }
+        for (int p = 0; p < 32; p++) {
+            if (p < T) {
+                const float ep = expf(sc[p] - mx);
+                l += ep;
+#pragma unroll
+                for (int u = 0; u < DPL; u++) o[u] = fmaf(ep, vs[p * HD + lane + 32 * u], o[u]);
             }
         }
         float *dst = a.out + tok * a.ldo + (int64_t)h * HD;
 #pragma unroll
-        for (int u = 0; u < ATT_HD_MAX / 32; u++) {
-            const int d = lane + 32 * u;
-            if (d < HD) dst[d] = __fdiv_rn(o[u], l);
-        }
-        __syncwarp();
+        for (int u = 0; u < DPL; u++) dst[lane + 32 * u] = __fdiv_rn(o[u], l);
     }
 }
 
@@ -262,6 +243,7 @@ static size_t attn_smem(int n_heads, int n_kv, int head_dim) {
 
 int init_attention(vb_ctx *ctx) {
     VB_CHECK(ctx, cudaFuncSetAttribute(attn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+    VB_CHECK(ctx, cudaFuncSetAttribute(attn_segment_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
     return VB_OK;
 }
 
@@ -269,11 +251,10 @@ int launch_attention_segments(vb_ctx *ctx, const float *q, int64_t ldq, const ui
                               int n_rows, int n_seg, int T, int n_heads, int n_kv, int head_dim, float *out,
                               int64_t ldo) {
     if (n_seg == 0) return VB_OK;
-    if (!q || !k || !v || !out || T <= 0 || T > 32 || n_kv <= 0 || n_heads % n_kv || head_dim % 2 ||
+    if (!q || !k || !v || !out || T <= 0 || T > 32 || n_kv <= 0 || n_heads % n_kv || head_dim % 32 ||
         head_dim > ATT_HD_MAX)
         return set_error(ctx, VB_ERR_INVALID_ARG, "segment attention: bad argument");
-    const int HW = head_dim >> 1, rw = (HW & 1) ? HW : HW + 1;
-    const size_t sm = (size_t)2 * 32 * rw * 4 + (size_t)ATT_WARPS * head_dim * 4 + (size_t)ATT_WARPS * 32 * 4;
+    const size_t sm = (size_t)2 * T * head_dim * 4;
     AttnArgs a{};
     a.q = q;
     a.ldq = ldq ? ldq : (int64_t)n_heads * head_dim;
@@ -286,9 +267,17 @@ int launch_attention_segments(vb_ctx *ctx, const float *q, int64_t ldq, const ui
     a.out = out;
     a.ldo = ldo ? ldo : (int64_t)n_heads * head_dim;
     a.kq_scale = 1.0f / sqrtf((float)head_dim);
-    const int pairs = T * (n_heads / n_kv);
-    attn_segment_kernel<<<dim3((unsigned)n_kv, (unsigned)n_seg, (unsigned)((pairs + ATT_SEG_PAIRS - 1) / ATT_SEG_PAIRS)),
-                          ATT_WARPS * 32, sm, ctx->stream>>>(a, T);
+    const dim3 grid((unsigned)n_kv, (unsigned)n_seg);
+    switch (head_dim / 32) {
+        case 1: attn_segment_kernel<1><<<grid, ATT_WARPS * 32, sm, ctx->stream>>>(a, T); break;
+        case 2: attn_segment_kernel<2><<<grid, ATT_WARPS * 32, sm, ctx->stream>>>(a, T); break;
+        case 3: attn_segment_kernel<3><<<grid, ATT_WARPS * 32, sm, ctx->stream>>>(a, T); break;
+        case 4: attn_segment_kernel<4><<<grid, ATT_WARPS * 32, sm, ctx->stream>>>(a, T); break;
+        case 5: attn_segment_kernel<5><<<grid, ATT_WARPS * 32, sm, ctx->stream>>>(a, T); break;
+        case 6: attn_segment_kernel<6><<<grid, ATT_WARPS * 32, sm, ctx->stream>>>(a, T); break;
+        case 7: attn_segment_kernel<7><<<grid, ATT_WARPS * 32, sm, ctx->stream>>>(a, T); break;
+        default: attn_segment_kernel<8><<<grid, ATT_WARPS * 32, sm, ctx->stream>>>(a, T); break;
+    }
     VB_LAUNCH_CHECK(ctx, "attn_segment");
     return VB_OK;
 }

@@ -364,7 +364,7 @@ static int run_layers(vb_ctx *ctx, vb_lm *lm, int M, float *h, const TokenTables
         if ((rc = launch_kv_write(ctx, qkv + QD, qkv + QD + KD, QKV, kc, vc, kv_rows, M, c.n_kv_heads, c.head_dim,
                                   tt.dst)))
             return rc;
-        if (tt.seg_T > 0 && tt.seg_T <= 32) {
+        if (tt.seg_T > 0 && tt.seg_T <= 32 && c.head_dim % 32 == 0) {
             if ((rc = launch_attention_segments(ctx, qkv, QKV, kc, vc, kv_rows, M / tt.seg_T, tt.seg_T, c.n_heads,
                                                 c.n_kv_heads, c.head_dim, att, QD)))
                 return rc;
