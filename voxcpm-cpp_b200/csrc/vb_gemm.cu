@@ -797,8 +797,10 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
     // tile that still gives about one tile per SM, then a K split only when
     // tiles are scarce.  Q8_0 (three MMAs per k-step, so per-unit work is
     // heavier): a small cost model of the persistent grid, time ~ waves x
-    // (BN x k-tiles per unit + a fixed per-unit overhead), which also
-    // splits K to even out the last wave.
+    // (BN x k-tiles per unit + a fixed per-unit overhead) + the split-K
+    // reduction (the last CTA of a tile reads every split's partials in
+    // turn: ~40 units per split per 16 columns, fitted to M = 64 and
+    // M = 1408 sweeps of splits 1-7 x BN 32-128).
     const int tiles_n = (N + GM_BM - 1) / GM_BM;
     const int mr = (int)((M + 15) / 16 * 16);
     const int kt_total = K / GM_BK;
@@ -817,12 +819,13 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
         double best = 1e300;
         for (int cand : {128, 64, 32, 16}) {
             if (cand > mr && (cand >> 1) >= mr) continue;   // no wider than M needs
+            if (cand == 16 && mr > 16) continue;             // N = 16 MMAs: issue-bound, measured slower
             const int64_t tiles = (int64_t)tiles_n * ((M + cand - 1) / cand);
             for (int sp = 1; sp <= std::max(1, kt_total / 2); sp++) {
                 const int kps = (kt_total + sp - 1) / sp;
                 const int64_t units = tiles * ((kt_total + kps - 1) / kps);
                 const int64_t waves = (units + ctx->sm_count - 1) / ctx->sm_count;
-                const double t = (double)waves * ((double)cand * kps + 2048.0) + (sp > 1 ? 0.02 * sp * cand : 0.0);
+                const double t = (double)waves * ((double)cand * kps + 2048.0) + (sp > 1 ? 40.0 * sp * (cand / 16) : 0.0);
                 if (t < best * 0.999) { best = t; BN = cand; splits = sp; }
                 if (units >= 4 * ctx->sm_count) break;
             }
