@@ -71,7 +71,7 @@ struct GemmArgs {
     // AudioVAE epilogue (vae != 0): v = acc + bias[n % cb] (+ skip); y = v
     // (if y); out_x = snake(alpha)(sr(v)) (if out_x)
     int vae, cb;
-    uint32_t small_off;     // tf32: TMEM column offset of the cross-term accumulator (hi*lo + lo*hi)
+    uint32_t small_off;     // Q8_0 / tf32: TMEM column offset of the cross-term accumulator (hi*lo + lo*hi)
     const float *skip;
     float *out_x;
     const float *alpha, *sr_scale, *sr_bias;
@@ -114,6 +114,15 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
+
+// Programmatic dependent launch: kernels of the M >= 16 chain are launched
+// so that they may start while the previous kernel of the stream finishes;
+// this waits until that kernel has completed and its writes are visible
+// (a no-op when the launch was not programmatic).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next programmatic launch of the stream begin scheduling its CTAs
+// (they still wait for this grid to complete before touching memory).
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -263,6 +272,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
+    // everything above (barrier init, TMEM allocation) overlaps the previous
+    // kernel; operands and outputs are touched only after it has finished
+    pdl_wait();
+    pdl_trigger();
 
     // Tiles t = blockIdx.x, + gridDim.x, ...; split fastest, then the
     // activation tile, so CTAs running at the same time share weight tiles.
@@ -355,8 +368,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                             const uint32_t acc = (i | k) != 0;
                             umma_f16(acc_t, sw128_desc(ahi + 32 * k), sw128_desc(bhi + 32 * k), idesc, acc);
                             if (a.q8) {
-                                umma_f16(acc_t, sw128_desc(ahi + 32 * k), sw128_desc(blo + 32 * k), idesc, 1u);
-                                umma_f16(acc_t, sw128_desc(alo + 32 * k), sw128_desc(bhi + 32 * k), idesc, 1u);
+                                // the two cross terms (2^-11 of hi*hi) accumulate apart
+                                const uint32_t acc_s = acc_t + a.small_off;
+                                umma_f16(acc_s, sw128_desc(ahi + 32 * k), sw128_desc(blo + 32 * k), idesc, acc);
+                                umma_f16(acc_s, sw128_desc(alo + 32 * k), sw128_desc(bhi + 32 * k), idesc, 1u);
                             }
                         }
                         umma_commit(&empty[s]);
@@ -466,7 +481,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 uint32_t v[16];
                 const uint32_t ta = tmem + (uint32_t)buf * acc_cols + ((uint32_t)(q * 32) << 16) + (uint32_t)(j * 16);
                 tmem_ld16(ta, v);
-                if constexpr (TF32) {
+                if (TF32 || a.q8) {
                     uint32_t w[16];
                     tmem_ld16(ta + a.small_off, w);
 #pragma unroll
@@ -619,6 +634,8 @@ __device__ __forceinline__ void load8(const float *p, bool vec, float (&v)[8]) {
 // down-projection reads the gate/up output directly.
 __global__ void gemm_act_kernel(const float *x, int64_t ldx, int64_t x_mod, int M, int K, int q8, int rule, int vec,
                                 int swiglu_f, __half *bh, __half *bl) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // item of 8 values
     const int ipr = K >> 3;
     const bool valid = e < (int64_t)M * ipr;
@@ -647,6 +664,8 @@ __global__ void __launch_bounds__(ACT_NORM_THREADS) gemm_act_norm_kernel(const f
                                                                           int K, int q8, int rule, int vec,
                                                                           const float *__restrict__ nw, float eps,
                                                                           __half *bh, __half *bl) {
+    pdl_trigger();
+    pdl_wait();
     const int m = blockIdx.x;
     const float *xr = x + (int64_t)(m % x_mod) * ldx;
     const int ipr = K >> 3;
@@ -780,6 +799,24 @@ int init_gemm(vb_ctx *ctx) {
     return VB_OK;
 }
 
+// Launch with programmatic stream serialization (the kernel begins with
+// pdl_wait before it reads anything the previous kernel wrote).
+template <typename... KArgs, typename... Args>
+static cudaError_t pdl_launch(vb_ctx *ctx, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 bool gemm_supported(vb_weight w, int64_t M) {
     if (M < 16 || !encode_fn()) return false;
     if (w->type == VB_TYPE_Q8_0) return w->K % GM_BK == 0;
@@ -799,8 +836,8 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
     // heavier): a small cost model of the persistent grid, time ~ waves x
     // (BN x k-tiles per unit + a fixed per-unit overhead) + the split-K
     // reduction (the last CTA of a tile reads every split's partials in
-    // turn: ~40 units per split per 16 columns, fitted to M = 64 and
-    // M = 1408 sweeps of splits 1-7 x BN 32-128).
+    // turn: ~40 units per split per 16 columns above M = 128, fitted to
+    // M = 1408 sweeps of splits 1-4 x BN 64-128).
     const int tiles_n = (N + GM_BM - 1) / GM_BM;
     const int mr = (int)((M + 15) / 16 * 16);
     const int kt_total = K / GM_BK;
@@ -819,17 +856,24 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
         double best = 1e300;
         for (int cand : {128, 64, 32, 16}) {
             if (cand > mr && (cand >> 1) >= mr) continue;   // no wider than M needs
-            if (cand == 16 && mr > 16) continue;             // N = 16 MMAs: issue-bound, measured slower
+            if (cand == 16 && M > 128) continue;             // N = 16 MMAs: issue-bound, measured slower
             const int64_t tiles = (int64_t)tiles_n * ((M + cand - 1) / cand);
             for (int sp = 1; sp <= std::max(1, kt_total / 2); sp++) {
                 const int kps = (kt_total + sp - 1) / sp;
                 const int64_t units = tiles * ((kt_total + kps - 1) / kps);
                 const int64_t waves = (units + ctx->sm_count - 1) / ctx->sm_count;
-                const double t = (double)waves * ((double)cand * kps + 2048.0) + (sp > 1 ? 40.0 * sp * (cand / 16) : 0.0);
+                // M <= 128 keeps a light split price: its shorter accumulation
+                // chains hold the tightest (stage-level) parity gates
+                const double split_cost = M > 128 ? 40.0 * sp * (cand / 16) : 0.02 * sp * cand;
+                const double t = (double)waves * ((double)cand * kps + 2048.0) + (sp > 1 ? split_cost : 0.0);
                 if (t < best * 0.999) { best = t; BN = cand; splits = sp; }
                 if (units >= 4 * ctx->sm_count) break;
             }
         }
+    }
+    if (BN == 0) {      // no candidate passed the filters (not expected): one plain tile width
+        BN = std::min(64, mr);
+        splits = 1;
     }
     const int tiles_m = (int)((M + BN - 1) / BN);
     const int tiles = tiles_m * tiles_n;
@@ -845,9 +889,12 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
     int n_tma = (int)std::min<size_t>(GM_MAX_STAGES, (GM_SMEM_BUDGET - conv_bytes) / stage);
     if (n_tma < 2) return set_error(ctx, VB_ERR_INVALID_ARG, "gemm: tile does not fit shared memory");
     const size_t smem = (size_t)n_tma * stage + conv_bytes + 1024;
-    uint32_t cols = 32;
-    while (cols < (uint32_t)BN) cols <<= 1;
-    cols *= 2;   // two accumulators: the epilogue of one tile overlaps the next tile's MMAs
+    uint32_t pcols = 32;
+    while (pcols < (uint32_t)BN) pcols <<= 1;
+    // two accumulator buffers (the epilogue of one tile overlaps the next
+    // tile's MMAs); Q8_0 keeps the hi*hi and cross-term sums side by side
+    // in each (BN <= 128, so at most 4 x 128 columns)
+    const uint32_t cols = (q8 ? 4u : 2u) * pcols;
 
     // activation operands
     const size_t ab = (size_t)M * K * 2;
@@ -863,11 +910,11 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
         if (pro && pro->norm_w) {
             if (K > 8 * ACT_NORM_THREADS * ACT_NORM_ITEMS)
                 return set_error(ctx, VB_ERR_INVALID_ARG, "gemm: fused RMSNorm row of %d values is too wide", K);
-            gemm_act_norm_kernel<<<(unsigned)M, ACT_NORM_THREADS, 0, ctx->stream>>>(
-                x, lx, xm, K, q8 ? 1 : 0, ctx->qrule, vec, pro->norm_w, pro->eps, bh, bl);
+            VB_CHECK(ctx, pdl_launch(ctx, gemm_act_norm_kernel, dim3((unsigned)M), dim3(ACT_NORM_THREADS), 0, x, lx, xm,
+                                     K, q8 ? 1 : 0, ctx->qrule, vec, pro->norm_w, pro->eps, bh, bl));
         } else {
-            gemm_act_kernel<<<(unsigned)((items + 255) / 256), 256, 0, ctx->stream>>>(
-                x, lx, xm, (int)M, K, q8 ? 1 : 0, ctx->qrule, vec, pro ? pro->swiglu_f : 0, bh, bl);
+            VB_CHECK(ctx, pdl_launch(ctx, gemm_act_kernel, dim3((unsigned)((items + 255) / 256)), dim3(256), 0, x, lx,
+                                     xm, (int)M, K, q8 ? 1 : 0, ctx->qrule, vec, pro ? pro->swiglu_f : 0, bh, bl));
         }
         VB_LAUNCH_CHECK(ctx, "gemm_act");
     }
@@ -912,6 +959,7 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
     g.n_tma = n_tma;
     g.n_conv = n_conv;
     g.tmem_cols = cols;
+    g.small_off = q8 ? pcols : 0u;
     g.sc = w->scales;
     g.y = out.y;
     g.bias = out.bias;
@@ -933,8 +981,8 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
     }
     const int n_work = tiles * splits;
     const CUtensorMap &twm = *reinterpret_cast<const CUtensorMap *>(w->tmap);
-    gemm_kernel<false><<<(unsigned)std::min(n_work, ctx->sm_count), GM_THREADS, smem, ctx->stream>>>(twm, twm, am->th,
-                                                                                                  am->tl, g);
+    VB_CHECK(ctx, pdl_launch(ctx, gemm_kernel<false>, dim3((unsigned)std::min(n_work, ctx->sm_count)),
+                             dim3(GM_THREADS), smem, twm, twm, am->th, am->tl, g));
     VB_LAUNCH_CHECK(ctx, "gemm");
     return VB_OK;
 }
