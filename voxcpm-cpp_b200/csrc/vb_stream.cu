@@ -192,6 +192,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                     default: fast_done = false; break;
                 }
                 if (!ok) bad = true;
+            } else if (op.wtype == VB_TYPE_F16 && M == 1 && (K == 1024 || (K == 2048 && op.epi != EPI_SWIGLU))) {
+                const uint16_t *xh = reinterpret_cast<const uint16_t *>(xq);
+                bool ok = K == 1024 ? f16_m1_op<16, 8>(op, wslot, xh, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns)
+                                    : f16_m1_op<32, 8>(op, wslot, xh, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns);
+                fast_done = true;
+                if (!ok) bad = true;
             }
             const int R = op.rows_per_chunk;
             for (int64_t r = r0; !fast_done && r < r1; r += R) {

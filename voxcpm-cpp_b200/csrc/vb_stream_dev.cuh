@@ -262,6 +262,69 @@ __device__ __forceinline__ bool q8_m1_op(const StreamOp &op, const uint8_t *wslo
 }
 
 
+
+// F16 decode fast path (M = 1): as q8_m1_op, LPR lanes own one weight row and
+// lane s of a row takes the 16-byte (8-value) pieces s, s+LPR, ...; the
+// lane's fp16 activation pieces stay in registers for the whole op.  Each
+// piece contributes eight fp16 x fp16 products accumulated in fp32; a row is
+// reduced over its LPR lanes.  EPI_SWIGLU needs RPW even (LPR <= 16).
+template <int LPR, int IT>
+__device__ __forceinline__ bool f16_m1_op(const StreamOp &op, const uint8_t *wslot, const uint16_t *xh,
+                                          uint64_t *full, uint64_t *empty, int &slot, uint32_t &phase, int64_t r0,
+                                          int64_t r1, int cw, int lane, volatile int *abort_flag, int *err, int ns) {
+    constexpr int RPW = 32 / LPR;
+    constexpr int RPP = RPW * ST_CONSUMER_WARPS;
+    const int K = op.K;
+    const int ls = lane % LPR, lr = lane / LPR;
+    int4 xr[IT];
+#pragma unroll
+    for (int i = 0; i < IT; i++) xr[i] = *reinterpret_cast<const int4 *>(xh + (ls + LPR * i) * 8);
+    float *y = op.y;
+    const float *bias = op.bias;
+    const bool b16 = op.flags & VB_OUT_BF16;
+    const bool residual = op.epi == EPI_RESIDUAL;
+    const bool swz = op.epi == EPI_SWIGLU;
+    const int R = op.rows_per_chunk;
+    for (int64_t r = r0; r < r1; r += R) {
+        const int nr = (int)((r1 - r) < R ? (r1 - r) : R);
+        if (!wait_phase(&full[slot], phase, abort_flag)) {
+            if (!*abort_flag) { atomicCAS(err, 0, STREAM_TIMEOUT_FULL); *abort_flag = 1; }
+            return false;
+        }
+        const uint8_t *wt = wslot + (size_t)slot * ST_SLOT;
+        for (int jb = cw * RPW; jb < nr; jb += RPP) {   // warp-uniform
+            const int j = jb + lr;
+            const bool valid = j < nr;
+            const int jj = valid ? j : jb;
+            const uint8_t *wr = wt + (int64_t)slot_row(jj, nr, swz) * K * 2;
+            float acc = 0.0f;
+#pragma unroll
+            for (int i = 0; i < IT; i++)
+                acc = dot8_f16(*reinterpret_cast<const int4 *>(wr + (ls + LPR * i) * 16), xr[i], acc);
+#pragma unroll
+            for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (swz) {
+                const float up = __shfl_down_sync(0xffffffffu, acc, LPR);   // row j + 1
+                if (valid && ls == 0 && !(lr & 1)) swiglu_store(op, 0, (r + j) >> 1, acc, up);
+            } else if (valid && ls == 0) {
+                const int64_t n = r + j;
+                if (residual) {
+                    y[n] = stream_epilogue(op, 0, n, acc);
+                } else {
+                    float v = acc;
+                    if (bias) v = __fadd_rn(v, bias[n]);
+                    if (b16) v = bf16r(v);
+                    y[n] = v;
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (++slot == ns) { slot = 0; phase ^= 1u; }
+    }
+    return true;
+}
+
 }  // namespace vb
 
 namespace vb {
