@@ -423,9 +423,9 @@ def run_b200(args, rank, world, local_rank):
 def sweep_rows(ctx, q8_weights, args):
     """BASELINE config 2 sweep: the 7 projection shapes x M x {Q8_0, F16}.
     M <= 2 runs as one streaming program over distinct weights (> L2);
-    larger M runs the per-launch GEMV kernel on one layer's weights (the
-    tcgen05 GEMM for M >= 16 is not built yet, so these rows show today's
-    path).  GB/s counts algorithmic bytes, TFLOP/s counts 2*M*N*K."""
+    M >= 16 runs one vb_matmul per weight of one layer (the tcgen05 GEMM,
+    weights L2-resident after the first pass).  GB/s counts algorithmic
+    bytes, TFLOP/s counts 2*M*N*K."""
     import torch
     import vcpm_b200 as vb
     rows = []
@@ -462,7 +462,7 @@ def sweep_rows(ctx, q8_weights, args):
         nbytes = sum((q8_bytes(K, N) if wtype == "q8_0" else 2 * N * K) + 4 * K * M + 4 * N * M for K, N, _ in ws)
         flops = sum(2 * M * N * K for K, N, _ in ws)
         ms = time_fn(lambda: [ctx.matmul(w, X, M, Y) for K, N, w in ws], 5)
-        return {"wtype": wtype, "M": M, "path": "per-launch GEMV (weights L2-resident)",
+        return {"wtype": wtype, "M": M, "path": "tcgen05 GEMM per launch (weights L2-resident)",
                 "gbs": nbytes / (ms * 1e-3) / 1e9, "tflops": flops / (ms * 1e-3) / 1e12}
 
     q8 = [(K, N, w) for (name, K, N, w) in q8_weights]
