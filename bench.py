@@ -52,6 +52,27 @@ OUT_PER_LAYER = sum(s[2] for s in SHAPES)
 NCU_TRAFFIC_STEP = 1_412_116_664
 
 
+# ------------------------------------------------------ multi-rank helpers
+def max_over_ranks(values, world, device="cuda"):
+    """Element-wise maximum of per-rank timings; every rank calls it
+    (one all-reduce on the default process group when world > 1)."""
+    import torch
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return [float(v) for v in t]
+
+
+def aggregate_gbs(bytes_per_rank_step, steps, world, ms_max):
+    """Whole-job GB/s: the bytes every rank processed / the slowest rank's time."""
+    return world * bytes_per_rank_step * steps / (ms_max * 1e-3) / 1e9
+
+
+def utterances_per_rank(total, world):
+    """Contiguous shard of the end-to-end utterances per rank (weak scaling)."""
+    return max(1, total // world)
+
+
 def q8_bytes(K, N):
     return N * K // 32 * 34
 
@@ -356,14 +377,9 @@ def run_b200(args, rank, world, local_rank):
     ms_e2e = timed(e2e_step, args.steps)
     ctx.sync()
 
-    # max over ranks
-    t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device="cuda")
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms, ms_e2e = float(t[0]), float(t[1])
-
-    value = world * STEP_BYTES * args.steps / (ms * 1e-3) / 1e9
-    e2e_value = world * STEP_BYTES * args.steps / (ms_e2e * 1e-3) / 1e9
+    ms, ms_e2e = max_over_ranks([ms, ms_e2e], world)
+    value = aggregate_gbs(STEP_BYTES, args.steps, world, ms)
+    e2e_value = aggregate_gbs(STEP_BYTES, args.steps, world, ms_e2e)
     peak, peak_kind = load_peaks()
     per_gpu = value / world
 
@@ -758,7 +774,7 @@ def e2e_bench(ctx, host_layers, args, rank, world, gpu_index=0):
     import torch
     import vcpm_b200 as vb
     rng = np.random.default_rng(11 + rank)
-    B = max(1, args.e2e_utts // world)
+    B = utterances_per_rank(args.e2e_utts, world)
     T, NP = 200, args.e2e_patches
 
     def q8(N, K):
@@ -861,10 +877,8 @@ def e2e_bench(ctx, host_layers, args, rank, world, gpu_index=0):
     vae_tflops = vae_flops(B * PATCH) / (vae_ms * 1e-3) / 1e12
     vst.close()
     vae.close()
-    tt = torch.tensor([pre_ms + steps_ms, pre_ms, steps_ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
-    total_ms = float(tt[0])
+    tt = max_over_ranks([pre_ms + steps_ms, pre_ms, steps_ms], world)
+    total_ms = tt[0]
     audio_s = B * world * NP * SAMPLES_PER_PATCH / SAMPLE_RATE
     gen.close()
     embed.release()
