@@ -50,7 +50,6 @@ constexpr int GM_SMEM_BUDGET = 220 * 1024;
 
 struct GemmArgs {
     int q8;                 // 1: Q8_0 weights (hi/lo split), 0: F16 weights
-    int tf32;               // 1: fp32 operands pre-split into tf32 hi/lo, three kind::tf32 MMAs
     int bk;                 // k elements per stage (64 fp16 / 32 tf32: one 128-byte swizzle row)
     int K, N, M, BN;
     int kt_total, kt_per_split, splits, tiles_m, tiles_n;
@@ -68,9 +67,9 @@ struct GemmArgs {
     int Mp;                 // tiles_m * BN
     unsigned *cnt;          // per-tile arrival counters (self-resetting)
     int *err;
-    // AudioVAE epilogue (vae != 0): v = acc + bias[n % cb] (+ skip); y = v
-    // (if y); out_x = snake(alpha)(sr(v)) (if out_x)
-    int vae, cb;
+    // AudioVAE epilogue (the tf32 instantiation): v = acc + bias[n % cb]
+    // (+ skip); y = v (if y); out_x = snake(alpha)(sr(v)) (if out_x)
+    int cb;
     uint32_t small_off;     // Q8_0 / tf32: TMEM column offset of the cross-term accumulator (hi*lo + lo*hi)
     const float *skip;
     float *out_x;
@@ -1059,7 +1058,6 @@ int launch_gemm_tf32(vb_ctx *ctx, Tf32Weight &w, const float *a_hi, const float 
         am->tf32 = true;
     }
     GemmArgs g{};
-    g.tf32 = 1;
     g.bk = BK;
     g.K = K;
     g.N = N;
@@ -1080,7 +1078,6 @@ int launch_gemm_tf32(vb_ctx *ctx, Tf32Weight &w, const float *a_hi, const float 
     g.seg_plain = 1;
     g.cnt = gs->cnt;
     g.err = gs->err;
-    g.vae = 1;
     g.small_off = pcols;
     g.cb = e.cb > 0 ? e.cb : N;
     g.skip = e.skip;
