@@ -462,7 +462,9 @@ int vb_vae_stream_reset(vb_ctx *ctx, vb_vae_stream s);
 /* latent: device [n_streams][n_timesteps][latent_dim] (time-major, as
  * vcpm_vae_stream_decode takes it); audio: device [n_streams][n_timesteps *
  * prod(rates)] in (-1, 1).  Both 16-byte aligned.  Enqueued on the context
- * stream; the caches advance by n_timesteps. */
+ * stream; the caches advance by n_timesteps.  The first call, and any call
+ * with more timesteps than the stream has seen, (re)allocates the stream's
+ * activation buffers (waiting for the stream first). */
 int vb_vae_stream_decode(vb_ctx *ctx, vb_vae_stream s, const float *latent, int n_timesteps, float *audio);
 void vb_vae_stream_destroy(vb_ctx *ctx, vb_vae_stream s);
 int vb_vae_stream_conv_cache_count(vb_vae_stream s);     /* 20 */
