@@ -138,13 +138,15 @@ def test_decoder_batched_slots_match_oracle(ctx):
     lm.close()
 
 
-@pytest.mark.parametrize("n", [1, 2])
-def test_decoder_full_width_agrees_with_per_op_path(ctx, n):
+@pytest.mark.parametrize("wtype,n", [(O.TYPE_Q8_0, 1), (O.TYPE_Q8_0, 2), (O.TYPE_F16, 1)])
+def test_decoder_full_width_agrees_with_per_op_path(ctx, wtype, n):
     """Projection shapes of the MiniCPM4 decode benchmark (hidden 2048, 16q/2kv,
     head_dim 128, FFN 6144) on two blocks: 40 steps through the decoder and,
     on a second cache, through vb_lm_forward(T = 1); the 40 steps cross the
-    32- and 64-row attention chunk boundaries."""
-    c, lm, _, _, _ = build_lm(ctx, O.TYPE_Q8_0, oracle=False, hidden=2048, n_heads=16, n_kv=2, head_dim=128,
+    32- and 64-row attention chunk boundaries.  F16 (n = 1: two rows of an
+    F16 K = 6144 operand exceed the streaming kernel's 16 KiB) runs the FFN
+    down projection (residual epilogue) with several warps per row."""
+    c, lm, _, _, _ = build_lm(ctx, wtype, oracle=False, hidden=2048, n_heads=16, n_kv=2, head_dim=128,
                               ffn=6144, n_layers=2)
     H, T = c["hidden"], 5
     kv_a = vb.KV(ctx, lm, n, 96)

@@ -96,6 +96,52 @@ def test_program_matches_per_op_launch(ctx):
     w.release()
 
 
+def test_f16_long_rows_split_over_warps(ctx):
+    """F16 M = 1 ops whose ring chunk holds 2 or 4 rows (K 4096 / 6144 / 8192),
+    so several warps share a row: ragged N (last chunks of one row, CTAs with
+    no rows), bias + bf16 epilogues, and dependent ops after them on the same
+    CTAs (the ring position must continue exactly where the split ops left
+    it)."""
+    cases = [  # K, N, bias, flags, group, wait_group, input (index of an earlier op or None)
+        (6144, 2048, True, vb.OUT_BF16, 0, -1, None),
+        (4096, 301, False, 0, 0, -1, None),
+        (8192, 150, True, 0, 0, -1, None),
+        (6144, 37, False, vb.OUT_BF16, 0, -1, None),
+        (2048, 8192, False, 0, 1, 0, 0),          # F16 K = 2048 reading op 0's output
+        (6144, 4096, False, 0, 2, 1, 4),          # then a long-row op reading op 4's output
+    ]
+    ops, keep = [], []
+    for i, (K, N, has_b, flags, g, wg, src) in enumerate(cases):
+        hw = S.weight(O.TYPE_F16, N, K)
+        w = ctx.weight(O.TYPE_F16, K, N, hw)
+        x = torch.from_numpy(S.normal((1, K))).cuda() if src is None else None
+        y = torch.zeros((1, N), dtype=torch.float32, device="cuda")
+        b = torch.from_numpy(S.normal(N, 0.3)).cuda() if has_b else None
+        keep.append(dict(hw=hw, w=w, x=x, y=y, b=b, K=K, N=N, flags=flags, src=src))
+    for i, c in enumerate(keep):
+        if c["src"] is not None:
+            c["x"] = keep[c["src"]]["y"][:, :c["K"]]
+        K, N, has_b, flags, g, wg, _ = cases[i]
+        ops.append(dict(w=c["w"], x=c["x"], y=c["y"], M=1, group=g, wait_group=wg, bias=c["b"], flags=flags))
+    prog = vb.Program(ctx, ops)
+    torch.cuda.synchronize()
+    for _ in range(2):
+        prog.run()
+    rc, err = prog.status()
+    assert rc == 0 and err == 0, ctx.last_error()
+    for c in keep:
+        ref = O.matmul(O.TYPE_F16, c["hw"], c["K"], c["N"], host(c["x"]))
+        if c["b"] is not None:
+            ref = ref + host(c["b"])
+        if c["flags"]:
+            S.assert_layer_close(host(c["y"]), O.bf16_round(ref), 1e-3)
+        else:
+            S.assert_matmul_close(host(c["y"]), ref, 1e-3)
+    prog.close()
+    for c in keep:
+        c["w"].release()
+
+
 def test_odd_shapes_and_scale_fallback(ctx):
     """K = 64 and 1024 (scales not bulk-copyable, read from global), N < #SMs
     (most CTAs own no rows), N not a multiple of the chunk."""

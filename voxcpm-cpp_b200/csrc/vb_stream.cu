@@ -9,8 +9,9 @@
 //   warp 0 (producer)   walks the program in order and, for this CTA's slice
 //                        of every weight, issues 1-D TMA bulk copies
 //                        (cp.async.bulk, no multicast) of row chunks into a
-//                        5-stage shared-memory ring, each stage completing
-//                        an mbarrier by transaction bytes;
+//                        6-stage shared-memory ring (5 when the program
+//                        needs the aux scratch), each stage completing an
+//                        mbarrier by transaction bytes;
 //   warps 1..8          quantize the activation of each op once into shared
 //   (consumers)          memory (ggml's Q8_0 rule, bit-exact), then reduce
 //                        every row chunk from the ring with dp4a block dots
@@ -47,6 +48,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     __shared__ StreamOp s_ops[2];
     __shared__ int2 s_rows[ST_MAX_OPS];        // rows [x, y) of this CTA's k-th op
     __shared__ uint16_t s_idx[ST_MAX_OPS];     // program index of this CTA's k-th op
+    __shared__ float s_part[2 * ST_CONSUMER_WARPS];   // row-segment partials of f16_m1_split_op
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, cta = blockIdx.x;
@@ -196,6 +198,19 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
                 const uint16_t *xh = reinterpret_cast<const uint16_t *>(xq);
                 bool ok = K == 1024 ? f16_m1_op<16, 8>(op, wslot, xh, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns)
                                     : f16_m1_op<32, 8>(op, wslot, xh, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns);
+                ring_advance(slot, phase, (r1 - r0 + op.rows_per_chunk - 1) / op.rows_per_chunk, ns);
+                fast_done = true;
+                if (!ok) bad = true;
+            } else if (op.wtype == VB_TYPE_F16 && M == 1 && op.epi != EPI_SWIGLU &&
+                       ((K == 4096 && op.rows_per_chunk == 4) || ((K == 6144 || K == 8192) && op.rows_per_chunk == 2))) {
+                const uint16_t *xh = reinterpret_cast<const uint16_t *>(xq);
+                bool ok;
+                switch (K) {
+                    case 4096: ok = f16_m1_split_op<2, 8>(op, wslot, xh, s_part, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns); break;
+                    case 6144: ok = f16_m1_split_op<4, 6>(op, wslot, xh, s_part, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns); break;
+                    default: ok = f16_m1_split_op<4, 8>(op, wslot, xh, s_part, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns); break;
+                }
+                ring_advance(slot, phase, (r1 - r0 + op.rows_per_chunk - 1) / op.rows_per_chunk, ns);
                 fast_done = true;
                 if (!ok) bad = true;
             }

@@ -263,22 +263,58 @@ __device__ __forceinline__ bool q8_m1_op(const StreamOp &op, const uint8_t *wslo
 
 
 
+// Eight fp16 weights (one 16-byte piece) against eight activations already
+// widened to fp32: the same products and fmaf order as dot8_f16 (an fp16 x
+// fp16 product is exact in fp32), with half the conversions.
+__device__ __forceinline__ float dot8_f16_f32(const int4 &a, const float *x, float acc) {
+    const __half2 *ha = reinterpret_cast<const __half2 *>(&a);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float2 fa = __half22float2(ha[i]);
+        acc = fmaf(fa.x, x[2 * i], acc);
+        acc = fmaf(fa.y, x[2 * i + 1], acc);
+    }
+    return acc;
+}
+
+// Widens the 16-byte fp16 activation piece p into x[0..8).
+__device__ __forceinline__ void widen8_f16(const uint16_t *xh, int p, float *x) {
+    const int4 v = *reinterpret_cast<const int4 *>(xh + p * 8);
+    const __half2 *h = reinterpret_cast<const __half2 *>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float2 f = __half22float2(h[i]);
+        x[2 * i] = f.x;
+        x[2 * i + 1] = f.y;
+    }
+}
+
+// Ring position after `chunks` more chunks from (slot, phase): the
+// out-of-line ops below take the position by value and the caller advances.
+__device__ __forceinline__ void ring_advance(int &slot, uint32_t &phase, int64_t chunks, int ns) {
+    const int64_t pos = slot + chunks;
+    slot = (int)(pos % ns);
+    if ((pos / ns) & 1) phase ^= 1u;
+}
+
 // F16 decode fast path (M = 1): as q8_m1_op, LPR lanes own one weight row and
 // lane s of a row takes the 16-byte (8-value) pieces s, s+LPR, ...; the
-// lane's fp16 activation pieces stay in registers for the whole op.  Each
-// piece contributes eight fp16 x fp16 products accumulated in fp32; a row is
-// reduced over its LPR lanes.  EPI_SWIGLU needs RPW even (LPR <= 16).
+// lane's activation pieces stay in registers, widened to fp32 once per op.
+// Each piece contributes eight fp16 x fp16 products accumulated in fp32; a
+// row is reduced over its LPR lanes.  EPI_SWIGLU needs RPW even (LPR <= 16).
+// Out of line (the 8*IT activation registers); the ring position comes by
+// value and the caller advances it by ceil((r1 - r0) / rows_per_chunk).
 template <int LPR, int IT>
-__device__ __forceinline__ bool f16_m1_op(const StreamOp &op, const uint8_t *wslot, const uint16_t *xh,
-                                          uint64_t *full, uint64_t *empty, int &slot, uint32_t &phase, int64_t r0,
-                                          int64_t r1, int cw, int lane, volatile int *abort_flag, int *err, int ns) {
+__device__ __noinline__ bool f16_m1_op(const StreamOp &op, const uint8_t *wslot, const uint16_t *xh,
+                                       uint64_t *full, uint64_t *empty, int slot, uint32_t phase, int64_t r0,
+                                       int64_t r1, int cw, int lane, volatile int *abort_flag, int *err, int ns) {
     constexpr int RPW = 32 / LPR;
     constexpr int RPP = RPW * ST_CONSUMER_WARPS;
     const int K = op.K;
     const int ls = lane % LPR, lr = lane / LPR;
-    int4 xr[IT];
+    float xf[8 * IT];
 #pragma unroll
-    for (int i = 0; i < IT; i++) xr[i] = *reinterpret_cast<const int4 *>(xh + (ls + LPR * i) * 8);
+    for (int i = 0; i < IT; i++) widen8_f16(xh, ls + LPR * i, xf + 8 * i);
     float *y = op.y;
     const float *bias = op.bias;
     const bool b16 = op.flags & VB_OUT_BF16;
@@ -300,7 +336,7 @@ __device__ __forceinline__ bool f16_m1_op(const StreamOp &op, const uint8_t *wsl
             float acc = 0.0f;
 #pragma unroll
             for (int i = 0; i < IT; i++)
-                acc = dot8_f16(*reinterpret_cast<const int4 *>(wr + (ls + LPR * i) * 16), xr[i], acc);
+                acc = dot8_f16_f32(*reinterpret_cast<const int4 *>(wr + (ls + LPR * i) * 16), xf + 8 * i, acc);
 #pragma unroll
             for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
             if (swz) {
@@ -320,6 +356,64 @@ __device__ __forceinline__ bool f16_m1_op(const StreamOp &op, const uint8_t *wsl
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
+        if (++slot == ns) { slot = 0; phase ^= 1u; }
+    }
+    return true;
+}
+
+// F16 decode path for long rows (M = 1, K = WPR * 256 * IT): a ring chunk
+// holds only R = ST_CONSUMER_WARPS / WPR rows (2 for K 6144/8192, 4 for
+// 4096), so WPR warps share a row: warp cw takes row cw / WPR and K segment
+// cw % WPR, lane l the 16-byte pieces seg*32*IT + l + 32 i, whose activation
+// stays in registers (widened to fp32 once per op).  The segment partials meet in `part` (two buffers of
+// ST_CONSUMER_WARPS floats, alternating per chunk) behind one consumer
+// barrier per chunk, which also makes a failed wait a uniform exit; the
+// segment-0 warp adds them in segment order and stores.  Not for
+// EPI_SWIGLU.  Out of line like f16_m1_op (ring position by value, the caller
+// advances it).  Returns false on a timeout or an abort.
+template <int WPR, int IT>
+__device__ __noinline__ bool f16_m1_split_op(const StreamOp &op, const uint8_t *wslot, const uint16_t *xh,
+                                             float *part, uint64_t *full, uint64_t *empty, int slot,
+                                             uint32_t phase, int64_t r0, int64_t r1, int cw, int lane,
+                                             volatile int *abort_flag, int *err, int ns) {
+    static_assert(ST_CONSUMER_WARPS % WPR == 0, "warps per row");
+    constexpr int R = ST_CONSUMER_WARPS / WPR;   // rows per chunk (checked by the caller)
+    constexpr int SEGP = 32 * IT;                 // 16-byte pieces per segment
+    const int K = op.K;
+    const int seg = cw % WPR, jrow = cw / WPR;
+    float xf[8 * IT];
+#pragma unroll
+    for (int i = 0; i < IT; i++) widen8_f16(xh, seg * SEGP + lane + 32 * i, xf + 8 * i);
+    int buf = 0;
+    for (int64_t r = r0; r < r1; r += R) {
+        const int nr = (int)((r1 - r) < R ? (r1 - r) : R);
+        const bool ok = wait_phase(&full[slot], phase, abort_flag);
+        if (!ok && !*abort_flag) { atomicCAS(err, 0, STREAM_TIMEOUT_FULL); *abort_flag = 1; }
+        if (__all_sync(0xffffffffu, ok)) {
+            float acc = 0.0f;
+            if (jrow < nr) {   // warp-uniform
+                const uint8_t *wr = wslot + (size_t)slot * ST_SLOT + (int64_t)jrow * K * 2;
+#pragma unroll
+                for (int i = 0; i < IT; i++)
+                    acc = dot8_f16_f32(*reinterpret_cast<const int4 *>(wr + (seg * SEGP + lane + 32 * i) * 16),
+                                       xf + 8 * i, acc);
+                acc = warp_sum(acc);
+            }
+            __syncwarp();
+            if (lane == 0) {
+                part[buf * ST_CONSUMER_WARPS + cw] = acc;
+                mbar_arrive(&empty[slot]);
+            }
+        }
+        if (consumer_sync_or(!ok, ST_CONSUMERS)) return false;
+        if (seg == 0 && jrow < nr && lane == 0) {
+            const float *p = part + buf * ST_CONSUMER_WARPS + cw;
+            float v = p[0];
+#pragma unroll
+            for (int s = 1; s < WPR; s++) v += p[s];
+            stream_store(op, 0, r + jrow, v);
+        }
+        buf ^= 1;
         if (++slot == ns) { slot = 0; phase ^= 1u; }
     }
     return true;
