@@ -502,15 +502,24 @@ def sweep_rows(ctx, q8_weights, args):
 def run_config1(args, local_rank):
     """Profiling case: BASELINE config 1 (Q8_0 W[2048 -> 6144], M=1) as a
     streaming program over `--copies` distinct weights (56 = 750 MB > L2),
-    run warmup + steps times.  Prints one JSON line with GB/s per GEMV."""
+    run warmup + steps times.  `--stream-type f16` and `--stream-kn K,N`
+    swap in another weight type or shape.  Prints one JSON line with GB/s
+    per GEMV (algorithmic bytes: weights + fp32 input + fp32 output)."""
     import torch
     import vcpm_b200 as vb
     torch.cuda.set_device(local_rank)
     ctx = vb.Context(local_rank)
     rng = np.random.default_rng(99)
-    ws = [ctx.weight(vb.TYPE_Q8_0, 2048, 6144, synth_q8_0(rng, 6144, 2048)) for _ in range(args.copies)]
-    x = torch.randn(2048, device="cuda")
-    y = torch.zeros(6144, device="cuda")
+    K, N = (int(v) for v in args.stream_kn.split(","))
+    if args.stream_type == "q8_0":
+        ws = [ctx.weight(vb.TYPE_Q8_0, K, N, synth_q8_0(rng, N, K)) for _ in range(args.copies)]
+        nbytes = alg_bytes(K, N)
+    else:
+        hw = (0.02 * rng.standard_normal((N, K))).astype(np.float16).view(np.uint16)
+        ws = [ctx.weight(vb.TYPE_F16, K, N, hw) for _ in range(args.copies)]
+        nbytes = 2 * N * K + 4 * K + 4 * N
+    x = torch.randn(K, device="cuda")
+    y = torch.zeros(N, device="cuda")
     torch.cuda.synchronize()
     prog = vb.Program(ctx, [dict(w=w, x=x, y=y, M=1, group=0) for w in ws])
     ev0, ev1 = ctx.event(), ctx.event()
@@ -523,8 +532,9 @@ def run_config1(args, local_rank):
     ms = ctx.elapsed_ms(ev0, ev1)
     rc, derr = prog.status()
     per = ms / (args.steps * len(ws))
-    print(json.dumps({"mode": "config1", "copies": len(ws), "us_per_gemv": per * 1e3,
-                      "gbs": alg_bytes(2048, 6144) / (per * 1e-3) / 1e9, "device_error": derr}), flush=True)
+    print(json.dumps({"mode": "config1", "wtype": args.stream_type, "K": K, "N": N, "copies": len(ws),
+                      "us_per_gemv": per * 1e3, "gbs": nbytes / (per * 1e-3) / 1e9, "device_error": derr}),
+          flush=True)
     prog.close()
     for w in ws:
         w.release()
@@ -924,6 +934,8 @@ def main():
     ap.add_argument("--gemm-shape", default="1408,1024,8192")
     ap.add_argument("--gemm-type", default="q8_0", choices=["q8_0", "f16"])
     ap.add_argument("--copies", type=int, default=56)
+    ap.add_argument("--stream-type", default="q8_0", choices=["q8_0", "f16"], help="config1 mode: weight type")
+    ap.add_argument("--stream-kn", default="2048,6144", help="config1 mode: weight shape K,N")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
