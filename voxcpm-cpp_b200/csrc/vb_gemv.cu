@@ -173,11 +173,15 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_fp_kernel(GemvArgs a) {
 #pragma unroll
                     for (int m = 0; m < MC; m++) {
                         if (m < mc) {
-                            const uint8_t *xp = smem + (m * K + c * EPC) * EB;
+                            // one 16-byte register copy of the activation piece, shared by the rows
+                            // (a reference into shared memory would be re-read as 4-byte loads)
+                            const int4 xv = *reinterpret_cast<const int4 *>(smem + (m * K + c * EPC) * EB);
 #pragma unroll
                             for (int r = 0; r < RPW; r++) {
-                                if (F16) acc[r][m] = dot8_f16(wv[u][r], *reinterpret_cast<const int4 *>(xp), acc[r][m]);
-                                else acc[r][m] = dot4_f32(wv[u][r], *reinterpret_cast<const float4 *>(xp), acc[r][m]);
+                                if (F16) acc[r][m] = dot8_f16(wv[u][r], xv, acc[r][m]);
+                                else acc[r][m] = dot4_f32(wv[u][r], make_float4(__int_as_float(xv.x), __int_as_float(xv.y),
+                                                                                 __int_as_float(xv.z), __int_as_float(xv.w)),
+                                                          acc[r][m]);
                             }
                         }
                     }

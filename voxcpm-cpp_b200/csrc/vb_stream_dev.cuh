@@ -265,7 +265,9 @@ __device__ __forceinline__ bool q8_m1_op(const StreamOp &op, const uint8_t *wslo
 
 // Eight fp16 weights (one 16-byte piece) against eight activations already
 // widened to fp32: the same products and fmaf order as dot8_f16 (an fp16 x
-// fp16 product is exact in fp32), with half the conversions.
+// fp16 product is exact in fp32), with half the conversions.  Callers pass a
+// register copy of the piece: a reference bound straight to shared memory
+// is read as four 4-byte loads at a 16-byte lane stride (4-way conflicts).
 __device__ __forceinline__ float dot8_f16_f32(const int4 &a, const float *x, float acc) {
     const __half2 *ha = reinterpret_cast<const __half2 *>(&a);
 #pragma unroll
@@ -335,8 +337,10 @@ __device__ __noinline__ bool f16_m1_op(const StreamOp &op, const uint8_t *wslot,
             const uint8_t *wr = wt + (int64_t)slot_row(jj, nr, swz) * K * 2;
             float acc = 0.0f;
 #pragma unroll
-            for (int i = 0; i < IT; i++)
-                acc = dot8_f16_f32(*reinterpret_cast<const int4 *>(wr + (ls + LPR * i) * 16), xf + 8 * i, acc);
+            for (int i = 0; i < IT; i++) {
+                const int4 wv = *reinterpret_cast<const int4 *>(wr + (ls + LPR * i) * 16);   // one 16-byte load
+                acc = dot8_f16_f32(wv, xf + 8 * i, acc);
+            }
 #pragma unroll
             for (int o = LPR / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
             if (swz) {
@@ -394,9 +398,10 @@ __device__ __noinline__ bool f16_m1_split_op(const StreamOp &op, const uint8_t *
             if (jrow < nr) {   // warp-uniform
                 const uint8_t *wr = wslot + (size_t)slot * ST_SLOT + (int64_t)jrow * K * 2;
 #pragma unroll
-                for (int i = 0; i < IT; i++)
-                    acc = dot8_f16_f32(*reinterpret_cast<const int4 *>(wr + (seg * SEGP + lane + 32 * i) * 16),
-                                       xf + 8 * i, acc);
+                for (int i = 0; i < IT; i++) {
+                    const int4 wv = *reinterpret_cast<const int4 *>(wr + (seg * SEGP + lane + 32 * i) * 16);
+                    acc = dot8_f16_f32(wv, xf + 8 * i, acc);
+                }
                 acc = warp_sum(acc);
             }
             __syncwarp();
