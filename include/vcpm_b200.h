@@ -367,7 +367,7 @@ int vb_cfm_solve(vb_ctx *ctx, vb_dit *dit, int n, const float *mu,
 /* ------------------------------------------------------------------ */
 /* Autoregressive generation on the device for a batch of utterances  */
 /* (src/gen_run.c:60-241, src/gen_prompt.c:186-272,                    */
-/*  src/gen_step.c:294-927, src/gen_stop.c:385-530)                     */
+/*  src/gen_step.c:294-927, src/gen_stop.c:85-230)                      */
 /* ------------------------------------------------------------------ */
 /* The parts are created beforehand and stay owned by the caller: TSLM and
  * RALM stacks with their final norms, the LocEnc blocks (no final norm;
@@ -376,7 +376,14 @@ int vb_cfm_solve(vb_ctx *ctx, vb_dit *dit, int n, const float *mu,
  *   enc_in      feat -> enc hidden        enc_to_lm   enc hidden -> hidden
  *   lm_to_dit   hidden -> dit hidden      res_to_dit  hidden -> dit hidden
  *   fsq_in      hidden -> fsq dim         fsq_out     fsq dim -> hidden
- *   fusion      2*hidden -> hidden        stop_proj / stop_head (optional)
+ *   fusion      2*hidden -> hidden
+ *   stop_proj / stop_head (optional, together): hidden*hidden and hidden*2
+ *               values in any registered type, read as the reference's stop
+ *               predictor reads them (src/gen_stop.c:126-135,180-195): flat
+ *               element j*hidden + i of stop_proj maps input j to output i,
+ *               element 2*j + o of stop_head maps input j to class o.  They
+ *               are re-laid out once, at vb_gen_create, as exact F32.
+ *               stop_head_bias is ignored, as the reference ignores it.
  * enc_special: device [enc hidden] CLS token; enc_norm: device [enc hidden]. */
 typedef struct {
     vb_lm *tslm, *ralm, *enc;
@@ -391,15 +398,48 @@ typedef struct {
 } vb_gen_parts;
 
 typedef struct vb_gen_s *vb_gen;
-/* `batch` utterances, each with its own KV slots of `max_len` positions. */
+/* `batch` utterances (indices 0..batch-1), each with its own KV slots of
+ * `max_len` positions; every utterance starts active. */
 int vb_gen_create(vb_ctx *ctx, const vb_gen_parts *parts, int batch, int max_len, vb_gen *out);
-/* Prompt of T positions per utterance; embeds: device [batch][T][hidden]. */
+/* Prompt of T positions per utterance; embeds: device [batch][T][hidden].
+ * Resets last_lm_hidden to zero (vcpm_gen_reset, src/gen_init.c:197-198).
+ * All utterances must be active.  Grows a prompt buffer owned by the
+ * generator when T exceeds every earlier prompt. */
 int vb_gen_prefill(vb_ctx *ctx, vb_gen g, int T, const float *embeds);
-/* One AR step for every utterance: mu -> CFM patch (noise stream seed + i,
- * this step) -> LocEnc -> TSLM -> FSQ -> RALM -> stop head.
- * patches: device [batch][patch][feat] or NULL; stop_logits: device
- * [batch][stop_head N] or NULL. */
+/* The min_len of vcpm_generation_params (default 2, src/gen_run.c:72): a
+ * stop class counts only once n_patches > min_len + 1 (:195-197). */
+int vb_gen_set_min_len(vb_gen g, int min_len);
+/* One AR step for every ACTIVE utterance (rows in vb_gen_active order):
+ * mu -> CFM patch (noise stream seed + utterance index, this step) ->
+ * LocEnc -> TSLM -> FSQ -> RALM, then the stop predictor on the hidden saved
+ * before the step (gen_predict_stop with the pre-update last_lm_hidden,
+ * src/gen_run.c:172-213; the updated hidden when hidden > 2048, as there).
+ * patches: device [n_active][patch][feat] or NULL; stop_logits: device
+ * [n_active][2] or NULL; stop: device int32 [n_active] or NULL, 1 where the
+ * stop class is 1 and the min-length gate is open (the utterance's last
+ * patch), else 0.  Stop outputs need stop_proj/stop_head. */
+int vb_gen_step_stop(vb_ctx *ctx, vb_gen g, uint64_t seed, float *patches, float *stop_logits, int32_t *stop);
+/* vb_gen_step_stop without the stop flags. */
 int vb_gen_step(vb_ctx *ctx, vb_gen g, uint64_t seed, float *patches, float *stop_logits);
+/* Number of active utterances; their indices in row order into
+ * `utterances` (host int32 [batch]) when not NULL.  -1 for a NULL g. */
+int vb_gen_active(const vb_gen g, int32_t *utterances);
+/* Ends the listed utterances (host int32 indices; retired or unknown-but-in-
+ * range indices are ignored): the per-utterance break of src/gen_run.c:208-213
+ * for a lockstep batch.  The remaining state rows are compacted so later
+ * steps run at the smaller batch; KV slots stay reserved.  Synchronises
+ * the context stream. */
+int vb_gen_retire(vb_ctx *ctx, vb_gen g, int n, const int32_t *utterances);
+/* Copies one state field of the active utterances (row order) into dst,
+ * device fp32 [n_active][width] (the fields of vcpm_generate_state,
+ * src/generate.h:155-212): */
+enum {
+    VB_GEN_LM_HIDDEN = 0,        /* lm_hidden_state [hidden]: prompt base[last], then the FSQ output */
+    VB_GEN_LAST_LM_HIDDEN = 1,   /* last_lm_hidden [hidden]: the stop predictor's input */
+    VB_GEN_RESIDUAL_HIDDEN = 2,  /* residual_hidden_state [hidden] */
+    VB_GEN_PREV_PATCH = 3        /* prev_patch [patch*feat] */
+};
+int vb_gen_state(vb_ctx *ctx, const vb_gen g, int which, float *dst);
 void vb_gen_destroy(vb_ctx *ctx, vb_gen g);
 
 /* ---- AudioVAE V2 decoder -------------------------------------------------

@@ -136,6 +136,7 @@ def _declare(L):
         "vo_cfm_noise": (None, [U64, I, P, I]),
         "vo_cfm_solve": (I, [P, P, P, P, P, I, F, P]),
         "vo_round_cache_capacity": (I, [I, I]),
+        "vo_stop_predict": (I, [I, P, P, I, P, P, I, P]),
         "vo_fill_normal": (None, [U64, F, F, P, I64]),
         "vo_vae_check_config": (I, [P]),
         "vo_vae_upsample": (I, [P]),
@@ -413,6 +414,20 @@ def fill_normal(seed, mean, std, n):
     x = np.zeros(n, np.float32)
     lib().vo_fill_normal(seed, mean, std, _p(x), n)
     return x
+
+
+def stop_predict(proj_type, proj_w, proj_bias, head_type, head_w, hidden):
+    """gen_predict_stop (src/gen_stop.c:85-230) on one hidden row: returns
+    (logits [2] float32, class).  proj_w / head_w are the flat tensors in
+    their storage type (stop_proj read as [in][out], stop_head as [in][2])."""
+    h = f32(hidden).ravel()
+    logits = np.zeros(2, np.float32)
+    pb = None if proj_bias is None else f32(proj_bias)
+    cls = lib().vo_stop_predict(proj_type, _p(np.ascontiguousarray(proj_w)), _p(pb), head_type,
+                                _p(np.ascontiguousarray(head_w)), _p(h), h.size, _p(logits))
+    if cls < 0:
+        raise ValueError("vo_stop_predict: bad argument")
+    return logits, cls
 
 
 def round_cache_capacity(required, model_max):

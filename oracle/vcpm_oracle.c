@@ -737,6 +737,76 @@ int vo_cfm_solve(const vo_dit_config *cfg, const vo_dit_weights *w,
     return 0;
 }
 
+/* ------------------------------------------------------------------------ */
+/* Stop predictor (src/gen_stop.c:28-230)                                    */
+/* ------------------------------------------------------------------------ */
+
+/* read_tensor_f32 (src/gen_stop.c:28-74): the flat tensor as F32 -- F16 the
+ * exact widening, Q8_0 (float)qs * fp16->fp32(d) per 34-byte block, F32 a
+ * copy.  Returns 0, or -1 for another type. */
+static int stop_read_f32(int type, const void *t, float *dst, size_t n) {
+    if (type == VO_TYPE_F32) {
+        memcpy(dst, t, n * 4u);
+        return 0;
+    }
+    if (type == VO_TYPE_F16) {
+        const uint16_t *h = (const uint16_t *)t;
+        for (size_t i = 0; i < n; i++) dst[i] = vo_fp16_to_fp32(h[i]);
+        return 0;
+    }
+    if (type == VO_TYPE_Q8_0) {
+        if (n % VO_QK8_0) return -1;
+        vo_dequantize_q8_0(t, dst, (int64_t)n);
+        return 0;
+    }
+    return -1;
+}
+
+/* gen_predict_stop (src/gen_stop.c:85-230) on one hidden row of hs values:
+ *   proj[i]  = bias[i] + sum_j W[j*hs + i] * hidden[j]   (stop_proj read in
+ *              its [in][out] storage order, :126-137, bias first)
+ *   proj[i]  = proj[i] / (1 + expf(-proj[i]))             (fp32 SiLU, :174-178)
+ *   logit[o] = sum_j H[2*j + o] * proj[j]                 (stop_head, no bias,
+ *              stride 2, :180-200)
+ * and the class with torch.argmax's tie rule (class 0 wins ties,
+ * gen_stop_class_from_logits :76-81).  The reference accumulates in fp32
+ * sequentially; VO_ACC is that order's accumulator (float in the
+ * fp32-accumulation build, which is then the reference's exact op order).
+ * Returns the class, or -1 on a bad argument. */
+int vo_stop_predict(int proj_type, const void *proj_w, const float *proj_bias, int head_type, const void *head_w,
+                    const float *hidden, int hs, float *logits) {
+    if (!proj_w || !head_w || !hidden || !logits || hs <= 0) return -1;
+    float *W = (float *)malloc((size_t)hs * hs * 4u);
+    float *Hh = (float *)malloc((size_t)hs * 2u * 4u);
+    float *proj = (float *)malloc((size_t)hs * 4u);
+    int rc = (W && Hh && proj) ? 0 : -1;
+    if (!rc) rc = stop_read_f32(proj_type, proj_w, W, (size_t)hs * hs);
+    if (!rc) rc = stop_read_f32(head_type, head_w, Hh, (size_t)hs * 2u);
+    if (!rc) {
+        for (int i = 0; i < hs; i++) {
+            VO_ACC sum = proj_bias ? proj_bias[i] : 0.0f;
+            for (int j = 0; j < hs; j++) sum += W[(size_t)j * hs + i] * hidden[j];
+            proj[i] = (float)sum;
+        }
+        for (int i = 0; i < hs; i++) {
+            const float x = proj[i];
+            proj[i] = x / (1.0f + expf(-x));
+        }
+        VO_ACC s0 = 0.0f, s1 = 0.0f;
+        for (int j = 0; j < hs; j++) {
+            s0 += Hh[2 * j + 0] * proj[j];
+            s1 += Hh[2 * j + 1] * proj[j];
+        }
+        logits[0] = (float)s0;
+        logits[1] = (float)s1;
+        rc = logits[1] > logits[0] ? 1 : 0;
+    }
+    free(W);
+    free(Hh);
+    free(proj);
+    return rc;
+}
+
 /* vcpm_gen_round_cache_capacity (src/gen_init.c:115-127). */
 int vo_round_cache_capacity(int required, int model_max) {
     if (required <= 0 || model_max <= 0 || required > model_max) return 0;

@@ -15,8 +15,9 @@
  *     its behaviour is restated from its documented algorithms.
  *   - the graph builders of the reference: src/minicpm4.c (norm, rope,
  *     attention, mlp, block, forward), src/locdit.c (LocDiT estimator),
- *     src/locenc.c (feature encoder), src/fsq.c, src/cfm_solver.c and the
- *     CFM/LM-update loop of src/gen_step.c.
+ *     src/locenc.c (feature encoder), src/fsq.c, src/cfm_solver.c, the
+ *     CFM/LM-update loop of src/gen_step.c and the stop predictor of
+ *     src/gen_stop.c.
  *
  * Parity status: the CFM schedule/CFG-Zero* goldens, the op fixtures and
  * the small known-answer tests of the reference pin the non-quantized ops.
@@ -176,6 +177,15 @@ void vo_cfm_noise(uint64_t seed, int ar_step, float *x, int n);
 int vo_cfm_solve(const vo_dit_config *cfg, const vo_dit_weights *w,
                  const float *mu, const float *cond, float *x, int n_steps,
                  float cfg_value, const vo_opts *o);
+
+/* ---- stop predictor (src/gen_stop.c:85-230) ---- */
+/* stop_proj: hs*hs values read as W[j*hs + i] (input j, output i), any of
+ * F32/F16/Q8_0 storage; proj_bias: F32 [hs] or NULL; stop_head: hs*2 values
+ * read as H[2*j + o].  Writes the two logits; returns the argmax class
+ * (class 0 wins ties) or -1. */
+int vo_stop_predict(int proj_type, const void *proj_w, const float *proj_bias,
+                    int head_type, const void *head_w, const float *hidden,
+                    int hs, float *logits);
 
 /* ---- misc host helpers (src/gen_init.c) ---- */
 int vo_round_cache_capacity(int required, int model_max);

@@ -1,11 +1,18 @@
 """GPU generation loop (vb_gen: prompt, then per-patch mu -> CFM -> LocEnc ->
-TSLM -> FSQ -> RALM -> stop head for a batch of utterances) against a replay
-of the same call order on the CPU oracle, one utterance at a time.
+TSLM -> FSQ -> RALM, and the stop predictor) against a replay of the same
+call order on the CPU oracle, one utterance at a time.
 
 Reduced widths keep the oracle fast.  Stacked, autoregressive outputs use
 the envelope gate of the other stack tests (synth.assert_envelope): the
 device must stay within a small multiple of the distance between the
-oracle's double- and fp32-accumulation builds."""
+oracle's double- and fp32-accumulation builds.
+
+The stop predictor is checked teacher-forced, at the 1e-3 mat-mul gate:
+the oracle's restatement of gen_predict_stop (src/gen_stop.c:85-230) runs on
+the device's own last_lm_hidden as it was BEFORE each step (the copy
+src/gen_run.c:172-183 saves), and the host loop replays src/gen_run.c:166-215
+(stop class counted once n_patches > min_len + 1, the utterance ends there)
+through vb_gen_retire."""
 import contextlib
 
 import numpy as np
@@ -22,6 +29,7 @@ import vcpm_b200 as vb  # noqa: E402
 H, NH, NKV, HD, FFN = 512, 4, 2, 128, 1024
 FEAT, PATCH, FSQ_D, STEPS, CFG = 64, 4, 64, 10, 2.0
 EPS, SCALE = 1e-5, 9.0
+STOP_STD = 0.2    # stop weights: logits of order one, so classes are well separated
 
 
 @pytest.fixture(scope="module")
@@ -58,7 +66,8 @@ class Model:
         shapes = {"enc_in": (FEAT, H), "enc_to_lm": (H, H), "lm_to_dit": (H, H), "res_to_dit": (H, H),
                   "fsq_in": (H, FSQ_D), "fsq_out": (FSQ_D, H), "fusion": (2 * H, H), "stop_proj": (H, H),
                   "stop_head": (H, 2)}
-        self.w = {k: (K, N, S.weight(wtype, N, K)) for k, (K, N) in shapes.items()}
+        self.w = {k: (K, N, S.weight(wtype, N, K, STOP_STD if k.startswith("stop") else 0.02))
+                  for k, (K, N) in shapes.items()}
         self.b = {k: S.normal(N, 0.02) for k, (K, N) in shapes.items()}
         self.special = S.normal(H, 0.5)
         self.enorm = S.normal(H, 0.02, 1.0)
@@ -94,8 +103,15 @@ class Model:
         K, N, W = self.w[k]
         return O.matmul(self.wtype, W, K, N, np.atleast_2d(x)) + self.b[k]
 
+    def stop(self, hidden):
+        """gen_predict_stop on one hidden row (the reference reads the stored
+        tensors as they are: bias of stop_proj only)."""
+        return O.stop_predict(self.wtype, self.w["stop_proj"][2], self.b["stop_proj"], self.wtype,
+                              self.w["stop_head"][2], hidden)
+
     def oracle_run(self, embeds, n_steps, seed, f32):
-        """Replays prompt + n_steps for each utterance; returns (patches, stops)."""
+        """Replays prompt + n_steps for each utterance; returns (patches,
+        stop logits of the pre-update hidden)."""
         B, T = embeds.shape[:2]
         tcfg, rcfg = self.lm_cfg(0, True), self.lm_cfg(1, True)
         tlay = [S.oracle_layer(self.wtype, L) for L in self.tl]
@@ -118,7 +134,9 @@ class Model:
                 fin = np.concatenate([base, np.zeros_like(base)], axis=1)
                 ral = O.lm_forward(rcfg, rlay, self.rnorm, rc, self.lin("fusion", fin), T, 0)
                 lm_h, res_h, prev, pos = base[-1], ral[-1], np.zeros((PATCH, FEAT), np.float32), T
+                last_lm = np.zeros(H, np.float32)       # src/gen_init.c:197-198
                 for s in range(n_steps):
+                    pre = last_lm.copy()                # src/gen_run.c:178-183
                     mu = np.concatenate([self.lin("lm_to_dit", lm_h)[0], self.lin("res_to_dit", res_h)[0]])
                     x0 = O.cfm_noise(seed + i, s, PATCH * FEAT).reshape(PATCH, FEAT)
                     patch = dit.cfm_solve(mu, prev, x0, STEPS, CFG)
@@ -128,11 +146,10 @@ class Model:
                     base = O.lm_forward(tcfg, tlay, self.tnorm, tc, audio[None], 1, pos)[0]
                     f = O.fsq_quantize(self.lin("fsq_in", base)[0], SCALE)
                     lm_h = self.lin("fsq_out", f)[0]
+                    last_lm = lm_h                      # src/gen_step.c:846-848
                     rin = self.lin("fusion", np.concatenate([lm_h, audio]))
                     res_h = O.lm_forward(rcfg, rlay, self.rnorm, rc, rin, 1, pos)[0]
-                    hs = self.lin("stop_proj", lm_h)[0]
-                    hs = O.bf16_round(hs / (1.0 + np.exp(-hs.astype(np.float64))).astype(np.float32))
-                    stops[s, i] = self.lin("stop_head", hs)[0]
+                    stops[s, i] = self.stop(pre)[0]
                     pos += 1
         return patches, stops
 
@@ -160,9 +177,96 @@ def test_generation_loop_matches_oracle(ctx, B):
     rp32, rs32 = m.oracle_run(embeds, n_steps, seed, True)
     for s in range(n_steps):
         S.assert_envelope(got_p[s], rp[s], rp32[s])
-        # stop logits: two values per utterance from a random 512 -> 2 head,
-        # near zero, so the oracle's own two builds differ by several percent;
-        # gate on relative L2 against that spread only
+        # stop logits of the end-to-end replay: the pre-update hidden of step
+        # 0 is zero (exact), later ones inherit the stack's drift
         spread = S.rel_l2(rs32[s], rs[s])
         assert S.rel_l2(got_s[s], rs[s]) <= max(0.05, 3.0 * spread)
+    S.assert_matmul_close(got_s[0], rs[0])
+    m.close()
+
+
+@pytest.mark.parametrize("B", [3, 2])
+def test_stop_predictor_and_termination(ctx, B):
+    """The gen_run loop on the device: every step the stop logits, class and
+    flag are those of the oracle's gen_predict_stop on the device's own
+    pre-update last_lm_hidden (1e-3), flagged utterances are retired, and at
+    least one step has a different class on the updated hidden (so the test
+    tells the two hiddens apart)."""
+    m = Model(ctx, O.TYPE_Q8_0)
+    parts = m.device_parts()
+    T, n_steps, seed, min_len = 5, 7, 77, 1
+    embeds = O.bf16_round(S.normal((B, T, H), 0.5))
+    g = vb.Gen(ctx, parts, B, 32)
+    g.set_min_len(min_len)
+    g.prefill(T, dev(embeds))
+    n_patches = {u: 0 for u in range(B)}
+    differs = 0
+    for s in range(n_steps):
+        act = g.active()
+        if not act:
+            break
+        n = len(act)
+        pre = torch.zeros((n, H), dtype=torch.float32, device="cuda")
+        post = torch.zeros((n, H), dtype=torch.float32, device="cuda")
+        g.state(vb.GEN_LAST_LM_HIDDEN, pre)
+        st = torch.zeros((n, 2), dtype=torch.float32, device="cuda")
+        flag = torch.full((n,), -1, dtype=torch.int32, device="cuda")
+        g.step(seed, None, st, flag)
+        g.state(vb.GEN_LAST_LM_HIDDEN, post)
+        ctx.sync()
+        pre, post, st, flag = pre.cpu().numpy(), post.cpu().numpy(), st.cpu().numpy(), flag.cpu().numpy()
+        if s == 0:
+            assert not pre.any(), "last_lm_hidden must start at zero after the prompt"
+        gate_open = (s + 1) > min_len + 1
+        done = []
+        for r, u in enumerate(act):
+            n_patches[u] += 1
+            ref, cls = m.stop(pre[r])
+            S.assert_matmul_close(st[r], ref)
+            margin = abs(float(ref[1] - ref[0]))
+            if margin > 1e-3 * max(float(np.abs(ref).max()), 1e-30):
+                assert int(st[r, 1] > st[r, 0]) == cls
+                assert flag[r] == (1 if (gate_open and cls == 1) else 0)
+            if m.stop(post[r])[1] != cls:
+                differs += 1
+            if flag[r] == 1:
+                done.append(u)
+        g.retire(done)
+        assert g.active() == [u for u in act if u not in done]
+    assert differs > 0, "pre- and post-update hiddens gave the same class everywhere"
+    assert all(v >= min(min_len + 2, n_steps) for v in n_patches.values())
+    g.close()
+    m.close()
+
+
+def test_retired_rows_compact(ctx):
+    """Retiring utterance 1 of 3 after two steps: the remaining two continue
+    on the single-launch decoder path from compacted rows, and their patches
+    still follow the oracle replay of each utterance."""
+    m = Model(ctx, O.TYPE_Q8_0)
+    parts = m.device_parts()
+    B, T, n_steps, seed = 3, 6, 4, 4321
+    embeds = O.bf16_round(S.normal((B, T, H), 0.5))
+    g = vb.Gen(ctx, parts, B, 32)
+    g.prefill(T, dev(embeds))
+    got = {}
+    for s in range(n_steps):
+        if s == 2:
+            g.retire([1])
+            assert g.active() == [0, 2]
+        act = g.active()
+        pt = torch.zeros((len(act), PATCH, FEAT), dtype=torch.float32, device="cuda")
+        g.step(seed, pt)
+        prev = torch.zeros((len(act), PATCH * FEAT), dtype=torch.float32, device="cuda")
+        g.state(vb.GEN_PREV_PATCH, prev)
+        ctx.sync()
+        assert np.array_equal(prev.cpu().numpy(), pt.cpu().numpy().reshape(len(act), -1))
+        for r, u in enumerate(act):
+            got[(s, u)] = pt[r].cpu().numpy()
+    g.close()
+    rp, _ = m.oracle_run(embeds, n_steps, seed, False)
+    rp32, _ = m.oracle_run(embeds, n_steps, seed, True)
+    for (s, u), p in got.items():
+        S.assert_envelope(p, rp[s, u], rp32[s, u])
+    assert (3, 1) not in got and (3, 0) in got and (3, 2) in got
     m.close()

@@ -10,6 +10,9 @@ int init_kernels(vb_ctx *ctx);
 // weights (vb_quant.cu)
 int weight_upload(vb_ctx *ctx, int type, int64_t K, int64_t N, const void *host, size_t nbytes, vb_weight *out);
 void weight_free(vb_ctx *ctx, vb_weight w);
+// A new F32 weight [out_dim][in_dim] holding element j*out_dim + o of the
+// flat storage of src at row o, column j (src keeps its own storage).
+int weight_transpose_f32(vb_ctx *ctx, vb_weight src, int64_t in_dim, int64_t out_dim, vb_weight *out);
 
 // Output mapping of a mat-mul: logical row m of the [M][N] result lands in
 // row  (m / seg) * seg_stride + seg_off + (m % seg)  of y (leading dim ldy).

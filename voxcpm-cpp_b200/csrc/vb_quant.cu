@@ -103,6 +103,54 @@ void weight_free(vb_ctx *ctx, vb_weight w) {
     delete w;
 }
 
+// dst[o][j] = value of flat element j*out_dim + o of a registered weight, as
+// exact F32: the stop predictor reads its two weights in [in][out] storage
+// order (W_buf[j*hs + i], H_buf[2*j + o], src/gen_stop.c:126-135,180-195)
+// after dequantizing them with read_tensor_f32 (:28-74).  Flat element f of
+// a registered [N][K] weight is row f / K, column f % K.
+__global__ void transpose_f32_kernel(const void *__restrict__ data, const uint16_t *__restrict__ sc, int type,
+                                     int64_t K, int64_t in_dim, int64_t out_dim, float *__restrict__ dst) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= in_dim * out_dim) return;
+    const int64_t o = i / in_dim, j = i % in_dim;
+    const int64_t f = j * out_dim + o, n = f / K, k = f % K;
+    float v;
+    if (type == VB_TYPE_Q8_0)
+        v = __fmul_rn((float)static_cast<const int8_t *>(data)[n * K + k], h2f(sc[n * (K / QK) + k / QK]));
+    else if (type == VB_TYPE_F16)
+        v = h2f(static_cast<const uint16_t *>(data)[n * K + k]);
+    else
+        v = static_cast<const float *>(data)[n * K + k];
+    dst[i] = v;
+}
+
+int weight_transpose_f32(vb_ctx *ctx, vb_weight src, int64_t in_dim, int64_t out_dim, vb_weight *out) {
+    *out = nullptr;
+    if (!src || in_dim <= 0 || out_dim <= 0 || src->K * src->N != in_dim * out_dim)
+        return set_error(ctx, VB_ERR_INVALID_ARG, "weight re-layout: %lld x %lld values expected", (long long)in_dim,
+                         (long long)out_dim);
+    if (fault_injected("alloc")) return set_error(ctx, VB_ERR_OOM, "weight: injected allocation fault");
+    vb_weight w = new vb_weight_s();
+    w->type = VB_TYPE_F32;
+    w->K = in_dim;
+    w->N = out_dim;
+    w->device_bytes = (size_t)(in_dim * out_dim) * 4u;
+    if (cudaMalloc(&w->data, w->device_bytes) != cudaSuccess) {
+        delete w;
+        return set_error(ctx, VB_ERR_OOM, "weight re-layout: allocation of %zu bytes failed", (size_t)(in_dim * out_dim) * 4u);
+    }
+    const int64_t n = in_dim * out_dim;
+    transpose_f32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(src->data, src->scales, src->type, src->K,
+                                                                             in_dim, out_dim, (float *)w->data);
+    const int rc = check_launch(ctx, "transpose_f32");
+    if (rc) {
+        weight_free(ctx, w);
+        return rc;
+    }
+    *out = w;
+    return VB_OK;
+}
+
 // One warp per 32-value block; output in the GGUF 34-byte layout.
 __global__ void quantize_q8_0_kernel(const float *__restrict__ x, int64_t nblocks, uint8_t *__restrict__ out,
                                      int rule) {

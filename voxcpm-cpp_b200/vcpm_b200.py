@@ -22,6 +22,7 @@ VB_OK, VB_ERR_INVALID_ARG, VB_ERR_BACKEND, VB_ERR_OOM, VB_ERR_NOT_IMPLEMENTED = 
 TYPE_F32, TYPE_F16, TYPE_Q8_0 = 0, 1, 8
 QRULE_X86, QRULE_REF = 0, 1
 OUT_BF16 = 1
+GEN_LM_HIDDEN, GEN_LAST_LM_HIDDEN, GEN_RESIDUAL_HIDDEN, GEN_PREV_PATCH = 0, 1, 2, 3
 
 _lib = None
 
@@ -139,6 +140,11 @@ SIGNATURES = {
     "vb_gen_create": (_I, [_P, _P, _I, _I, C.POINTER(_P)]),
     "vb_gen_prefill": (_I, [_P, _P, _I, _P]),
     "vb_gen_step": (_I, [_P, _P, C.c_uint64, _P, _P]),
+    "vb_gen_step_stop": (_I, [_P, _P, C.c_uint64, _P, _P, _P]),
+    "vb_gen_set_min_len": (_I, [_P, _I]),
+    "vb_gen_active": (_I, [_P, _P]),
+    "vb_gen_retire": (_I, [_P, _P, _I, _P]),
+    "vb_gen_state": (_I, [_P, _P, _I, _P]),
     "vb_gen_destroy": (None, [_P, _P]),
     "vb_vae_create": (_I, [_P, _P, _P, C.POINTER(_P)]),
     "vb_vae_destroy": (None, [_P, _P]),
@@ -474,8 +480,31 @@ class Gen:
     def prefill(self, T, embeds):
         self.ctx.check(self.ctx.L.vb_gen_prefill(self.ctx.h, self.h, T, _addr(embeds)))
 
-    def step(self, seed, patches=None, stop_logits=None):
-        self.ctx.check(self.ctx.L.vb_gen_step(self.ctx.h, self.h, seed, _addr(patches), _addr(stop_logits)))
+    def step(self, seed, patches=None, stop_logits=None, stop=None):
+        """One step of every active utterance; stop: device int32 [n_active]
+        (1 = the utterance's stop check fired)."""
+        self.ctx.check(self.ctx.L.vb_gen_step_stop(self.ctx.h, self.h, seed, _addr(patches), _addr(stop_logits),
+                                                   _addr(stop)))
+
+    def set_min_len(self, min_len):
+        self.ctx.check(self.ctx.L.vb_gen_set_min_len(self.h, min_len))
+
+    def active(self):
+        """Indices of the active utterances, in row order."""
+        n = self.ctx.L.vb_gen_active(self.h, None)
+        buf = (C.c_int32 * max(n, 1))()
+        self.ctx.L.vb_gen_active(self.h, buf)
+        return [buf[i] for i in range(n)]
+
+    def retire(self, utterances):
+        u = list(utterances)
+        arr = (C.c_int32 * max(len(u), 1))(*u)
+        self.ctx.check(self.ctx.L.vb_gen_retire(self.ctx.h, self.h, len(u), arr))
+
+    def state(self, which, dst):
+        """Copies a state field (GEN_LM_HIDDEN, GEN_LAST_LM_HIDDEN,
+        GEN_RESIDUAL_HIDDEN, GEN_PREV_PATCH) of the active rows into dst."""
+        self.ctx.check(self.ctx.L.vb_gen_state(self.ctx.h, self.h, which, _addr(dst)))
 
     def close(self):
         if self.h:
