@@ -13,6 +13,12 @@ import oracle as O
 _seed = [1000]
 
 
+def reseed(seed):
+    """Restart the seed sequence, so a test's draws do not depend on which
+    tests ran before it."""
+    _seed[0] = seed
+
+
 def next_seed():
     _seed[0] += 1
     return _seed[0]
@@ -25,6 +31,34 @@ def normal(n, std=1.0, mean=0.0, seed=None):
 def weight(wtype, N, K, std=0.02):
     """GGUF storage of a random [N, K] weight."""
     return O.make_weight(wtype, normal((N, K), std), O.QRULE_REF)
+
+
+def fast_weight(wtype, N, K, rng, std=0.02):
+    """GGUF storage of a random [N, K] weight for the full-size configs,
+    drawn with numpy (seconds for a 28-layer stack): Q8_0 blocks of uniform
+    int8 quants in [-127, 127] with fp16 scales near std * 2.2 / 127 (the
+    block maximum of N(0, std) draws), or F16 rows of N(0, std)."""
+    if wtype == O.TYPE_Q8_0:
+        nb = K // 32
+        blk = np.empty((N, nb, 34), np.uint8)
+        d = np.abs(std * 2.2 / 127.0 * (1.0 + 0.1 * rng.standard_normal((N, nb), np.float32))).astype(np.float16)
+        blk[..., :2] = d.view(np.uint8).reshape(N, nb, 2)
+        blk[..., 2:] = rng.integers(-127, 128, size=(N, nb, 32), dtype=np.int8).view(np.uint8)
+        return blk.reshape(-1)
+    if wtype == O.TYPE_F16:
+        return (rng.standard_normal((N, K), np.float32) * np.float32(std)).astype(np.float16).view(np.uint16).reshape(-1)
+    return (rng.standard_normal((N, K), np.float32) * np.float32(std)).reshape(-1)
+
+
+def fast_layer(wtype, hidden, n_heads, n_kv, head_dim, ffn, rng):
+    qd, kd = n_heads * head_dim, n_kv * head_dim
+    w = lambda n, k: fast_weight(wtype, n, k, rng)  # noqa: E731
+    return {
+        "q": w(qd, hidden), "k": w(kd, hidden), "v": w(kd, hidden), "o": w(hidden, qd),
+        "gate": w(ffn, hidden), "up": w(ffn, hidden), "down": w(hidden, ffn),
+        "attn_norm": (1.0 + 0.02 * rng.standard_normal(hidden, np.float32)).astype(np.float32),
+        "ffn_norm": (1.0 + 0.02 * rng.standard_normal(hidden, np.float32)).astype(np.float32),
+    }
 
 
 def layer(wtype, hidden, n_heads, n_kv, head_dim, ffn):
@@ -91,11 +125,15 @@ def assert_envelope(y, r, r_f32, floor=1.5e-2, factor=3.0):
     comes from the oracle itself: its two builds differ by up to 9.0e-3 on a
     2-layer Q8_0 LocDiT output when one flip cascades, and by exactly 0 when
     none does, so one sample of their distance can understate the spread.
-    Stage-by-stage exactness is checked separately (test_stages_gpu.py)."""
+    Stage-by-stage exactness is checked separately (test_stages_gpu.py).
+    On deep stacks (28 random-init layers) the two builds themselves drift
+    below cos 0.9999; the cosine gate then widens the same way, to factor
+    times their own cosine distance."""
     s = rel_l2(r_f32, r)
     e = rel_l2(y, r)
     c = cos_sim(y, r)
-    assert c >= 0.9999, f"cos {c:.6f} < 0.9999"
+    c_min = min(0.9999, 1.0 - factor * (1.0 - cos_sim(r_f32, r)))
+    assert c >= c_min, f"cos {c:.6f} < {c_min:.6f}"
     assert e <= max(floor, factor * s), f"relative L2 {e:.3e} > max({floor}, {factor} x {s:.3e})"
 
 

@@ -29,7 +29,9 @@ import vcpm_b200 as vb  # noqa: E402
 H, NH, NKV, HD, FFN = 512, 4, 2, 128, 1024
 FEAT, PATCH, FSQ_D, STEPS, CFG = 64, 4, 64, 10, 2.0
 EPS, SCALE = 1e-5, 9.0
-STOP_STD = 0.2    # stop weights: logits of order one, so classes are well separated
+STOP_STD = 0.2    # stop weights: logits of order one
+STOP_EPS = 0.005  # stop_head column 1 = column 0 + N(0, STOP_EPS): the class then turns on
+                  # the particular hidden, not on a component every hidden shares
 
 
 @pytest.fixture(scope="module")
@@ -42,7 +44,24 @@ def ctx():
 
 
 def dev(a):
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    """Device copy of a host array, complete before the library (whose
+    stream is not ordered after torch's) reads it."""
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    torch.cuda.synchronize()
+    return t
+
+
+def zeros(shape, dtype=None):
+    """Zeroed device buffer, cleared before the library writes into it."""
+    t = torch.zeros(shape, dtype=dtype or torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    return t
+
+
+def full(shape, value, dtype):
+    t = torch.full(shape, value, dtype=dtype, device="cuda")
+    torch.cuda.synchronize()
+    return t
 
 
 def variant(f32):
@@ -52,9 +71,10 @@ def variant(f32):
 class Model:
     """Random weights of every part, on the device and for the oracle."""
 
-    def __init__(self, ctx, wtype):
+    def __init__(self, ctx, wtype, seed=5100):
         self.wtype = wtype
         self.ctx = ctx
+        S.reseed(seed)
         L = lambda: S.layer(wtype, H, NH, NKV, HD, FFN)  # noqa: E731
         self.tl = [L() for _ in range(2)]
         self.rl = [L() for _ in range(2)]
@@ -69,6 +89,9 @@ class Model:
         self.w = {k: (K, N, S.weight(wtype, N, K, STOP_STD if k.startswith("stop") else 0.02))
                   for k, (K, N) in shapes.items()}
         self.b = {k: S.normal(N, 0.02) for k, (K, N) in shapes.items()}
+        a = S.normal(H, STOP_STD)
+        head = np.stack([a, a + S.normal(H, STOP_EPS)], 1)    # [in][class], the reference's read order
+        self.w["stop_head"] = (H, 2, O.make_weight(wtype, head.reshape(1, 2 * H), O.QRULE_REF).ravel())
         self.special = S.normal(H, 0.5)
         self.enorm = S.normal(H, 0.02, 1.0)
 
@@ -166,8 +189,8 @@ def test_generation_loop_matches_oracle(ctx, B):
     g.prefill(T, dev(embeds))
     got_p, got_s = [], []
     for s in range(n_steps):
-        pt = torch.zeros((B, PATCH, FEAT), dtype=torch.float32, device="cuda")
-        st = torch.zeros((B, 2), dtype=torch.float32, device="cuda")
+        pt = zeros((B, PATCH, FEAT))
+        st = zeros((B, 2))
         g.step(seed, pt, st)
         ctx.sync()
         got_p.append(pt.cpu().numpy())
@@ -206,11 +229,11 @@ def test_stop_predictor_and_termination(ctx, B):
         if not act:
             break
         n = len(act)
-        pre = torch.zeros((n, H), dtype=torch.float32, device="cuda")
-        post = torch.zeros((n, H), dtype=torch.float32, device="cuda")
+        pre = zeros((n, H))
+        post = zeros((n, H))
         g.state(vb.GEN_LAST_LM_HIDDEN, pre)
-        st = torch.zeros((n, 2), dtype=torch.float32, device="cuda")
-        flag = torch.full((n,), -1, dtype=torch.int32, device="cuda")
+        st = zeros((n, 2))
+        flag = full((n,), -1, torch.int32)
         g.step(seed, None, st, flag)
         g.state(vb.GEN_LAST_LM_HIDDEN, post)
         ctx.sync()
@@ -255,9 +278,9 @@ def test_retired_rows_compact(ctx):
             g.retire([1])
             assert g.active() == [0, 2]
         act = g.active()
-        pt = torch.zeros((len(act), PATCH, FEAT), dtype=torch.float32, device="cuda")
+        pt = zeros((len(act), PATCH, FEAT))
         g.step(seed, pt)
-        prev = torch.zeros((len(act), PATCH * FEAT), dtype=torch.float32, device="cuda")
+        prev = zeros((len(act), PATCH * FEAT))
         g.state(vb.GEN_PREV_PATCH, prev)
         ctx.sync()
         assert np.array_equal(prev.cpu().numpy(), pt.cpu().numpy().reshape(len(act), -1))

@@ -63,6 +63,24 @@ def test_quantize_q8_0_bit_exact(ctx, rule):
     assert np.array_equal(host(out), ref)
 
 
+def test_quantize_q8_0_ref_rule_matches_gguf_py(ctx):
+    """VB_QRULE_REF on the device against gguf-py's Q8_0 quantizer (the
+    third-party restatement of ggml's reference rule from the same upstream
+    project), byte for byte, with no oracle in between."""
+    gq = pytest.importorskip("gguf.quants")
+    import gguf
+    K, M = 4096, 16
+    x = S.normal((M, K), 0.02)
+    x[0, :32] = 0.0
+    x[1, :32] = np.linspace(-1, 1, 32)
+    x[2, 64:96] = S.normal(32, 300.0)
+    xd = dev(x)
+    out = torch.zeros(M * K // 32 * 34, dtype=torch.uint8, device="cuda")
+    run(ctx, lambda: ctx.quantize_q8_0(xd, K, M, out, vb.QRULE_REF))
+    want = gq.quantize(x, gguf.GGMLQuantizationType.Q8_0).ravel()
+    assert np.array_equal(host(out), want)
+
+
 def test_dequantize_q8_0_bit_exact(ctx):
     w = S.weight(O.TYPE_Q8_0, 64, 2048)
     wd = dev(w.ravel())
