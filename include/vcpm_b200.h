@@ -231,9 +231,9 @@ int vb_attention(vb_ctx *ctx, const float *q, const uint16_t *k,
  * every input and output buffer.  Limit: T * n_heads * ceil(n_rows / 64) *
  * (head_dim + 2) * 4 bytes must not exceed the array size (for example one
  * decode token with 16 heads of 128 over up to 8192 rows fits); larger calls
- * return VB_ERR_INVALID_ARG with the sizes in vb_last_error().  The first
- * call on each device looks up the array's device address, so make that
- * first call before any stream capture.  All calls on a device share the
+ * return VB_ERR_INVALID_ARG with the sizes in vb_last_error().  vb_create
+ * looks up the array's device address for its context, so a call itself
+ * does no set-up.  All calls on a device share the
  * one array: calls that overlap on the GPU (two streams, two contexts of
  * the same device) race and corrupt each other's results.  Nothing in the
  * array needs to start at zero; each call writes every entry it reads. */

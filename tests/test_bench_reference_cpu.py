@@ -30,6 +30,7 @@ def test_reference_arm_prints_the_contract_line():
     base = d["cpu_baseline"]
     assert base["kind"] == "port" and base["cores"] >= 1 and base["unit"] == "GB/s" and base["sample"]
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+    assert d["arm"].startswith("oracle port")
     assert d["config"]["M"] == 1 and d["config"]["layers"] == 28 and len(d["config"]["shapes"]) == 7
 
 

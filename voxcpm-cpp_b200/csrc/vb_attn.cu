@@ -18,7 +18,6 @@
 #include "vb_common.cuh"
 #include "vb_kernels.cuh"
 
-#include <mutex>
 
 namespace vb {
 
@@ -241,7 +240,10 @@ static size_t attn_smem(int n_heads, int n_kv, int head_dim) {
     return (size_t)2 * ATT_CH * rw * 4 + (size_t)qpk * head_dim * 4 + (size_t)ATT_WARPS * ATT_CH * 4;
 }
 
+int init_noalloc_scratch(vb_ctx *ctx);
+
 int init_attention(vb_ctx *ctx) {
+    if (init_noalloc_scratch(ctx)) return VB_ERR_BACKEND;
     VB_CHECK(ctx, cudaFuncSetAttribute(attn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
     VB_CHECK(ctx, cudaFuncSetAttribute(attn_segment_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
     return VB_OK;
@@ -338,28 +340,17 @@ int launch_attention(vb_ctx *ctx, const float *q, int64_t ldq, const uint16_t *k
 // records of the flash-decoding split.  It lives in the library image, so
 // every device that loads the library holds these bytes until the process
 // exits, and no call ever allocates.  Host code must not pass the symbol
-// itself to a kernel (on the host it names a stand-in, not device memory);
-// noalloc_scratch() resolves the real device address once per device.
+// itself to a kernel (on the host it names a stand-in, not device memory):
+// init_attention resolves the real device address when a context is
+// created, with its device current, and keeps it in the context, so the
+// address always belongs to the device context the calls run in.
 constexpr size_t NOALLOC_SCRATCH_BYTES = VB_ATTENTION_NOALLOC_SCRATCH_BYTES;
 static __device__ __align__(256) float g_attn_noalloc_scratch[NOALLOC_SCRATCH_BYTES / sizeof(float)];
 
-constexpr int NOALLOC_MAX_DEVICES = 64;
-static std::mutex g_noalloc_mu;
-static float *g_noalloc_ptr[NOALLOC_MAX_DEVICES];
-
-// Device address of the scratch array on ctx's device; the first call per
-// device looks it up (with that device current) and caches it.
-static int noalloc_scratch(vb_ctx *ctx, float **out) {
-    if (ctx->device < 0 || ctx->device >= NOALLOC_MAX_DEVICES)
-        return set_error(ctx, VB_ERR_INVALID_ARG, "attention_noalloc: device id %d out of range", ctx->device);
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_ptr[ctx->device]) {
-        VB_CHECK(ctx, cudaSetDevice(ctx->device));
-        void *p = nullptr;
-        VB_CHECK(ctx, cudaGetSymbolAddress(&p, g_attn_noalloc_scratch));
-        g_noalloc_ptr[ctx->device] = (float *)p;
-    }
-    *out = g_noalloc_ptr[ctx->device];
+int init_noalloc_scratch(vb_ctx *ctx) {
+    void *p = nullptr;
+    VB_CHECK(ctx, cudaGetSymbolAddress(&p, g_attn_noalloc_scratch));
+    ctx->attn_noalloc = p;
     return VB_OK;
 }
 
@@ -380,11 +371,8 @@ extern "C" int vb_attention_noalloc(vb_ctx *ctx, const float *q, const uint16_t 
                          "vb_attention_noalloc: needs %zu bytes of scratch (T=%d, heads=%d, head_dim=%d, rows=%d); "
                          "the fixed scratch holds %zu bytes -- use vb_attention or fewer rows/tokens per call",
                          need, T, n_heads, head_dim, n_rows, (size_t)NOALLOC_SCRATCH_BYTES);
-    float *part = nullptr;
-    if (need) {
-        int rc = noalloc_scratch(ctx, &part);
-        if (rc) return rc;
-    }
+    float *part = need ? static_cast<float *>(ctx->attn_noalloc) : nullptr;
+    if (need && !part) return set_error(ctx, VB_ERR_BACKEND, "vb_attention_noalloc: scratch address unresolved");
     return launch_attention_with(ctx, q, 0, k, v, n_rows, T, n_heads, n_kv_heads, head_dim, row_start, kv_len,
                                  n_rows, out, 0, part);
 }

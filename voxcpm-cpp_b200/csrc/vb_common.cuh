@@ -81,6 +81,7 @@ struct vb_ctx {
     size_t smem_optin = 0;
     bool use_gemm = true;               // tensor-core path for M >= 16 (VB_GEMM=0 disables)
     void *gemm = nullptr;               // tensor-core path state (vb_gemm.cu)
+    void *attn_noalloc = nullptr;       // device address of vb_attention_noalloc's fixed scratch on this device
 };
 
 namespace vb {

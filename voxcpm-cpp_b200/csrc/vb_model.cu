@@ -16,6 +16,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <map>
 
 namespace vb {
 
@@ -787,16 +788,61 @@ struct vb_dit {
     float *t_b1 = nullptr, *t_b2 = nullptr, *dt_b1 = nullptr, *dt_b2 = nullptr, *norm = nullptr;
     vb_lm *blocks = nullptr;
     size_t weight_bytes = 0;
+    // Per-call tables kept on the device, filled once outside stream capture
+    // (so a solve issues no host-to-device copy and can be captured after
+    // one eager call of the same shape): the time sinusoid of each t the CFM
+    // schedule visits, the block token tables per item count, the has_mu
+    // tables, and the solver's velocity buffer.
+    std::map<uint32_t, float *> sin_rows;       // t bits -> [hidden]
+    std::map<int, int32_t *> seg_tables;        // items -> [4][items * (3 + 2P)]
+    int *ones = nullptr;                        // [ones_n] all 1
+    int ones_n = 0;
+    int *cfg_hm = nullptr;                      // [2 * cfg_n]: n ones then n zeros
+    int cfg_n = 0, cfg_cap = 0;
+    int *user_hm = nullptr;                     // caller's has_mu, [user_cap]
+    int user_cap = 0;
+    vb::Arena vel;                              // velocities [items][patch * feat]
 };
 
 static void dit_free(vb_ctx *ctx, vb_dit *d) {
     if (!d) return;
+    if (ctx) cudaStreamSynchronize(ctx->stream);
     for (vb_weight w : {d->in_proj, d->cond_proj, d->out_proj, d->t_w1, d->t_w2, d->dt_w1, d->dt_w2})
         weight_free(ctx, w);
     for (float *p : {d->in_bias, d->cond_bias, d->out_bias, d->t_b1, d->t_b2, d->dt_b1, d->dt_b2, d->norm}) cudaFree(p);
+    for (auto &e : d->sin_rows) cudaFree(e.second);
+    for (auto &e : d->seg_tables) cudaFree(e.second);
+    cudaFree(d->ones);
+    cudaFree(d->cfg_hm);
+    cudaFree(d->user_hm);
+    cudaFree(d->vel.ptr);
     lm_free(ctx, d->blocks);
     delete d;
 }
+
+namespace vb {
+// Creating a device table synchronises and allocates, so it is refused
+// inside stream capture (the eager call before capture creates it).
+static bool capturing(vb_ctx *ctx) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    return cudaStreamIsCapturing(ctx->stream, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone;
+}
+
+static int device_table(vb_ctx *ctx, void **dst, const void *host, size_t bytes, const char *what) {
+    if (capturing(ctx))
+        return set_error(ctx, VB_ERR_BACKEND, "%s: table first needed during stream capture (run the call once "
+                         "before capturing it)", what);
+    if (fault_injected("alloc")) return set_error(ctx, VB_ERR_OOM, "%s: injected allocation fault", what);
+    VB_CHECK(ctx, cudaMalloc(dst, bytes));
+    const cudaError_t e = cudaMemcpy(*dst, host, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(*dst);
+        *dst = nullptr;
+        return check_cuda(ctx, e, what);
+    }
+    return VB_OK;
+}
+}  // namespace vb
 
 extern "C" int vb_dit_create(vb_ctx *ctx, const vb_dit_config *cfg, const vb_dit_host *w, vb_dit **out) {
     if (!ctx || !cfg || !w || !out) return VB_ERR_INVALID_ARG;
@@ -874,9 +920,64 @@ static void dit_time_sin(float t, int dim, float *out) {
     }
 }
 
+// Device row of the time sinusoid of t, cached per value of t (the CFM
+// schedule visits the same few values in every solve).
+static const float *dit_sin_row(vb_ctx *ctx, vb_dit *d, float t, int *rc) {
+    uint32_t key;
+    memcpy(&key, &t, 4);
+    auto it = d->sin_rows.find(key);
+    if (it != d->sin_rows.end()) return it->second;
+    const int H = d->cfg.hidden;
+    std::vector<float> row((size_t)H);
+    dit_time_sin(t, H, row.data());
+    void *dev = nullptr;
+    if ((*rc = device_table(ctx, &dev, row.data(), (size_t)H * 4, "LocDiT time sinusoid"))) return nullptr;
+    d->sin_rows[key] = (float *)dev;
+    return (const float *)dev;
+}
+
+// Token tables of the bidirectional blocks for `items` segments of T tokens:
+// rope position, K/V row, first visible row, visible rows.
+static const int32_t *dit_seg_table(vb_ctx *ctx, vb_dit *d, int items, int T, int *rc) {
+    auto it = d->seg_tables.find(items);
+    if (it != d->seg_tables.end()) return it->second;
+    const int M = items * T;
+    std::vector<int32_t> tab((size_t)4 * M);
+    for (int m = 0; m < M; m++) {
+        tab[m] = m % T;
+        tab[M + m] = m;
+        tab[2 * M + m] = (m / T) * T;
+        tab[3 * M + m] = T;
+    }
+    void *dev = nullptr;
+    if ((*rc = device_table(ctx, &dev, tab.data(), tab.size() * 4, "LocDiT token tables"))) return nullptr;
+    d->seg_tables[items] = (int32_t *)dev;
+    return (const int32_t *)dev;
+}
+
+// An all-ones has_mu table of at least n entries.
+static const int *dit_ones(vb_ctx *ctx, vb_dit *d, int n, int *rc) {
+    if (d->ones_n >= n) return d->ones;
+    if (capturing(ctx)) {
+        *rc = set_error(ctx, VB_ERR_BACKEND, "LocDiT has_mu table first needed during stream capture");
+        return nullptr;
+    }
+    std::vector<int> ones((size_t)n, 1);
+    void *dev = nullptr;
+    if ((*rc = device_table(ctx, &dev, ones.data(), (size_t)n * 4, "LocDiT has_mu table"))) return nullptr;
+    if (d->ones) {
+        cudaStreamSynchronize(ctx->stream);
+        cudaFree(d->ones);
+    }
+    d->ones = (int *)dev;
+    d->ones_n = n;
+    return d->ones;
+}
+
 // The LocDiT forward of n items.  x_mod: item rows of x/cond wrap modulo
 // x_mod items (the CFG batch reads the same patch for both branches).
-// t_shared: every item uses t[0], dt[0].
+// t_shared: every item uses t[0], dt[0] (then the sinusoids come from the
+// device cache and the call copies nothing from the host).
 static int dit_forward_impl(vb_ctx *ctx, vb_dit *d, int n, const float *x, const float *cond, int x_mod,
                             const float *t, const float *dt, int t_shared, const float *mu, const int *has_mu_dev,
                             float *out) {
@@ -885,13 +986,22 @@ static int dit_forward_impl(vb_ctx *ctx, vb_dit *d, int n, const float *x, const
     const int nt = t_shared ? 1 : n;
     const vb_lm_config &lc = d->blocks->cfg;
     const int M = (int)(n * T);
+    int rc = VB_OK;
+    // tables first: creating one synchronises, so it must not split the launches below
+    const float *ts_dev = nullptr, *dts_dev = nullptr;
+    if (t_shared) {
+        if (!(ts_dev = dit_sin_row(ctx, d, t[0], &rc))) return rc;
+        if (!(dts_dev = dit_sin_row(ctx, d, dt[0], &rc))) return rc;
+    }
+    const int32_t *tab = dit_seg_table(ctx, d, n, (int)T, &rc);
+    if (!tab) return rc;
+    if (mu && !has_mu_dev && !(has_mu_dev = dit_ones(ctx, d, n, &rc))) return rc;
     // workspace: blocks need their own carve region after ours
     size_t mine = align256((size_t)M * H * 4) + 4 * align256((size_t)nt * H * 4) + align256((size_t)n * P * H * 4) +
-                  align256((size_t)n * 4) + 4096;
+                  4096;
     size_t need = mine + layer_ws_bytes(lc, M) + 2 * align256((size_t)lc.n_kv_heads * M * lc.head_dim * 2) +
                   align256((size_t)16 * M) + 4096;
-    int rc = ws_reserve(ctx, need);
-    if (rc) return rc;
+    if ((rc = ws_reserve(ctx, need))) return rc;
     Carve cv(ctx->ws.ptr);
     float *seq = cv.take<float>((size_t)M * H);
     float *tsin = cv.take<float>((size_t)nt * H);
@@ -899,24 +1009,31 @@ static int dit_forward_impl(vb_ctx *ctx, vb_dit *d, int n, const float *x, const
     float *tf = cv.take<float>((size_t)nt * H);
     float *dtf = cv.take<float>((size_t)nt * H);
     float *xn = cv.take<float>((size_t)n * P * H);
-    int *hm = cv.take<int>((size_t)n);
 
-    // time embeddings: host sinusoid, device time MLPs
-    std::vector<float> ts((size_t)nt * H), dts((size_t)nt * H);
-    for (int i = 0; i < nt; i++) {
-        dit_time_sin(t[i], (int)H, ts.data() + (size_t)i * H);
-        dit_time_sin(dt[i], (int)H, dts.data() + (size_t)i * H);
+    // time embeddings: sinusoid (host libm, so the values equal the
+    // reference's), device time MLPs
+    std::vector<float> ts, dts;
+    if (!t_shared) {
+        ts.resize((size_t)nt * H);
+        dts.resize((size_t)nt * H);
+        for (int i = 0; i < nt; i++) {
+            dit_time_sin(t[i], (int)H, ts.data() + (size_t)i * H);
+            dit_time_sin(dt[i], (int)H, dts.data() + (size_t)i * H);
+        }
     }
-    MatmulOut o;
-    o.flags = VB_OUT_BF16;
-    auto time_mlp = [&](const std::vector<float> &sinv, vb_weight w1, const float *b1, vb_weight w2, const float *b2,
-                        float *dst) -> int {
-        VB_CHECK(ctx, cudaMemcpyAsync(tsin, sinv.data(), (size_t)nt * H * 4, cudaMemcpyHostToDevice, ctx->stream));
+    auto time_mlp = [&](const float *sin_dev, const std::vector<float> &sin_host, vb_weight w1, const float *b1,
+                        vb_weight w2, const float *b2, float *dst) -> int {
+        const float *src = sin_dev;
+        if (!src) {
+            VB_CHECK(ctx, cudaMemcpyAsync(tsin, sin_host.data(), (size_t)nt * H * 4, cudaMemcpyHostToDevice,
+                                          ctx->stream));
+            src = tsin;
+        }
         MatmulOut m1;
         m1.y = h1;
         m1.bias = b1;
         m1.flags = VB_OUT_BF16;
-        int r = launch_matmul(ctx, w1, tsin, nt, 0, 0, m1);
+        int r = launch_matmul(ctx, w1, src, nt, 0, 0, m1);
         if (r) return r;
         silu_bf16_kernel<<<(unsigned)((nt * H + 255) / 256), 256, 0, ctx->stream>>>(h1, nt * H);
         VB_LAUNCH_CHECK(ctx, "silu_bf16");
@@ -926,8 +1043,8 @@ static int dit_forward_impl(vb_ctx *ctx, vb_dit *d, int n, const float *x, const
         m2.flags = VB_OUT_BF16;
         return launch_matmul(ctx, w2, h1, nt, 0, 0, m2);
     };
-    if ((rc = time_mlp(ts, d->t_w1, d->t_b1, d->t_w2, d->t_b2, tf))) return rc;
-    if ((rc = time_mlp(dts, d->dt_w1, d->dt_b1, d->dt_w2, d->dt_b2, dtf))) return rc;
+    if ((rc = time_mlp(ts_dev, ts, d->t_w1, d->t_b1, d->t_w2, d->t_b2, tf))) return rc;
+    if ((rc = time_mlp(dts_dev, dts, d->dt_w1, d->dt_b1, d->dt_w2, d->dt_b2, dtf))) return rc;
 
     // x tokens -> rows 3+P.., cond tokens -> rows 3.. of every item
     MatmulOut ox;
@@ -943,13 +1060,6 @@ static int dit_forward_impl(vb_ctx *ctx, vb_dit *d, int n, const float *x, const
     ox.seg_off = 3;
     if ((rc = launch_matmul(ctx, d->cond_proj, cond, (int64_t)n * P, F, (int64_t)x_mod * P, ox))) return rc;
     // mu / zero tokens and the time token
-    if (mu) {
-        if (!has_mu_dev) {
-            std::vector<int> ones(n, 1);
-            VB_CHECK(ctx, cudaMemcpyAsync(hm, ones.data(), (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream));
-            has_mu_dev = hm;
-        }
-    }
     dit_head_kernel<<<n, 256, 0, ctx->stream>>>(seq, T, H, mu, has_mu_dev, tf, dtf, t_shared);
     VB_LAUNCH_CHECK(ctx, "dit_head");
     dump(ctx, "dit.tf", tf, H, nt);
@@ -959,23 +1069,18 @@ static int dit_forward_impl(vb_ctx *ctx, vb_dit *d, int n, const float *x, const
     // the blocks carve the workspace after our region
     Carve inner((uint8_t *)ctx->ws.ptr + align256(cv.off));
     {
-        const int M2 = M;
-        std::vector<int32_t> tab((size_t)4 * M2);
-        for (int m = 0; m < M2; m++) {
-            tab[m] = (int)(m % T);
-            tab[M2 + m] = m;
-            tab[2 * M2 + m] = (int)((m / T) * T);
-            tab[3 * M2 + m] = (int)T;
-        }
         TokenTables tt;
-        if ((rc = upload_tables(ctx, inner, M2, tab, tt))) return rc;
+        tt.pos = const_cast<int32_t *>(tab);
+        tt.dst = tt.pos + M;
+        tt.start = tt.pos + 2 * M;
+        tt.len = tt.pos + 3 * M;
         tt.max_len = (int)T;
         tt.seg_T = (int)T;
-        const size_t kv_elems = (size_t)lc.n_kv_heads * M2 * lc.head_dim;
+        const size_t kv_elems = (size_t)lc.n_kv_heads * M * lc.head_dim;
         uint16_t *kc = inner.take<uint16_t>(kv_elems);
         uint16_t *vc = inner.take<uint16_t>(kv_elems);
         g_dump_prefix = "dit.";
-        rc = run_layers(ctx, d->blocks, M2, seq, tt, kc, vc, 0, M2, inner);
+        rc = run_layers(ctx, d->blocks, M, seq, tt, kc, vc, 0, M, inner);
         g_dump_prefix = "";
         if (rc) return rc;
     }
@@ -999,17 +1104,24 @@ static int dit_forward_impl(vb_ctx *ctx, vb_dit *d, int n, const float *x, const
 extern "C" int vb_dit_forward(vb_ctx *ctx, vb_dit *d, int n, const float *x, const float *cond, const float *t,
                               const float *dt, const float *mu, const int *has_mu, float *out) {
     if (!ctx || !d || n <= 0 || !x || !cond || !t || !dt || !out) return VB_ERR_INVALID_ARG;
-    int *hm_dev = nullptr;
+    const int *hm_dev = nullptr;
     if (mu && has_mu) {
-        VB_CHECK(ctx, cudaMalloc(&hm_dev, (size_t)n * 4));
-        cudaMemcpyAsync(hm_dev, has_mu, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream);
+        // the caller's per-item flags go to a buffer of the estimator (grown,
+        // never freed per call); the copy from pageable memory is staged, so
+        // the caller may reuse its array when this returns
+        if (d->user_cap < n) {
+            if (capturing(ctx)) return set_error(ctx, VB_ERR_BACKEND, "vb_dit_forward: has_mu buffer grows during capture");
+            VB_CHECK(ctx, cudaStreamSynchronize(ctx->stream));
+            cudaFree(d->user_hm);
+            d->user_hm = nullptr;
+            d->user_cap = 0;
+            VB_CHECK(ctx, cudaMalloc(&d->user_hm, (size_t)n * 4));
+            d->user_cap = n;
+        }
+        VB_CHECK(ctx, cudaMemcpyAsync(d->user_hm, has_mu, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream));
+        hm_dev = d->user_hm;
     }
-    int rc = dit_forward_impl(ctx, d, n, x, cond, n, t, dt, 0, mu, hm_dev, out);
-    if (hm_dev) {
-        cudaStreamSynchronize(ctx->stream);
-        cudaFree(hm_dev);
-    }
-    return rc;
+    return dit_forward_impl(ctx, d, n, x, cond, n, t, dt, 0, mu, hm_dev, out);
 }
 
 extern "C" int vb_cfm_solve(vb_ctx *ctx, vb_dit *d, int n, const float *mu, const float *cond, float *x, int n_steps,
@@ -1020,28 +1132,41 @@ extern "C" int vb_cfm_solve(vb_ctx *ctx, vb_dit *d, int n, const float *mu, cons
     const int use_cfg = (cfg_value != 1.0f && mu != nullptr);
     const int items = use_cfg ? 2 * n : n;
     const int zero_star = vb_cfm_zero_star_steps(n_steps);
-    // velocity buffer and the has_mu table live in the attention arena's
-    // neighbour: a dedicated allocation sized once per call shape.
-    float *vel = nullptr;
-    int *hm = nullptr;
-    VB_CHECK(ctx, cudaMallocAsync(&vel, (size_t)items * len * 4, ctx->stream));
-    VB_CHECK(ctx, cudaMallocAsync(&hm, (size_t)items * 4, ctx->stream));
-    std::vector<int> hmh(items, 0);
-    for (int i = 0; i < n; i++) hmh[i] = 1;
-    int rc = VB_OK;
-    if (cudaMemcpyAsync(hm, hmh.data(), (size_t)items * 4, cudaMemcpyHostToDevice, ctx->stream) != cudaSuccess)
-        rc = set_error(ctx, VB_ERR_BACKEND, "cfm: upload failed");
-    for (int step = zero_star; step < n_steps && rc == VB_OK; step++) {
+    // velocities and the branch table live in the estimator (grown outside
+    // capture); with them and the cached sinusoids the solve copies nothing
+    // from the host, so one eager call makes the same shape capturable
+    int rc = arena_reserve(ctx, d->vel, (size_t)items * len * 4);
+    if (rc) return rc;
+    float *vel = (float *)d->vel.ptr;
+    const int *hm = nullptr;
+    if (use_cfg) {
+        if (d->cfg_n != n) {
+            if (capturing(ctx)) return set_error(ctx, VB_ERR_BACKEND, "vb_cfm_solve: branch table changes during capture");
+            std::vector<int> hmh((size_t)items, 0);
+            for (int i = 0; i < n; i++) hmh[i] = 1;
+            if (d->cfg_cap < items) {
+                VB_CHECK(ctx, cudaStreamSynchronize(ctx->stream));
+                cudaFree(d->cfg_hm);
+                d->cfg_hm = nullptr;
+                d->cfg_cap = 0;
+                VB_CHECK(ctx, cudaMalloc(&d->cfg_hm, (size_t)items * 4));
+                d->cfg_cap = items;
+            }
+            VB_CHECK(ctx, cudaMemcpyAsync(d->cfg_hm, hmh.data(), (size_t)items * 4, cudaMemcpyHostToDevice, ctx->stream));
+            d->cfg_n = n;
+        }
+        hm = d->cfg_hm;
+    } else if (mu) {
+        if (!(hm = dit_ones(ctx, d, items, &rc))) return rc;
+    }
+    for (int step = zero_star; step < n_steps; step++) {
         const float t = vb_cfm_sway_t_bf16(step, n_steps);
         const float nt = vb_cfm_sway_t_bf16(step + 1, n_steps);
-            const float step_size = ::vb_host_bf16(-(t - nt));
+        const float step_size = ::vb_host_bf16(-(t - nt));
         const float zero = 0.0f;
-        rc = dit_forward_impl(ctx, d, items, x, cond, n, &t, &zero, 1, mu, hm, vel);
-        if (rc) break;
+        if ((rc = dit_forward_impl(ctx, d, items, x, cond, n, &t, &zero, 1, mu, hm, vel))) return rc;
         cfm_update_kernel<<<n, 256, 0, ctx->stream>>>(x, vel, n, len, use_cfg, cfg_value, step_size);
-        rc = check_launch(ctx, "cfm_update");
+        if ((rc = check_launch(ctx, "cfm_update"))) return rc;
     }
-    cudaFreeAsync(vel, ctx->stream);
-    cudaFreeAsync(hm, ctx->stream);
-    return rc;
+    return VB_OK;
 }
