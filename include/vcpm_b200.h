@@ -163,9 +163,19 @@ int vb_program_create(vb_ctx *ctx, int n_ops, const vb_gemv_op *ops,
 /* Enqueues one run on the context stream (capturable in a vb_graph). */
 int vb_program_run(vb_ctx *ctx, vb_program p);
 /* Waits for the stream and reports a device-side error code (a bounded
- * wait that timed out); 0 = OK. */
+ * wait that timed out); 0 = OK.  A reported code is cleared, so the program
+ * can run again. */
 int vb_program_status(vb_ctx *ctx, vb_program p, int *device_error);
 void vb_program_destroy(vb_program p);
+/* Diagnosis hook for the streaming kernel (programs and the decode step):
+ * the number of GPU clock cycles one wait on other CTAs (a grid dependency
+ * or a value another CTA writes) may take before the kernel records
+ * STREAM_TIMEOUT_GRID (device error 3), stops and exits; 0 restores the
+ * default (4e9 cycles, about 2 s).  Waits for the CTA's own weight copies
+ * keep the default.  The failure path this exercises (bounded wait, error
+ * code, clean exit, a context that stays usable) has no counterpart in the
+ * reference, whose host waits on ggml's synchronous compute. */
+int vb_set_wait_limit(vb_ctx *ctx, long long cycles);
 
 /* Q8_0 quantization of M rows of K floats into GGUF blocks (34 bytes per
  * 32 values) -- the activation conversion inside every Q8_0 ggml_mul_mat. */
@@ -311,7 +321,10 @@ int vb_lm_forward_noncausal(vb_ctx *ctx, vb_lm *lm, int n, int T, float *h);
  * vb_lm_forward(n, seq, pos, T = 1) does; results agree with it within the
  * fp32 accumulation-order tolerance.  x, out: device [n][hidden].  A step is
  * asynchronous; vb_decoder_status synchronises and reports a device-side
- * timeout (the kernel's waits are bounded). */
+ * timeout (the kernel's waits are bounded).  After a reported error the
+ * decoder can step again; the failed step's token was still counted in the
+ * KV slots (vb_kv_used), which the caller resets or rewinds by prefilling
+ * again. */
 typedef struct vb_decoder_s *vb_decoder;
 int vb_decoder_create(vb_ctx *ctx, vb_lm *lm, vb_kv *kv, int n,
                       const int32_t *seq, vb_decoder *out);

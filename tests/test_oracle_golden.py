@@ -18,6 +18,7 @@ import pytest
 
 import oracle as O
 
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 FX = os.path.join(GOLD, "ref_fixtures")
 KAT = json.load(open(os.path.join(GOLD, "reference_kat.json")))
@@ -35,7 +36,8 @@ def cos_rmse(a, b):
 
 
 def test_manifest_matches_reference_when_present():
-    ref = os.environ.get("VCPM_REFERENCE_DIR", "/root/reference")
+    # the reference tree beside this repository, or VCPM_REFERENCE_DIR
+    ref = os.environ.get("VCPM_REFERENCE_DIR") or os.path.normpath(os.path.join(ROOT, "..", "reference"))
     fx = os.path.join(ref, "tests", "fixtures")
     if not os.path.isdir(fx):
         pytest.skip("reference tree not mounted")

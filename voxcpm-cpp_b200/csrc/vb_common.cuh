@@ -82,6 +82,7 @@ struct vb_ctx {
     bool use_gemm = true;               // tensor-core path for M >= 16 (VB_GEMM=0 disables)
     void *gemm = nullptr;               // tensor-core path state (vb_gemm.cu)
     void *attn_noalloc = nullptr;       // device address of vb_attention_noalloc's fixed scratch on this device
+    long long dep_wait_limit = 0;       // streaming kernel: cycles of a wait on other CTAs (0 = default)
 };
 
 namespace vb {

@@ -34,7 +34,7 @@ namespace vb {
 __global__ void __launch_bounds__(ST_THREADS, 1)
     stream_gemv_kernel(const StreamOp *__restrict__ ops, const int2 *__restrict__ rows,
                        const uint16_t *__restrict__ idx, const int *__restrict__ counts, int n_ops, unsigned *bars,
-                       int *err, const StreamStep step, const int ns) {
+                       int *err, const StreamStep step, const int ns, const long long dep_limit) {
     extern __shared__ __align__(128) uint8_t sm[];
     uint8_t *wslot = sm;
     uint8_t *sslot = wslot + (size_t)ns * ST_SLOT;
@@ -58,6 +58,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             mbar_init(&empty[s], ST_CONSUMER_WARPS);
         }
         s_abort = 0;
+        s_dep_limit = dep_limit;
         mbar_fence_init();
     }
     // step parameters to shared memory (constant offsets into the argument)
@@ -414,7 +415,8 @@ int stream_program_launch(vb_ctx *ctx, vb_program p, const StreamStep &step) {
     cfg.numAttrs = 1;
     VB_CHECK(ctx, cudaLaunchKernelEx(&cfg, stream_gemv_kernel, (const StreamOp *)p->d_ops, (const int2 *)p->d_rows,
                                      (const uint16_t *)p->d_idx, (const int *)p->d_counts, p->n_ops, p->d_bars,
-                                     p->d_err, step, p->stages));
+                                     p->d_err, step, p->stages,
+                                     ctx->dep_wait_limit > 0 ? ctx->dep_wait_limit : WAIT_LIMIT_CYCLES));
     VB_LAUNCH_CHECK(ctx, "stream_gemv");
     return VB_OK;
 }
@@ -470,6 +472,12 @@ extern "C" int vb_program_create(vb_ctx *ctx, int n_ops, const vb_gemv_op *ops, 
     return stream_program_build(ctx, h, n_groups, 0, wbytes, out);
 }
 
+extern "C" int vb_set_wait_limit(vb_ctx *ctx, long long cycles) {
+    if (!ctx || cycles < 0) return VB_ERR_INVALID_ARG;
+    ctx->dep_wait_limit = cycles;
+    return VB_OK;
+}
+
 extern "C" int vb_program_run(vb_ctx *ctx, vb_program p) {
     if (!ctx || !p) return VB_ERR_INVALID_ARG;
     return stream_program_launch(ctx, p, StreamStep{});
@@ -478,7 +486,11 @@ extern "C" int vb_program_status(vb_ctx *ctx, vb_program p, int *device_error) {
     if (!ctx || !p || !device_error) return VB_ERR_INVALID_ARG;
     VB_CHECK(ctx, cudaStreamSynchronize(ctx->stream));
     VB_CHECK(ctx, cudaMemcpy(device_error, p->d_err, sizeof(int), cudaMemcpyDeviceToHost));
-    if (*device_error) return set_error(ctx, VB_ERR_BACKEND, "streaming kernel reported error %d", *device_error);
+    if (*device_error) {
+        // reported once: clear it so the program can run again
+        VB_CHECK(ctx, cudaMemset(p->d_err, 0, sizeof(int)));
+        return set_error(ctx, VB_ERR_BACKEND, "streaming kernel reported error %d", *device_error);
+    }
     return VB_OK;
 }
 

@@ -10,6 +10,10 @@
 
 namespace vb {
 
+// Cycles a wait on other CTAs (a grid dependency) may take before the kernel
+// records a timeout: the launch argument of vb_set_wait_limit, per CTA.
+__shared__ long long s_dep_limit;
+
 // Epilogue of one output value.  Values written earlier in the same launch
 // (the residual stream) are read through L2 (__ldcg), never through the
 // non-coherent per-SM L1.
@@ -53,7 +57,7 @@ __device__ __forceinline__ bool wait_grid(const unsigned *ctr, unsigned target, 
     const long long t0 = clock64();
     while (ld_acquire_gpu(ctr) < target) {
         if (*abort_flag) return false;
-        if (clock64() - t0 > WAIT_LIMIT_CYCLES) return false;
+        if (clock64() - t0 > s_dep_limit) return false;
         __nanosleep(64);
     }
     return true;

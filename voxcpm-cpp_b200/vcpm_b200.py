@@ -107,6 +107,7 @@ SIGNATURES = {
     "vb_program_run": (_I, [_P, _P]),
     "vb_program_status": (_I, [_P, _P, C.POINTER(_I)]),
     "vb_program_destroy": (None, [_P]),
+    "vb_set_wait_limit": (_I, [_P, C.c_longlong]),
     "vb_quantize_q8_0": (_I, [_P, _P, _I64, _I64, _P, _I]),
     "vb_dequantize_q8_0": (_I, [_P, _P, _I64, _P]),
     "vb_get_rows": (_I, [_P, _P, _P, _I64, _P]),
@@ -239,6 +240,10 @@ class Context:
 
     def set_qrule(self, rule):
         self.check(self.L.vb_set_qrule(self.h, rule))
+
+    def set_wait_limit(self, cycles):
+        """Streaming-kernel limit (GPU cycles) of a wait on other CTAs; 0 = default."""
+        self.check(self.L.vb_set_wait_limit(self.h, cycles))
 
     # ------------------------------------------------------------- graphs
     def graph_begin(self):
