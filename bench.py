@@ -50,6 +50,7 @@ OUT_PER_LAYER = sum(s[2] for s in SHAPES)
 # dram bytes (read + write) of one headline-step launch of stream_gemv_kernel
 # from the ncu capture summarised in profiles/stream_gemv_headline_step.md
 NCU_TRAFFIC_STEP = 1_412_116_664
+CHAIN_LAUNCHES = 224   # config-1 launch chain: 4 passes over 56 distinct weights
 
 
 # ------------------------------------------------------ multi-rank helpers
@@ -355,8 +356,15 @@ def run_b200(args, rank, world, local_rank):
             i += 1
     g_launch = ctx.graph_end()
 
-    # config-1 shape alone: the 56 gate/up weights [2048 -> 6144] in one program
+    # config 1 as the single ggml_mul_mat the reference issues: CHAIN_LAUNCHES
+    # back-to-back vb_matmul launches in one graph, rotating over the 56
+    # distinct gate/up weights [2048 -> 6144] (750 MB, larger than L2)
     c1 = [(w, K, N) for (name, K, N, w) in weights if name in ("gate", "up")]
+    ctx.graph_begin()
+    for j in range(CHAIN_LAUNCHES):
+        ctx.matmul(c1[j % len(c1)][0], xo, 1, yo)
+    g_c1chain = ctx.graph_end()
+
     prog1 = vb.Program(ctx, [dict(w=w, x=xo, y=yo, M=1, group=0) for w, K, N in c1])
     ctx.graph_begin()
     prog1.run()
@@ -408,6 +416,13 @@ def run_b200(args, rank, world, local_rank):
     kl = max(5, args.steps // 4)
     ms_l = timed(lambda: ctx.graph_launch(g_launch), kl)
     per_launch_gbs = STEP_BYTES * kl / (ms_l * 1e-3) / 1e9
+
+    # config 1 as a launch chain
+    for _ in range(3):
+        ctx.graph_launch(g_c1chain)
+    kc = max(3, args.steps // 8)
+    ms_cc = timed(lambda: ctx.graph_launch(g_c1chain), kc)
+    c1_chain_gbs = alg_bytes(2048, 6144) * CHAIN_LAUNCHES * kc / (ms_cc * 1e-3) / 1e9
 
     # decode-shaped dependency chain of the same GEMVs
     for _ in range(3):
@@ -472,6 +487,8 @@ def run_b200(args, rank, world, local_rank):
                          "achieved_config1": c1_gbs, "config1_us_per_gemv": per_gemv_ms * 1e3,
                          "config1_alg_bytes": alg_bytes(2048, 6144),
                          "separate_launches_gbs": per_launch_gbs,
+                         "config1_launch_chain_gbs": c1_chain_gbs,
+                         "config1_launch_chain_us_per_launch": ms_cc * 1e3 / (kc * CHAIN_LAUNCHES),
                          "decode_chain_gbs": chain_gbs},
             "sweep": sweep,
             "cpu_baseline": base,
@@ -491,6 +508,7 @@ def run_b200(args, rank, world, local_rank):
     ctx.graph_destroy(g)
     ctx.graph_destroy(g1)
     ctx.graph_destroy(g_launch)
+    ctx.graph_destroy(g_c1chain)
     prog.close()
     prog1.close()
     prog_chain.close()
@@ -669,6 +687,52 @@ def run_vae_case(args, local_rank):
     vae.close()
     ctx.close()
     return 0
+
+
+def run_launches_case(args, local_rank):
+    """Profiling case: vb_matmul as separate launches in a graph -- config 1
+    (CHAIN_LAUNCHES launches over 56 distinct W[2048->6144]) and the 196
+    projection GEMVs of 28 layers.  Prints GB/s of both."""
+    import torch
+    import vcpm_b200 as vb
+    torch.cuda.set_device(local_rank)
+    ctx = vb.Context(local_rank)
+    rng = np.random.default_rng(3)
+    ws = [(name, K, N, ctx.weight(vb.TYPE_Q8_0, K, N, synth_q8_0(rng, N, K))) for _ in range(LAYERS)
+          for name, K, N, _ in SHAPES]
+    X = torch.randn(FFN, dtype=torch.float32, device="cuda")
+    Y = torch.zeros(FFN, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    c1 = [w for name, K, N, w in ws if name in ("gate", "up")]
+    ctx.graph_begin()
+    for j in range(CHAIN_LAUNCHES):
+        ctx.matmul(c1[j % len(c1)], X.data_ptr(), 1, Y.data_ptr())
+    g1 = ctx.graph_end()
+    ctx.graph_begin()
+    for name, K, N, w in ws:
+        ctx.matmul(w, X.data_ptr(), 1, Y.data_ptr())
+    g2 = ctx.graph_end()
+    ev0, ev1 = ctx.event(), ctx.event()
+    out = {}
+    for key, g, nbytes in (("config1_launch_chain_gbs", g1, alg_bytes(2048, 6144) * CHAIN_LAUNCHES),
+                           ("separate_launches_gbs", g2, STEP_BYTES)):
+        for _ in range(args.warmup):
+            ctx.graph_launch(g)
+        ctx.record(ev0)
+        for _ in range(args.steps):
+            ctx.graph_launch(g)
+        ctx.record(ev1)
+        ms = ctx.elapsed_ms(ev0, ev1)
+        out[key] = nbytes * args.steps / (ms * 1e-3) / 1e9
+    rc, derr = ctx.device_status()
+    out.update(mode="launches", device_error=derr)
+    print(json.dumps(out), flush=True)
+    ctx.graph_destroy(g1)
+    ctx.graph_destroy(g2)
+    for *_, w in ws:
+        w.release()
+    ctx.close()
+    return 0 if rc == 0 else 1
 
 
 def run_decode_case(args, local_rank):
@@ -1099,7 +1163,7 @@ def main():
     ap.add_argument("--e2e-utts", type=int, default=64)
     ap.add_argument("--e2e-patches", type=int, default=100)
     ap.add_argument("--e2e-clock-ms", type=int, default=500, help="nvidia-smi sampling period during the e2e run")
-    ap.add_argument("--mode", default="full", choices=["full", "config1", "gemm", "decode", "vae"],
+    ap.add_argument("--mode", default="full", choices=["full", "config1", "gemm", "decode", "vae", "launches"],
                     help="config1 / gemm / decode: small profiling cases (config-1 streaming program, one "
                          "tensor-core mat-mul shape, the single-launch decode step)")
     ap.add_argument("--gemm-shape", default="1408,1024,8192")
@@ -1123,6 +1187,8 @@ def main():
         return run_vae_case(args, local_rank)
     if args.mode == "decode":
         return run_decode_case(args, local_rank)
+    if args.mode == "launches":
+        return run_launches_case(args, local_rank)
     if world > 1:
         import datetime
         import torch

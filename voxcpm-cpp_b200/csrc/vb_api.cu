@@ -205,7 +205,7 @@ extern "C" int vb_device_status(vb_ctx *ctx, int *device_error) {
     if (!ctx || !device_error) return VB_ERR_INVALID_ARG;
     int rc = gemm_device_error(ctx, device_error);
     if (rc) return rc;
-    if (*device_error) return set_error(ctx, VB_ERR_BACKEND, "tensor-core kernel reported error %d", *device_error);
+    if (*device_error) return set_error(ctx, VB_ERR_BACKEND, "mat-mul kernel reported error %d", *device_error);
     return VB_OK;
 }
 

@@ -795,6 +795,9 @@ int init_gemm(vb_ctx *ctx) {
                                        GM_SMEM_BUDGET + 1024));
     VB_CHECK(ctx, cudaFuncSetAttribute(gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        GM_SMEM_BUDGET + 1024));
+    // the mat-mul kernels' counters and error word exist from creation on, so
+    // no later call allocates them (and every call can be captured)
+    if (!gemm_state(ctx)) return set_error(ctx, VB_ERR_OOM, "mat-mul state allocation failed");
     return VB_OK;
 }
 
@@ -1097,6 +1100,11 @@ int launch_gemm_tf32(vb_ctx *ctx, Tf32Weight &w, const float *a_hi, const float 
         am->tl, g);
     VB_LAUNCH_CHECK(ctx, "gemm_tf32");
     return VB_OK;
+}
+
+int *gemm_error_word(vb_ctx *ctx) {
+    GemmState *gs = gemm_state(ctx);
+    return gs ? gs->err : nullptr;
 }
 
 int gemm_device_error(vb_ctx *ctx, int *code) {

@@ -288,6 +288,11 @@ int launch_matmul(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t l
     if (out.ldy == 0) out.ldy = w->N;
     if (out.seg == 0) { out.seg = M; out.seg_stride = 0; out.seg_off = 0; }
     if (ctx->use_gemm && gemm_supported(w, M)) return launch_gemm(ctx, w, x, M, ldx, x_mod, out);
+    {
+        // small M on Q8_0 / F16: the weight-streaming kernel as a single op
+        const int rc = launch_stream1(ctx, w, x, M, ldx ? ldx : w->K, x_mod > 0 ? x_mod : M, out);
+        if (rc >= 0) return rc;
+    }
     GemvArgs a;
     a.w = w->data;
     a.sc = w->scales;

@@ -56,6 +56,14 @@ bool matmul_uses_gemm(vb_ctx *ctx, vb_weight w, int64_t M);
 int launch_matmul_pro(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx, const GemmPro &pro,
                       const MatmulOut &out);
 int gemm_device_error(vb_ctx *ctx, int *code);
+// The context's device error word of the mat-mul kernels (created on first
+// use): a bounded wait that runs out records its code there.
+int *gemm_error_word(vb_ctx *ctx);
+// vb_matmul for M <= 8 on a Q8_0 / F16 weight through the weight-streaming
+// kernel as a single op (vb_stream.cu); -1 when the shape is not supported
+// there (the caller then takes the per-launch GEMV kernel).
+int launch_stream1(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx, int64_t x_mod,
+                   const MatmulOut &out);
 void gemm_free(vb_ctx *ctx);
 
 int launch_quantize_q8_0(vb_ctx *ctx, const float *x, int64_t K, int64_t M, void *blocks, int rule);

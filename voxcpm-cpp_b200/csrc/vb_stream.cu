@@ -23,6 +23,8 @@
 // depend on activations -- so it keeps HBM busy through the barriers, up to
 // the ring depth.  Every wait is bounded: on timeout the kernel records an
 // error code, stops issuing work, drains its own bulk copies and exits.
+#include <algorithm>
+
 #include "vb_common.cuh"
 #include "vb_kernels.cuh"
 #include "vb_device.cuh"
@@ -265,6 +267,161 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     }
 }
 
+// ------------------------------------------------------------ one mat-mul
+// vb_matmul for M <= 8 on a Q8_0 / F16 weight: the same ring and mat-vec
+// routines as a program, for ONE op passed by value (no program upload).  The
+// CTAs split the op's rows evenly; with a small activation operand two CTAs
+// share an SM, so a CTA of the next launch streams while one of this launch
+// finishes.  Programmatic dependent launch: every CTA lets the next launch
+// be scheduled at once, and its producer starts on the weights (which no
+// kernel writes) right away; the consumers wait for the previous kernel to
+// complete before they read x or write y.
+constexpr int ST1_EARLY = 1;   // weight chunks a CTA requests before its activation operand is loaded
+
+__device__ __forceinline__ void pdl_wait_prev() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_let_next() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__global__ void __launch_bounds__(ST_THREADS, 2)
+    stream_gemv1_kernel(const __grid_constant__ StreamOp op, int *err, const int ns, const int xq_bytes) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    uint8_t *wslot = sm;
+    uint8_t *sslot = wslot + (size_t)ns * ST_SLOT;
+    int8_t *xq = reinterpret_cast<int8_t *>(sslot + (size_t)ns * ST_SC_SLOT);
+    float *xd = reinterpret_cast<float *>(xq + xq_bytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(xd + xq_bytes / 32);
+    uint64_t *empty = full + ST_STAGES_MAX;
+    __shared__ volatile int s_abort1;
+    __shared__ volatile int s_xready;   // the consumers hold the activation operand
+    __shared__ float s_part[2 * ST_CONSUMER_WARPS];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x, cta = blockIdx.x;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ns; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], ST_CONSUMER_WARPS);
+        }
+        s_abort1 = 0;
+        s_xready = 0;
+        mbar_fence_init();
+    }
+    pdl_let_next();
+    __syncthreads();
+    int64_t r0, r1;
+    rows_of(op.N, cta, G, r0, r1);
+    const int R = op.rows_per_chunk, nb = op.K / QK;
+
+    if (warp == 0) {   // producer
+        if (lane != 0) return;
+        int slot = 0;
+        uint32_t phase = 0;
+        long long fills = 0;
+        for (int64_t r = r0; r < r1 && !s_abort1; r += R) {
+            const int nr = (int)((r1 - r) < R ? (r1 - r) : R);
+            // The first chunk goes out at once (it may overlap the previous
+            // kernel); the rest only after the consumers have loaded x, whose
+            // loads would otherwise queue behind every CTA's weight bytes.
+            if (fills == ST1_EARLY) {
+                const long long t0 = clock64();
+                while (!s_xready && !s_abort1) {
+                    if (clock64() - t0 > WAIT_LIMIT_CYCLES) { atomicCAS(err, 0, STREAM_TIMEOUT_GRID); s_abort1 = 1; }
+                }
+                if (s_abort1) break;
+            }
+            if (!wait_phase(&empty[slot], phase ^ 1u, &s_abort1)) {
+                if (!s_abort1) { atomicCAS(err, 0, STREAM_TIMEOUT_EMPTY); s_abort1 = 1; }
+                break;
+            }
+            const uint32_t wb = (uint32_t)nr * (uint32_t)op.row_bytes;
+            const uint32_t sb = op.sc_bulk ? (uint32_t)nr * (uint32_t)nb * 2u : 0u;
+            mbar_arrive_expect_tx(&full[slot], wb + sb);
+            bulk_g2s(wslot + (size_t)slot * ST_SLOT, op.w + r * op.row_bytes, wb, &full[slot]);
+            if (sb) bulk_g2s(sslot + (size_t)slot * ST_SC_SLOT, op.sc + r * nb, sb, &full[slot]);
+            fills++;
+            if (++slot == ns) { slot = 0; phase ^= 1u; }
+        }
+        for (int s = 0; s < ns; s++) {
+            const long long n_s = fills / ns + ((fills % ns) > s ? 1 : 0);
+            if (n_s == 0) continue;
+            const uint32_t par = (uint32_t)((n_s - 1) & 1);
+            const long long t0 = clock64();
+            while (!mbar_try_wait(&full[s], par)) {
+                if (clock64() - t0 > WAIT_LIMIT_CYCLES) { atomicCAS(err, 0, STREAM_TIMEOUT_FULL); break; }
+            }
+        }
+        return;
+    }
+
+    // consumers
+    const int ctid = threadIdx.x - 32, cw = warp - 1;
+    pdl_wait_prev();   // x written and y free: the previous kernel has completed
+    if (r1 <= r0) return;
+    stream_prologue(op, xq, xd, nullptr, ctid, cw, lane);
+    if (ctid == 0) s_xready = 1;
+    int slot = 0;
+    uint32_t phase = 0;
+    [[maybe_unused]] bool ok = true;
+    const int K = op.K, M = op.M;
+    if (op.wtype == VB_TYPE_Q8_0 && M == 1 && (K == 1024 || K == 2048 || K == 4096 || K == 6144 || K == 8192)) {
+        switch (K) {
+            case 1024: ok = q8_m1_op<16, 4>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort1, err, ns); break;
+            case 2048: ok = q8_m1_op<16, 8>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort1, err, ns); break;
+            case 4096: ok = q8_m1_op<16, 16>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort1, err, ns); break;
+            case 6144: ok = q8_m1_op<32, 12>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort1, err, ns); break;
+            default: ok = q8_m1_op<32, 16>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort1, err, ns); break;
+        }
+    } else if (op.wtype == VB_TYPE_F16 && M == 1 && (K == 1024 || K == 2048)) {
+        const uint16_t *xh = reinterpret_cast<const uint16_t *>(xq);
+        ok = K == 1024 ? f16_m1_op<16, 8>(op, wslot, xh, full, empty, slot, phase, r0, r1, cw, lane, &s_abort1, err, ns)
+                       : f16_m1_op<32, 8>(op, wslot, xh, full, empty, slot, phase, r0, r1, cw, lane, &s_abort1, err, ns);
+    } else if (op.wtype == VB_TYPE_F16 && M == 1 &&
+               ((K == 4096 && R == 4) || ((K == 6144 || K == 8192) && R == 2))) {
+        const uint16_t *xh = reinterpret_cast<const uint16_t *>(xq);
+        switch (K) {
+            case 4096: ok = f16_m1_split_op<2, 8>(op, wslot, xh, s_part, full, empty, slot, phase, r0, r1, cw, lane, &s_abort1, err, ns); break;
+            case 6144: ok = f16_m1_split_op<4, 6>(op, wslot, xh, s_part, full, empty, slot, phase, r0, r1, cw, lane, &s_abort1, err, ns); break;
+            default: ok = f16_m1_split_op<4, 8>(op, wslot, xh, s_part, full, empty, slot, phase, r0, r1, cw, lane, &s_abort1, err, ns); break;
+        }
+    } else {
+        for (int64_t r = r0; r < r1; r += R) {
+            const int nr = (int)((r1 - r) < R ? (r1 - r) : R);
+            if (!wait_phase(&full[slot], phase, &s_abort1)) {
+                if (!s_abort1) { atomicCAS(err, 0, STREAM_TIMEOUT_FULL); s_abort1 = 1; }
+                break;
+            }
+            const uint8_t *wt = wslot + (size_t)slot * ST_SLOT;
+            if (op.wtype == VB_TYPE_Q8_0) {
+                const uint16_t *sct = op.sc_bulk ? reinterpret_cast<const uint16_t *>(sslot + (size_t)slot * ST_SC_SLOT)
+                                                 : op.sc + r * nb;
+                switch (M) {
+                    case 1: q8_chunk<1>(op, wt, sct, xq, xd, nr, cw, lane, r); break;
+                    case 2: q8_chunk<2>(op, wt, sct, xq, xd, nr, cw, lane, r); break;
+                    case 3: q8_chunk<3>(op, wt, sct, xq, xd, nr, cw, lane, r); break;
+                    case 4: q8_chunk<4>(op, wt, sct, xq, xd, nr, cw, lane, r); break;
+                    case 5: q8_chunk<5>(op, wt, sct, xq, xd, nr, cw, lane, r); break;
+                    case 6: q8_chunk<6>(op, wt, sct, xq, xd, nr, cw, lane, r); break;
+                    case 7: q8_chunk<7>(op, wt, sct, xq, xd, nr, cw, lane, r); break;
+                    default: q8_chunk<8>(op, wt, sct, xq, xd, nr, cw, lane, r); break;
+                }
+            } else {
+                const uint16_t *xh = reinterpret_cast<const uint16_t *>(xq);
+                switch (M) {
+                    case 1: f16_chunk<1>(op, wt, xh, nr, cw, lane, r); break;
+                    case 2: f16_chunk<2>(op, wt, xh, nr, cw, lane, r); break;
+                    case 3: f16_chunk<3>(op, wt, xh, nr, cw, lane, r); break;
+                    case 4: f16_chunk<4>(op, wt, xh, nr, cw, lane, r); break;
+                    case 5: f16_chunk<5>(op, wt, xh, nr, cw, lane, r); break;
+                    case 6: f16_chunk<6>(op, wt, xh, nr, cw, lane, r); break;
+                    case 7: f16_chunk<7>(op, wt, xh, nr, cw, lane, r); break;
+                    default: f16_chunk<8>(op, wt, xh, nr, cw, lane, r); break;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (++slot == ns) { slot = 0; phase ^= 1u; }
+        }
+    }
+}
+
 }  // namespace vb
 
 using namespace vb;
@@ -300,8 +457,82 @@ struct vb_program_s {
 };
 
 namespace vb {
+// Dynamic shared memory of a one-op launch: ST1_STAGES ring stages, the
+// activation operand (xq_bytes, a multiple of 128) and its scales, the
+// mbarriers.
+constexpr int ST1_STAGES = 3;
+static size_t st1_smem(int xq_bytes) {
+    return (size_t)ST1_STAGES * (ST_SLOT + ST_SC_SLOT) + (size_t)xq_bytes + (size_t)xq_bytes / 32 * 4 +
+           2 * ST_STAGES_MAX * 8 + 64;
+}
+
 int init_stream(vb_ctx *ctx) {
     VB_CHECK(ctx, cudaFuncSetAttribute(stream_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ST_SMEM_ALL));
+    VB_CHECK(ctx, cudaFuncSetAttribute(stream_gemv1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)st1_smem(ST_XBYTES)));
+    // all of the SM's unified memory as shared memory, so two CTAs fit (one of
+    // this launch and one of the next)
+    VB_CHECK(ctx, cudaFuncSetAttribute(stream_gemv1_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                       (int)cudaSharedmemCarveoutMaxShared));
+    return VB_OK;
+}
+
+int launch_stream1(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx, int64_t x_mod,
+                   const MatmulOut &out) {
+    if (M < 1 || M > ST_MMAX || (w->type != VB_TYPE_Q8_0 && w->type != VB_TYPE_F16)) return -1;
+    const int64_t K = w->K, N = w->N;
+    const int eb = w->type == VB_TYPE_Q8_0 ? 1 : 2;
+    if (K % 32 || K * eb > ST_SLOT || M * K * eb > ST_XBYTES || N < 1 || N > 0x7fffffff) return -1;
+    if (((uintptr_t)x & 15) || (ldx & 3)) return -1;   // 16-byte activation loads
+    StreamOp s{};
+    s.kind = OPK_GEMV;
+    s.pro = PRO_LOAD;
+    s.epi = out.res ? EPI_RESIDUAL : EPI_STORE;
+    s.res = out.res;
+    s.res_scale = out.res_scale;
+    s.qrule = ctx->qrule;
+    s.wtype = w->type;
+    s.K = (int)K;
+    s.N = (int)N;
+    s.M = (int)M;
+    s.w = (const uint8_t *)w->data;
+    s.sc = w->scales;
+    s.x = x;
+    s.ldx = ldx;
+    s.y = out.y;
+    s.ldy = out.ldy;
+    s.bias = out.bias;
+    s.flags = out.flags;
+    s.seg = (out.seg == M && out.seg_stride == 0 && out.seg_off == 0) ? 0 : out.seg;
+    s.seg_stride = out.seg_stride;
+    s.seg_off = out.seg_off;
+    s.x_mod = x_mod > 0 && x_mod < M ? x_mod : 0;
+    if (stream_gemv_geometry(ctx, s, 0)) {
+        ctx->last_error.clear();
+        return -1;
+    }
+    const int xq_bytes = (int)((M * K * eb + 127) & ~(int64_t)127);
+    const size_t smem = st1_smem(xq_bytes);
+    int per_sm = 0;
+    VB_CHECK(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stream_gemv1_kernel, ST_THREADS, smem));
+    if (per_sm < 1) return -1;
+    // CTAs: up to per_sm per SM, but no more than the op has ring chunks
+    const int64_t chunks = (N + s.rows_per_chunk - 1) / s.rows_per_chunk;
+    const int G = (int)std::min<int64_t>(chunks, (int64_t)ctx->sm_count * std::min(per_sm, 2));
+    int *err = gemm_error_word(ctx);
+    if (!err) return set_error(ctx, VB_ERR_OOM, "matmul: error word allocation failed");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(G);
+    cfg.blockDim = dim3(ST_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    VB_CHECK(ctx, cudaLaunchKernelEx(&cfg, stream_gemv1_kernel, s, err, ST1_STAGES, xq_bytes));
+    VB_LAUNCH_CHECK(ctx, "stream_gemv1");
     return VB_OK;
 }
 

@@ -14,21 +14,29 @@ namespace vb {
 // records a timeout: the launch argument of vb_set_wait_limit, per CTA.
 __shared__ long long s_dep_limit;
 
-// Epilogue of one output value.  Values written earlier in the same launch
+// Output / input row of logical row m (identity unless the op carries a
+// vb_matmul row mapping).
+__device__ __forceinline__ int64_t out_row(const StreamOp &op, int m) {
+    return op.seg > 0 ? (m / op.seg) * op.seg_stride + op.seg_off + m % op.seg : m;
+}
+__device__ __forceinline__ int64_t in_row(const StreamOp &op, int m) { return op.x_mod > 0 ? m % op.x_mod : m; }
+
+// Epilogue of one output value: bias, the bf16 flag, then the block residual
+// y = bf16(res + scale * value).  Values written earlier in the same launch
 // (the residual stream) are read through L2 (__ldcg), never through the
 // non-coherent per-SM L1.
 __device__ __forceinline__ float stream_epilogue(const StreamOp &op, int m, int64_t n, float v) {
     if (op.bias) v = __fadd_rn(v, op.bias[n]);
+    if (op.flags & VB_OUT_BF16) v = bf16r(v);
     if (op.epi == EPI_RESIDUAL) {
-        float a = bf16r(v);
-        if (op.res_scale != 1.0f) a = __fmul_rn(a, op.res_scale);
-        return bf16r(__fadd_rn(__ldcg(op.res + (int64_t)m * op.ldy + n), a));
+        if (op.res_scale != 1.0f) v = __fmul_rn(v, op.res_scale);
+        return bf16r(__fadd_rn(__ldcg(op.res + out_row(op, m) * op.ldy + n), v));
     }
-    return (op.flags & VB_OUT_BF16) ? bf16r(v) : v;
+    return v;
 }
 
 __device__ __forceinline__ void stream_store(const StreamOp &op, int m, int64_t n, float v) {
-    op.y[(int64_t)m * op.ldy + n] = stream_epilogue(op, m, n, v);
+    op.y[out_row(op, m) * op.ldy + n] = stream_epilogue(op, m, n, v);
 }
 
 // Slot row of logical row j in a chunk of nr rows.  An EPI_SWIGLU chunk
@@ -39,7 +47,7 @@ __device__ __forceinline__ int slot_row(int j, int nr, bool swz) {
 }
 
 __device__ __forceinline__ void swiglu_store(const StreamOp &op, int m, int64_t t, float g, float u) {
-    op.y[(int64_t)m * op.ldy + t] = bf16r(__fmul_rn(bf16r(silu_f(bf16r(g))), bf16r(u)));
+    op.y[out_row(op, m) * op.ldy + t] = bf16r(__fmul_rn(bf16r(silu_f(bf16r(g))), bf16r(u)));
 }
 
 // Bounded wait on an mbarrier phase; false on timeout or abort.
@@ -209,7 +217,7 @@ __device__ __forceinline__ bool q8_m1_op(const StreamOp &op, const uint8_t *wslo
         xr[i] = *reinterpret_cast<const int4 *>(xq + hb * 16);
         dxr[i] = xd[hb >> 1];
     }
-    float *y = op.y;
+    float *y = op.y + out_row(op, 0) * op.ldy;
     const float *bias = op.bias;
     const bool b16 = op.flags & VB_OUT_BF16;
     const bool residual = op.epi == EPI_RESIDUAL;
@@ -321,7 +329,7 @@ __device__ __noinline__ bool f16_m1_op(const StreamOp &op, const uint8_t *wslot,
     float xf[8 * IT];
 #pragma unroll
     for (int i = 0; i < IT; i++) widen8_f16(xh, ls + LPR * i, xf + 8 * i);
-    float *y = op.y;
+    float *y = op.y + out_row(op, 0) * op.ldy;
     const float *bias = op.bias;
     const bool b16 = op.flags & VB_OUT_BF16;
     const bool residual = op.epi == EPI_RESIDUAL;
@@ -459,7 +467,7 @@ __device__ __forceinline__ void stream_row_scales(const float *x, int64_t ldx, i
 
 // Eight consecutive prologue values of row m starting at column k0.
 __device__ __forceinline__ void stream_pro_values(const StreamOp &op, int m, int k0, const float *aux, float v[8]) {
-    const float *xr = op.x + (int64_t)m * op.ldx;
+    const float *xr = op.x + in_row(op, m) * op.ldx;
     if (op.pro == PRO_SWIGLU) {
         const int F = op.pro_len;
         const float4 g0 = __ldcg(reinterpret_cast<const float4 *>(xr + k0));
@@ -539,7 +547,7 @@ __device__ __forceinline__ void q8_prologue_batch(const StreamOp &op, int r0, bo
         a[r][0] = a[r][1] = b[r][0] = b[r][1] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (it < total) {
             const int m = it / ipr, k0 = (it - m * ipr) * 8;
-            const float *xr = op.x + (int64_t)m * op.ldx + k0;
+            const float *xr = op.x + in_row(op, m) * op.ldx + k0;
             a[r][0] = ldcg4(xr);
             a[r][1] = ldcg4(xr + 4);
             if (pro == PRO_SWIGLU) {

@@ -48,8 +48,12 @@ struct alignas(16) StreamOp {
     const float *pro_w;     // RMSNorm weight
     float eps;
     int pro_len;            // SWIGLU: ffn width F
-    const float *res;       // EPI_RESIDUAL source [M][ldy]
+    const float *res;       // EPI_RESIDUAL source [M][ldy] (rows mapped like y's)
     float res_scale;        // residual multiplier (1 = none)
+    // row mappings of a single mat-mul (vb_matmul): logical output row m goes
+    // to row (m / seg) * seg_stride + seg_off + m % seg (seg 0: row m); input
+    // row m is read from row m % x_mod (x_mod 0: row m)
+    int64_t seg, seg_stride, seg_off, x_mod;
     // decode attention (OPK_ATTN; y = merged output [M][n_heads*head_dim])
     const float *qkv;       // [M][ldqkv] bf16 values: q | k | v
     int64_t ldqkv;
