@@ -1,6 +1,7 @@
 """Tensor-core mat-mul (tcgen05, M >= 16 activation rows) against the CPU
-oracle: Q8_0 (exact block values split into fp16 hi/lo operands) and F16
-weights, tile edges (N not a multiple of 128, M not a multiple of 16), one
+oracle: Q8_0 (int8 MMAs with exact int32 block sums when K % 128 == 0;
+otherwise, or with VB_GEMM_I8=0, exact block values split into fp16 hi/lo
+operands) and F16 weights, tile edges (N not a multiple of 128, M not a multiple of 16), one
 and many k tiles, split-K, bias / bf16 epilogue, both activation rounding
 rules, and agreement with the weight-streaming GEMV path on the same call."""
 import os
@@ -89,21 +90,87 @@ def test_gemm_qrule_ref(ctx):
     w.release()
 
 
+def context_with(var, value):
+    """A context created with environment variable `var` set (read once at
+    creation)."""
+    old = os.environ.get(var)
+    os.environ[var] = value
+    try:
+        return vb.Context(0)
+    finally:
+        if old is None:
+            del os.environ[var]
+        else:
+            os.environ[var] = old
+
+
+@pytest.fixture(scope="module")
+def ctx_split():
+    """Q8_0 through the fp16 hi/lo split kernel instead of the int8 one."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    c = context_with("VB_GEMM_I8", "0")
+    yield c
+    c.close()
+
+
+@pytest.mark.parametrize("K,N,M", [(2048, 2048, 16), (2048, 6144, 256), (1024, 64, 200), (4096, 384, 600)])
+def test_gemm_q8_split_kernel_vs_oracle(ctx_split, K, N, M):
+    out, ref, _ = run_matmul(ctx_split, O.TYPE_Q8_0, K, N, M)
+    S.assert_matmul_close(out, ref, 1e-3)
+    assert S.rel_l2(out, ref) < 2e-5
+
+
+@pytest.fixture(scope="module")
+def ctx_i8():
+    """Q8_0 through the int8 kernel at every M (the default picks it only
+    where it is faster)."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    c = context_with("VB_GEMM_I8", "2")
+    yield c
+    c.close()
+
+
+@pytest.mark.parametrize("K,N,M", [(4096, 384, 600), (1024, 2048, 512), (2048, 6144, 1000), (128, 200, 97)])
+def test_gemm_int8_kernel_vs_oracle_at_large_m(ctx_i8, K, N, M):
+    out, ref, _ = run_matmul(ctx_i8, O.TYPE_Q8_0, K, N, M)
+    S.assert_matmul_close(out, ref, 1e-3)
+    assert S.rel_l2(out, ref) < 2e-5
+
+
+def test_gemm_int8_fused_epilogue(ctx_i8):
+    out, ref, b = run_matmul(ctx_i8, O.TYPE_Q8_0, 2048, 1024, 200, vb.OUT_BF16, with_bias=True)
+    S.assert_layer_close(out, O.bf16_round(ref + b), 1e-3)
+
+
+@pytest.mark.parametrize("K,N,M", [(1024, 1536, 256), (2048, 1024, 100), (6144, 1024, 48), (2048, 2048, 700)])
+def test_gemm_int8_and_split_kernels_agree(ctx_i8, ctx_split, K, N, M):
+    """The int8 kernel (exact int32 block sums) and the fp16 hi/lo split
+    kernel compute the same block products."""
+    W = S.weight(O.TYPE_Q8_0, N, K)
+    x = S.normal((M, K))
+    outs = []
+    for c in (ctx_i8, ctx_split):
+        w = c.weight(O.TYPE_Q8_0, K, N, W)
+        xd = dev(x)
+        y = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        c.matmul(w, xd, M, y)
+        c.sync()
+        assert c.device_status() == (0, 0)
+        outs.append(host(y))
+        w.release()
+    assert S.rel_l2(outs[0], outs[1]) < 2e-5
+
+
 def test_gemm_agrees_with_gemv_path(ctx):
     """Same call through a context with the tensor-core path switched off
     (VB_GEMM=0 at creation): both follow the same block arithmetic."""
     K, N, M = 2048, 768, 40
     W = S.weight(O.TYPE_Q8_0, N, K)
     x = S.normal((M, K))
-    old = os.environ.get("VB_GEMM")
-    os.environ["VB_GEMM"] = "0"
-    try:
-        c2 = vb.Context(0)
-    finally:
-        if old is None:
-            del os.environ["VB_GEMM"]
-        else:
-            os.environ["VB_GEMM"] = old
+    c2 = context_with("VB_GEMM", "0")
     outs = []
     for c in (ctx, c2):
         w = c.weight(O.TYPE_Q8_0, K, N, W)

@@ -169,6 +169,8 @@ extern "C" int vb_create(int device, vb_ctx **out) {
     {
         const char *g = getenv("VB_GEMM");
         c->use_gemm = !(g && g[0] == '0');
+        const char *gi = getenv("VB_GEMM_I8");
+        c->gemm_i8 = !gi ? 1 : gi[0] == '0' ? 0 : gi[0] == '2' ? 2 : 1;
     }
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
         delete c;

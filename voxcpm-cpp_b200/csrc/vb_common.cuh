@@ -62,6 +62,8 @@ struct vb_weight_s {
     size_t device_bytes = 0;
     alignas(64) unsigned char tmap[128];   // tensor-core path: TMA descriptor of the weight tiles
     bool tmap_ok = false;
+    alignas(64) unsigned char tmap_i8[128];   // int8 tensor-core path (Q8_0): 128 x 128 swizzled tiles
+    bool tmap_i8_ok = false;
 };
 
 // Host F32->BF16->F32 (round to nearest even, quiet NaN).
@@ -80,6 +82,8 @@ struct vb_ctx {
     int sm_count = 0;
     size_t smem_optin = 0;
     bool use_gemm = true;               // tensor-core path for M >= 16 (VB_GEMM=0 disables)
+    int gemm_i8 = 1;                    // Q8_0 on the int8 tensor cores: 1 where faster (the default),
+                                        // 2 always (VB_GEMM_I8=2), 0 never (VB_GEMM_I8=0: the fp16 split form)
     void *gemm = nullptr;               // tensor-core path state (vb_gemm.cu)
     void *attn_noalloc = nullptr;       // device address of vb_attention_noalloc's fixed scratch on this device
     long long dep_wait_limit = 0;       // streaming kernel: cycles of a wait on other CTAs (0 = default)

@@ -126,13 +126,17 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+// The load and its wait are one asm statement: the destination registers
+// are written asynchronously until tcgen05.wait::ld, and with two
+// statements the compiler may schedule a use of a register between them.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        "tcgen05.wait::ld.sync.aligned;"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        : "r"(taddr)
+        : "memory");
 }
 
 // Bounded mbarrier wait (no abort flag: every role of the CTA reaches the
@@ -163,6 +167,28 @@ __device__ __forceinline__ void gm_store16(const GemmArgs &a, int m0, int n, con
     const float b = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
     for (int cc = 0; cc < 16; cc++) {
+        if (m0 + cc >= a.M) break;
+        float v = acc[cc];
+        if (a.bias) v = __fadd_rn(v, b);
+        if (a.flags & VB_OUT_BF16) v = bf16r(v);
+        if (a.res) {
+            if (a.res_scale != 1.0f) v = __fmul_rn(v, a.res_scale);
+            v = bf16r(__fadd_rn(r[cc], v));
+        }
+        a.y[gm_out_row(a, m0 + cc) * a.ldy + n] = v;
+    }
+}
+
+// The same epilogue for 8 outputs (activation rows m0 .. m0+7).
+__device__ __forceinline__ void gm_store8(const GemmArgs &a, int m0, int n, const float *acc) {
+    float r[8];
+    if (a.res) {
+#pragma unroll
+        for (int cc = 0; cc < 8; cc++) r[cc] = __ldcg(a.res + gm_out_row(a, min(m0 + cc, a.M - 1)) * a.ldy + n);
+    }
+    const float b = a.bias ? a.bias[n] : 0.0f;
+#pragma unroll
+    for (int cc = 0; cc < 8; cc++) {
         if (m0 + cc >= a.M) break;
         float v = acc[cc];
         if (a.bias) v = __fadd_rn(v, b);
@@ -712,6 +738,442 @@ __global__ void __launch_bounds__(ACT_NORM_THREADS) gemm_act_norm_kernel(const f
     }
 }
 
+// ============================================================ int8 path
+// Q8_0 x Q8_0 on the integer tensor cores (tcgen05.mma kind::i8): the exact
+// semantics of ggml's block dot,
+//   y[m][n] = sum_b (d_w[n,b] * d_x[m,b]) * isum_b,  isum_b = sum_{j<32} qw qx,
+// with isum_b an exact int32 for every (weight row, activation row) pair.
+// The block scales differ per block, so integer sums cannot run across
+// blocks: one MMA (K = 32) per Q8_0 block writes isum_b into one of four
+// TMEM buffers, and the epilogue warps fold each buffer into fp32 registers
+// as acc = fma(float(isum_b), d_w * d_x, acc) in block order (the product of
+// two fp16 scales is exact in fp32).
+//
+// int32 -> fp32 without a conversion: every buffer is preset to the int32
+// 0x4B400000 (the bits of 1.5 * 2^23) and the MMA accumulates into it, so
+// a buffer word holds the bits of the fp32 1.5 * 2^23 + isum_b, exactly
+// (|isum_b| <= 32 * 127 * 128 < 2^22); subtracting 1.5 * 2^23 is exact too.
+// The epilogue reads a buffer, writes the preset back, and works on pairs
+// of columns with the packed fp32 operations (add, mul, fma: each rounds
+// as its scalar form does): 1.5 instructions per output and block.
+//
+// The weight's repacked int8 quants stream by TMA as they are; the
+// activation is quantized once per call (gemm_act_i8_kernel) into int8
+// rows and fp32 block scales stored transposed, [K/32][Mq], so a stage's
+// scales are one TMA box.
+//
+// Tile: 128 weight rows (MMA M, TMEM lanes) x BN = NG * CW activation rows
+// (MMA N, TMEM columns) x 128 k per stage (one 128-byte swizzle row = four
+// blocks).  Warp 0 issues TMA, warp 1 allocates TMEM and issues the MMAs,
+// warps 2 .. 4 * NG + 1 are the epilogue: warp w reads TMEM lanes
+// 32*(w%4).. and columns [CW * g, CW * (g+1)) with g = (w-2)/4.  A stage is
+// refilled once its MMAs have completed AND the epilogue has read its scales.
+constexpr int GI_BK = 128;
+// NG column groups of CW columns: BN = NG * CW, 4 * NG epilogue warps
+constexpr int gi_threads(int ng) { return 64 + 128 * ng; }
+constexpr int GI_DBUF = 4;
+constexpr int GI_MAX_STAGES = 6;
+constexpr uint32_t GI_MAGIC = 0x4B400000u;     // bits of 12582912.0f = 1.5 * 2^23
+
+// D += A * B (D holds the preset)
+__device__ __forceinline__ void umma_i8(uint32_t tmem, uint64_t a, uint64_t b, uint32_t idesc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.eq.b32 p, 0, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc)
+        : "memory");
+}
+
+// TMEM loads of CW columns of this warp's 32 lanes, with the wait in the
+// same statement (see tmem_ld16)
+template <int CW>
+__device__ __forceinline__ void tmem_ld_cw(uint32_t taddr, uint32_t (&r)[CW]);
+template <>
+__device__ __forceinline__ void tmem_ld_cw<8>(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        : "r"(taddr)
+        : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_ld_cw<16>(uint32_t taddr, uint32_t (&r)[16]) {
+    tmem_ld16(taddr, r);
+}
+// Presets CW columns of this warp's 32 lanes to GI_MAGIC and waits for the
+// stores.
+template <int CW>
+__device__ __forceinline__ void tmem_preset(uint32_t taddr) {
+    const uint32_t m = GI_MAGIC;
+    if constexpr (CW == 8) {
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};\n"
+            "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+            "r"(m)
+            : "memory");
+    } else {
+#pragma unroll
+        for (int c = 0; c < CW; c += 16)
+            asm volatile(
+                "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(
+                    taddr + (uint32_t)c),
+                "r"(m)
+                : "memory");
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    }
+}
+
+template <int CW, int NG>
+__global__ void __launch_bounds__(gi_threads(NG), 1)
+    gemm_i8_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                   const __grid_constant__ CUtensorMap tm_dx, const GemmArgs a) {
+    constexpr int BN = NG * CW;
+    constexpr int GI_EPI_WARPS = 4 * NG;
+    extern __shared__ uint8_t gsm_raw[];
+    uint8_t *gsm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~(uintptr_t)1023);
+    __shared__ uint64_t bars[2 * GI_MAX_STAGES + 2 * GI_DBUF];
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_last;
+    uint64_t *full = bars, *empty = bars + GI_MAX_STAGES, *dfull = bars + 2 * GI_MAX_STAGES, *dempty = dfull + GI_DBUF;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr uint32_t a_bytes = GM_BM * GI_BK;      // 16 KB of weight quants
+    constexpr uint32_t b_bytes = BN * GI_BK;         // activation quants
+    constexpr uint32_t s_bytes = 4u * BN * 4u;       // the four blocks' activation scales
+    constexpr uint32_t stage_bytes = a_bytes + b_bytes + ((s_bytes + 1023) & ~1023u);
+    const int n_tiles = a.tiles_n * a.tiles_m * a.splits;
+    const uint32_t pcols = a.tmem_cols / GI_DBUF;
+    const int nbk = a.K / QK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < GI_MAX_STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1 + GI_EPI_WARPS);
+        }
+        for (int d = 0; d < GI_DBUF; d++) {
+            mbar_init(&dfull[d], 1);
+            mbar_init(&dempty[d], GI_EPI_WARPS);
+        }
+        mbar_fence_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(a.tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+    const int q = warp & 3, cg = (warp - 2) >> 2, c0 = cg * CW;
+    if (warp >= 2) {
+        // the preset of every buffer, before the first MMA
+#pragma unroll 1
+        for (int d = 0; d < GI_DBUF; d++)
+            tmem_preset<CW>(tmem + (uint32_t)d * pcols + ((uint32_t)(q * 32) << 16) + (uint32_t)c0);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    pdl_wait();
+    pdl_trigger();
+
+    auto coords = [&](int t, int &n0, int &m0, int &split, int &kt0, int &nkt) {
+        split = t % a.splits;
+        t /= a.splits;
+        m0 = (t % a.tiles_m) * BN;
+        n0 = (t / a.tiles_m) * GM_BM;
+        kt0 = split * a.kt_per_split;
+        nkt = min(a.kt_per_split, a.kt_total - kt0);
+    };
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA
+        if (lane == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+                int n0, m0, split, kt0, nkt;
+                coords(t, n0, m0, split, kt0, nkt);
+                for (int i = 0; i < nkt; i++, it++) {
+                    const int s = it % a.n_tma;
+                    const uint32_t ph = (uint32_t)(it / a.n_tma) & 1u;
+                    if (!gm_wait(&empty[s], ph ^ 1u)) { atomicCAS(a.err, 0, 21); ok = false; break; }
+                    uint8_t *st = gsm + (size_t)s * stage_bytes;
+                    mbar_arrive_expect_tx(&full[s], a_bytes + b_bytes + s_bytes);
+                    const int kx = (kt0 + i) * GI_BK;
+                    tma_load_2d(st, &tm_w, kx, n0, &full[s]);
+                    tma_load_2d(st + a_bytes, &tm_x, kx, m0, &full[s]);
+                    tma_load_2d(st + a_bytes + b_bytes, &tm_dx, m0, kx / QK, &full[s]);
+                }
+            }
+            for (int s = 0; s < a.n_tma; s++) {
+                const int fills = it / a.n_tma + (it % a.n_tma > s ? 1 : 0);
+                if (fills) gm_wait(&full[s], (uint32_t)(fills - 1) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA
+        if (lane == 0) {
+            // D s32 (bits 4-5 = 2); A and B signed 8-bit (1) in bits 7-9 / 10-12;
+            // K-major both; N >> 3 at bit 17, M >> 4 at bit 24
+            const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                   ((uint32_t)(GM_BM >> 4) << 24);
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+                int n0, m0, split, kt0, nkt;
+                coords(t, n0, m0, split, kt0, nkt);
+                for (int i = 0; i < nkt && ok; i++, it++) {
+                    const int s = it % a.n_tma;
+                    const uint32_t ph = (uint32_t)(it / a.n_tma) & 1u;
+                    if (!gm_wait(&full[s], ph)) { atomicCAS(a.err, 0, 22); ok = false; break; }
+                    uint8_t *st = gsm + (size_t)s * stage_bytes;
+                    // block k of every stage goes to buffer k (four blocks per
+                    // stage), so the buffers turn over once per stage
+                    const uint32_t bph = (uint32_t)it & 1u;
+#pragma unroll
+                    for (int k = 0; k < GI_DBUF; k++) {
+                        if (!gm_wait(&dempty[k], bph ^ 1u)) { atomicCAS(a.err, 0, 23); ok = false; break; }
+                        tc_fence_after();
+                        umma_i8(tmem + (uint32_t)k * pcols, sw128_desc(st + 32 * k), sw128_desc(st + a_bytes + 32 * k),
+                                idesc);
+                        umma_commit(&dfull[k]);
+                    }
+                    umma_commit(&empty[s]);   // the stage's MMAs are done with its operands
+                }
+            }
+        }
+    } else {
+        // -------------------------------------------------------- epilogue
+        const int et = threadIdx.x - 64;
+        const float2 nmagic = make_float2(-12582912.0f, -12582912.0f);
+        int it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+            int n0, m0, split, kt0, nkt;
+            coords(tile, n0, m0, split, kt0, nkt);
+            const int r = q * 32 + lane, n = n0 + r;
+            const bool nv = n < a.N;
+            const uint2 *scp = reinterpret_cast<const uint2 *>(a.sc + (int64_t)(nv ? n : 0) * nbk) + kt0;
+            float2 acc[CW / 2];
+#pragma unroll
+            for (int c = 0; c < CW / 2; c++) acc[c] = make_float2(0.0f, 0.0f);
+            // the four weight scales of a stage: one 8-byte load (K % 128 == 0),
+            // fetched a stage ahead
+            uint2 dw_next = nv ? __ldg(scp) : make_uint2(0u, 0u);
+            for (int i = 0; i < nkt; i++, it++) {
+                const int s = it % a.n_tma;
+                const uint32_t ph = (uint32_t)(it / a.n_tma) & 1u;
+                const uint32_t bph = (uint32_t)it & 1u;   // the buffers turn over once per stage
+                const uint2 dw4 = dw_next;
+                if (i + 1 < nkt && nv) dw_next = __ldg(scp + i + 1);
+                const float2 dw01 = __half22float2(*reinterpret_cast<const __half2 *>(&dw4.x));
+                const float2 dw23 = __half22float2(*reinterpret_cast<const __half2 *>(&dw4.y));
+                if (ok && !gm_wait(&full[s], ph)) { atomicCAS(a.err, 0, 24); ok = false; }
+                const float4 *dx4 =
+                    reinterpret_cast<const float4 *>(gsm + (size_t)s * stage_bytes + a_bytes + b_bytes) + c0 / 4;
+#pragma unroll
+                for (int k = 0; k < GI_DBUF; k++) {
+                    if (ok && !gm_wait(&dfull[k], bph)) { atomicCAS(a.err, 0, 25); ok = false; }
+                    tc_fence_after();
+                    const float dw = k == 0 ? dw01.x : k == 1 ? dw01.y : k == 2 ? dw23.x : dw23.y;
+                    const float2 dw2 = make_float2(dw, dw);
+                    const uint32_t tb = tmem + (uint32_t)k * pcols + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
+                    // in loads of at most 16 columns (registers: 16 epilogue warps)
+                    constexpr int LC = CW < 16 ? CW : 16;
+#pragma unroll
+                    for (int c = 0; c < CW; c += LC) {
+                        uint32_t v[LC];
+                        tmem_ld_cw<LC>(tb + (uint32_t)c, v);
+                        if (c + LC == CW) {
+                            // the buffer is read: preset it and hand it back to the MMA
+                            tmem_preset<CW>(tb);
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&dempty[k]);
+                        }
+#pragma unroll
+                        for (int e = 0; e < LC / 4; e++) {
+                            const float4 dx = dx4[k * (BN / 4) + c / 4 + e];
+                            const int o = c / 2 + 2 * e;
+                            acc[o] = __ffma2_rn(
+                                __fadd2_rn(make_float2(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1])), nmagic),
+                                __fmul2_rn(dw2, make_float2(dx.x, dx.y)), acc[o]);
+                            acc[o + 1] = __ffma2_rn(
+                                __fadd2_rn(make_float2(__uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3])),
+                                           nmagic),
+                                __fmul2_rn(dw2, make_float2(dx.z, dx.w)), acc[o + 1]);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);   // this warp has read the stage's scales
+            }
+            // ---- output (or split partials) for row n, columns m0 + c0 ..
+            const bool split_k = a.splits > 1;
+            const float *accf = reinterpret_cast<const float *>(acc);
+            if (nv) {
+                if (split_k) {
+                    float4 *pw = reinterpret_cast<float4 *>(a.ws + ((int64_t)split * a.N + n) * a.Mp + m0 + c0);
+#pragma unroll
+                    for (int q4 = 0; q4 < CW / 4; q4++)
+                        pw[q4] = make_float4(accf[4 * q4], accf[4 * q4 + 1], accf[4 * q4 + 2], accf[4 * q4 + 3]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < CW; j += 8) gm_store8(a, m0 + c0 + j, n, accf + j);
+                }
+            }
+            if (split_k) {
+                // the last CTA of this tile adds the split partials in split order
+                asm volatile("bar.sync 2, %0;" ::"r"(32 * GI_EPI_WARPS) : "memory");
+                if (et == 0) {
+                    fence_acq_rel_gpu();
+                    const unsigned tid = (unsigned)(tile / a.splits);
+                    s_last = atomicAdd(a.cnt + tid, 1u) == (unsigned)(a.splits - 1);
+                    if (s_last) {
+                        fence_acq_rel_gpu();
+                        a.cnt[tid] = 0;
+                    }
+                }
+                asm volatile("bar.sync 2, %0;" ::"r"(32 * GI_EPI_WARPS) : "memory");
+                if (s_last && nv) {
+#pragma unroll 1
+                    for (int j = 0; j < CW; j += 8) {
+                        float4 sum[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+#pragma unroll 1
+                        for (int sp = 0; sp < a.splits; sp++) {
+                            const float4 *pr = reinterpret_cast<const float4 *>(
+                                a.ws + ((int64_t)sp * a.N + n) * a.Mp + m0 + c0 + j);
+#pragma unroll
+                            for (int q4 = 0; q4 < 2; q4++) {
+                                const float4 v = __ldcg(pr + q4);
+                                sum[q4].x = __fadd_rn(sum[q4].x, v.x);
+                                sum[q4].y = __fadd_rn(sum[q4].y, v.y);
+                                sum[q4].z = __fadd_rn(sum[q4].z, v.z);
+                                sum[q4].w = __fadd_rn(sum[q4].w, v.w);
+                            }
+                        }
+                        gm_store8(a, m0 + c0 + j, n, reinterpret_cast<const float *>(sum));
+                    }
+                }
+                asm volatile("bar.sync 2, %0;" ::"r"(32 * GI_EPI_WARPS) : "memory");
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols) : "memory");
+    }
+}
+
+// Q8_0 quantization of 8 activation values (ggml's rule, bit-exact; the four
+// threads of a 32-value block are consecutive lanes and all take part in the
+// shuffles) into the int8 operand row and the transposed scale table.
+__device__ __forceinline__ void act_emit8_i8(const float (&v)[8], bool valid, int m, int k0, int K, int Mp, int rule,
+                                             int8_t *qx, float *dxt) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) amax = fmaxf(amax, fabsf(v[j]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const uint16_t dh = f2h(d);
+    const bool x86 = rule == VB_QRULE_X86;
+    float id;
+    if (x86) id = (amax != 0.0f) ? __fdiv_rn(127.0f, amax) : 0.0f;
+    else id = (d != 0.0f) ? __fdiv_rn(1.0f, d) : 0.0f;
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float t = __fmul_rn(v[j], id);
+        const int qv = x86 ? __float2int_rn(t) : (int)roundf(t);
+        w[j >> 2] |= ((uint32_t)(qv & 0xff)) << (8 * (j & 3));
+    }
+    if (valid) {
+        *reinterpret_cast<uint2 *>(qx + (int64_t)m * K + k0) = make_uint2(w[0], w[1]);
+        if ((k0 & 31) == 0) dxt[(int64_t)(k0 >> 5) * Mp + m] = h2f(dh);
+    }
+}
+
+__global__ void gemm_act_i8_kernel(const float *x, int64_t ldx, int64_t x_mod, int M, int K, int Mp, int rule, int vec,
+                                   int swiglu_f, int8_t *qx, float *dxt) {
+    pdl_trigger();
+    pdl_wait();
+    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;   // item of 8 values
+    const int ipr = K >> 3;
+    const bool valid = e < (int64_t)M * ipr;
+    const int m = valid ? (int)(e / ipr) : 0, k0 = valid ? (int)(e - (int64_t)m * ipr) * 8 : 0;
+    const float *xr = x + (int64_t)(m % x_mod) * ldx + k0;
+    float v[8];
+    load8(xr, vec, v);
+    if (swiglu_f > 0) {
+        float u[8];
+        load8(xr + swiglu_f, vec, u);
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = bf16r(__fmul_rn(bf16r(silu_f(bf16r(v[j]))), bf16r(u[j])));
+    }
+    act_emit8_i8(v, valid, m, k0, K, Mp, rule, qx, dxt);
+}
+
+// The int8 operand of a mat-mul that follows vcpm_rms_norm (the statistic
+// and rounding of gemm_act_norm_kernel).
+__global__ void __launch_bounds__(ACT_NORM_THREADS) gemm_act_i8_norm_kernel(const float *x, int64_t ldx, int64_t x_mod,
+                                                                             int K, int Mp, int rule, int vec,
+                                                                             const float *__restrict__ nw, float eps,
+                                                                             int8_t *qx, float *dxt) {
+    pdl_trigger();
+    pdl_wait();
+    const int m = blockIdx.x;
+    const float *xr = x + (int64_t)(m % x_mod) * ldx;
+    const int ipr = K >> 3;
+    float v[ACT_NORM_ITEMS][8];
+    double s = 0.0;
+#pragma unroll
+    for (int it = 0; it < ACT_NORM_ITEMS; it++) {
+        const int item = it * ACT_NORM_THREADS + threadIdx.x;
+        if (item < ipr) {
+            load8(xr + item * 8, vec, v[it]);
+#pragma unroll
+            for (int j = 0; j < 8; j++) s += (double)__fmul_rn(v[it][j], v[it][j]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[it][j] = 0.0f;
+        }
+    }
+    __shared__ double red[ACT_NORM_THREADS / 32];
+    __shared__ float s_scale;
+    s = warp_sum_d(s);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        double t = threadIdx.x < ACT_NORM_THREADS / 32 ? red[threadIdx.x] : 0.0;
+        t = warp_sum_d(t);
+        if (threadIdx.x == 0) {
+            const float mean = __double2float_rn(__ddiv_rn(t, (double)K));
+            s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+        }
+    }
+    __syncthreads();
+    const float scale = s_scale;
+#pragma unroll
+    for (int it = 0; it < ACT_NORM_ITEMS; it++) {
+        const int item = it * ACT_NORM_THREADS + threadIdx.x;
+        if (it * ACT_NORM_THREADS >= ipr) break;     // uniform over the CTA
+        const bool valid = item < ipr;
+        float y[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const float wv = valid ? __ldg(nw + item * 8 + j) : 0.0f;
+            y[j] = bf16r(__fmul_rn(bf16r(__fmul_rn(v[it][j], scale)), wv));
+        }
+        act_emit8_i8(y, valid, m, valid ? item * 8 : 0, K, Mp, rule, qx, dxt);
+    }
+}
+
 // ------------------------------------------------------------------ host
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -748,7 +1210,7 @@ static bool make_map(CUtensorMap *m, const void *base, CUtensorMapDataType dt, i
 struct ActMaps {                // TMA descriptors of one activation buffer shape
     const void *bh = nullptr, *bl = nullptr;
     int K = 0, M = 0, BN = 0;
-    bool tf32 = false;
+    bool tf32 = false, i8 = false;
     CUtensorMap th, tl;
 };
 
@@ -795,6 +1257,12 @@ int init_gemm(vb_ctx *ctx) {
                                        GM_SMEM_BUDGET + 1024));
     VB_CHECK(ctx, cudaFuncSetAttribute(gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        GM_SMEM_BUDGET + 1024));
+    VB_CHECK(ctx, cudaFuncSetAttribute(gemm_i8_kernel<8, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       GM_SMEM_BUDGET + 1024));
+    VB_CHECK(ctx, cudaFuncSetAttribute(gemm_i8_kernel<16, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       GM_SMEM_BUDGET + 1024));
+    VB_CHECK(ctx, cudaFuncSetAttribute(gemm_i8_kernel<32, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       GM_SMEM_BUDGET + 1024));
     // the mat-mul kernels' counters and error word exist from creation on, so
     // no later call allocates them (and every call can be captured)
     if (!gemm_state(ctx)) return set_error(ctx, VB_ERR_OOM, "mat-mul state allocation failed");
@@ -819,6 +1287,152 @@ static cudaError_t pdl_launch(vb_ctx *ctx, void (*kernel)(KArgs...), dim3 grid, 
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Q8_0 weights on the int8 tensor cores (gemm_i8_kernel); K % 128 == 0.
+static int launch_gemm_i8(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx, int64_t x_mod,
+                          const MatmulOut &out, const GemmPro *pro) {
+    GemmState *gs = gemm_state(ctx);
+    if (!gs) return set_error(ctx, VB_ERR_OOM, "gemm: state allocation failed");
+    const int K = (int)w->K, N = (int)w->N;
+    const int tiles_n = (N + GM_BM - 1) / GM_BM;
+    const int mr = (int)((M + 15) / 16 * 16);
+    const int kt_total = K / GI_BK;
+    // Tile width and K split: the epilogue (four fp32 operations per output
+    // and Q8_0 block) sets a unit's time, ~ BN x k-stages + a fixed
+    // per-unit cost, over waves of the persistent grid, plus the split
+    // reduction (the last CTA of a tile reads every split's partials).
+    int BN = 0, splits = 1;
+    double best = 1e300;
+    // (BN = 96: three column groups of 32, twelve epilogue warps -- with 4
+    // groups of 32 the register budget of 16 epilogue warps spills)
+    for (int cand : {96, 64, 32}) {
+        if (cand > 32 && cand > mr && (cand == 96 ? 64 : cand >> 1) >= mr) continue;
+        const int64_t tiles = (int64_t)tiles_n * ((M + cand - 1) / cand);
+        for (int sp = 1; sp <= std::max(1, kt_total / 2); sp++) {
+            const int kps = (kt_total + sp - 1) / sp;
+            const int64_t units = tiles * ((kt_total + kps - 1) / kps);
+            const int64_t waves = (units + ctx->sm_count - 1) / ctx->sm_count;
+            const double t = (double)waves * ((double)cand * kps + 256.0) + (sp > 1 ? 8.0 * sp * cand : 0.0);
+            if (t < best * 0.999) { best = t; BN = cand; splits = sp; }
+            if (units >= 4 * ctx->sm_count) break;
+        }
+    }
+    if (BN == 0) {
+        BN = 64;
+        splits = 1;
+    }
+    const int tiles_m = (int)((M + BN - 1) / BN);
+    const int tiles = tiles_m * tiles_n;
+    const int kt_per_split = (kt_total + splits - 1) / splits;
+    splits = (kt_total + kt_per_split - 1) / kt_per_split;
+    if (tiles > 65536) return set_error(ctx, VB_ERR_INVALID_ARG, "gemm: too many tiles");
+
+    const size_t stage = (size_t)GM_BM * GI_BK + (size_t)BN * GI_BK + (((size_t)16 * BN + 1023) & ~(size_t)1023);
+    const int n_tma = (int)std::min<size_t>(GI_MAX_STAGES, GM_SMEM_BUDGET / stage);
+    if (n_tma < 2) return set_error(ctx, VB_ERR_INVALID_ARG, "gemm: tile does not fit shared memory");
+    const size_t smem = (size_t)n_tma * stage + 1024;
+    uint32_t pcols = 32;
+    while (pcols < (uint32_t)BN) pcols <<= 1;
+    const uint32_t cols = GI_DBUF * pcols;
+
+    // activation operand: int8 rows [M][K] and block scales [K/32][Mq]
+    const int Mq = (int)((M + 3) / 4 * 4);
+    const size_t qb = ((size_t)M * K + 1023) & ~(size_t)1023;
+    int rc = arena_reserve(ctx, gs->act, qb + (size_t)(K / QK) * Mq * 4 + 512);
+    if (rc) return rc;
+    int8_t *qx = (int8_t *)gs->act.ptr;
+    float *dxt = (float *)((uint8_t *)gs->act.ptr + qb);
+    {
+        const int64_t items = M * (K / 8);
+        const int64_t lx = ldx ? ldx : (pro && pro->swiglu_f ? 2 * (int64_t)K : K);
+        const int vec = ((uintptr_t)x % 16 == 0) && (lx % 4 == 0);
+        const int64_t xm = x_mod > 0 ? x_mod : M;
+        if (pro && pro->norm_w) {
+            if (K > 8 * ACT_NORM_THREADS * ACT_NORM_ITEMS)
+                return set_error(ctx, VB_ERR_INVALID_ARG, "gemm: fused RMSNorm row of %d values is too wide", K);
+            VB_CHECK(ctx, pdl_launch(ctx, gemm_act_i8_norm_kernel, dim3((unsigned)M), dim3(ACT_NORM_THREADS), 0, x, lx,
+                                     xm, K, Mq, ctx->qrule, vec, pro->norm_w, pro->eps, qx, dxt));
+        } else {
+            VB_CHECK(ctx, pdl_launch(ctx, gemm_act_i8_kernel, dim3((unsigned)((items + 255) / 256)), dim3(256), 0, x,
+                                     lx, xm, (int)M, K, Mq, ctx->qrule, vec, pro ? pro->swiglu_f : 0, qx, dxt));
+        }
+        VB_LAUNCH_CHECK(ctx, "gemm_act_i8");
+    }
+    if (!w->tmap_i8_ok) {
+        CUtensorMap *tw = reinterpret_cast<CUtensorMap *>(w->tmap_i8);
+        w->tmap_i8_ok = make_map(tw, w->data, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, GI_BK, GM_BM, true);
+        if (!w->tmap_i8_ok) return set_error(ctx, VB_ERR_BACKEND, "gemm: weight tensor map encoding failed");
+    }
+    // activation descriptors per (buffer, shape): th over the quants, tl over the scales
+    ActMaps *am = nullptr;
+    for (ActMaps &c : gs->cache)
+        if (c.bh == qx && c.bl == dxt && c.K == K && c.M == (int)M && c.BN == BN && c.i8) am = &c;
+    if (!am) {
+        am = &gs->cache[gs->next];
+        gs->next = (gs->next + 1) % 8;
+        am->bh = nullptr;
+        if (!make_map(&am->th, qx, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, GI_BK, BN, true) ||
+            !make_map(&am->tl, dxt, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Mq, K / QK, BN, GI_BK / QK, false))
+            return set_error(ctx, VB_ERR_BACKEND, "gemm: activation tensor map encoding failed");
+        am->bh = qx;
+        am->bl = dxt;
+        am->K = K;
+        am->M = (int)M;
+        am->BN = BN;
+        am->tf32 = false;
+        am->i8 = true;
+    }
+
+    GemmArgs g{};
+    g.q8 = 1;
+    g.bk = GI_BK;
+    g.K = K;
+    g.N = N;
+    g.M = (int)M;
+    g.BN = BN;
+    g.kt_total = kt_total;
+    g.kt_per_split = kt_per_split;
+    g.splits = splits;
+    g.tiles_m = tiles_m;
+    g.tiles_n = tiles_n;
+    g.n_tma = n_tma;
+    g.tmem_cols = cols;
+    g.sc = w->scales;
+    g.y = out.y;
+    g.bias = out.bias;
+    g.flags = out.flags;
+    g.res = out.res;
+    g.res_scale = out.res_scale;
+    g.ldy = out.ldy ? out.ldy : N;
+    g.seg = out.seg ? out.seg : M;
+    g.seg_stride = out.seg ? out.seg_stride : 0;
+    g.seg_off = out.seg ? out.seg_off : 0;
+    g.seg_plain = g.seg >= M && g.seg_off == 0;
+    g.cnt = gs->cnt;
+    g.err = gs->err;
+    if (splits > 1) {
+        g.Mp = tiles_m * BN;
+        rc = arena_reserve(ctx, gs->part, (size_t)splits * N * g.Mp * 4);
+        if (rc) return rc;
+        g.ws = (float *)gs->part.ptr;
+    }
+    const int n_work = tiles * splits;
+    const CUtensorMap &twm = *reinterpret_cast<const CUtensorMap *>(w->tmap_i8);
+    void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmArgs) =
+        BN == 96 ? gemm_i8_kernel<32, 3> : BN == 64 ? gemm_i8_kernel<16, 4> : gemm_i8_kernel<8, 4>;
+    const int threads = gi_threads(BN == 96 ? 3 : 4);
+    VB_CHECK(ctx, pdl_launch(ctx, kern, dim3((unsigned)std::min(n_work, ctx->sm_count)), dim3(threads), smem, twm,
+                             am->th, am->tl, g));
+    VB_LAUNCH_CHECK(ctx, "gemm_i8");
+    return VB_OK;
+}
+
+// Where the int8 kernel beats the fp16 split kernel (B200 sweep of the
+// MiniCPM4 projection shapes, M = 64 .. 4096): its epilogue work grows with
+// M x N x K/32 while the split kernel's fixed per-call cost falls away.
+static bool gemm_i8_faster(int64_t M, int64_t K, int64_t N) {
+    return M <= 256 || (M <= 512 && N <= 2560) || (M <= 768 && K >= 3 * N);
+}
+
 bool gemm_supported(vb_weight w, int64_t M) {
     if (M < 16 || !encode_fn()) return false;
     if (w->type == VB_TYPE_Q8_0) return w->K % GM_BK == 0;
@@ -828,6 +1442,9 @@ bool gemm_supported(vb_weight w, int64_t M) {
 
 int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx, int64_t x_mod,
                 const MatmulOut &out, const GemmPro *pro) {
+    if (w->type == VB_TYPE_Q8_0 && w->K % GI_BK == 0 &&
+        (ctx->gemm_i8 == 2 || (ctx->gemm_i8 == 1 && gemm_i8_faster(M, w->K, w->N))))
+        return launch_gemm_i8(ctx, w, x, M, ldx, x_mod, out, pro);
     GemmState *gs = gemm_state(ctx);
     if (!gs) return set_error(ctx, VB_ERR_OOM, "gemm: state allocation failed");
     const bool q8 = w->type == VB_TYPE_Q8_0;
@@ -930,7 +1547,7 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
     const void *blp = q8 ? (const void *)bl : (const void *)bh;
     ActMaps *am = nullptr;
     for (ActMaps &c : gs->cache)
-        if (c.bh == bh && c.bl == blp && c.K == K && c.M == (int)M && c.BN == BN && !c.tf32) am = &c;
+        if (c.bh == bh && c.bl == blp && c.K == K && c.M == (int)M && c.BN == BN && !c.tf32 && !c.i8) am = &c;
     if (!am) {
         am = &gs->cache[gs->next];
         gs->next = (gs->next + 1) % 8;
@@ -944,6 +1561,7 @@ int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx
         am->M = (int)M;
         am->BN = BN;
         am->tf32 = false;
+        am->i8 = false;
     }
 
     GemmArgs g{};
@@ -1045,7 +1663,7 @@ int launch_gemm_tf32(vb_ctx *ctx, Tf32Weight &w, const float *a_hi, const float 
     }
     ActMaps *am = nullptr;
     for (ActMaps &c : gs->cache)
-        if (c.bh == a_hi && c.bl == a_lo && c.K == K && c.M == (int)M && c.BN == BN && c.tf32) am = &c;
+        if (c.bh == a_hi && c.bl == a_lo && c.K == K && c.M == (int)M && c.BN == BN && c.tf32 && !c.i8) am = &c;
     if (!am) {
         am = &gs->cache[gs->next];
         gs->next = (gs->next + 1) % 8;
@@ -1059,6 +1677,7 @@ int launch_gemm_tf32(vb_ctx *ctx, Tf32Weight &w, const float *a_hi, const float 
         am->M = (int)M;
         am->BN = BN;
         am->tf32 = true;
+        am->i8 = false;
     }
     GemmArgs g{};
     g.bk = BK;
