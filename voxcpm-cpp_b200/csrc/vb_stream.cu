@@ -52,6 +52,12 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     __shared__ uint16_t s_idx[ST_MAX_OPS];     // program index of this CTA's k-th op
     __shared__ float s_part[2 * ST_CONSUMER_WARPS];   // row-segment partials of f16_m1_split_op
 
+    // residual rows of the current M = 1 op, fetched ahead (in the aux
+    // scratch, past what the prologues use; programs without aux skip it)
+    uint32_t dyn_smem;
+    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_smem));
+    float *s_res = dyn_smem >= st_smem(ns, true) ? reinterpret_cast<float *>(aux + ST_RES_OFF) : nullptr;
+
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, cta = blockIdx.x;
     if (threadIdx.x == 0) {
@@ -176,6 +182,15 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             const int64_t r0 = s_rows[k].x, r1 = s_rows[k].y;
             // The previous op ended with a consumer barrier, so no warp still
             // reads the activation buffers when they are rewritten here.
+            // The residual rows of an M = 1 Q8_0 op are fetched while the
+            // prologue runs, so the epilogue does not wait on global memory.
+            const float *sres = nullptr;
+            if (s_res && op.epi == EPI_RESIDUAL && op.wtype == VB_TYPE_Q8_0 && M == 1 && r1 > r0 &&
+                r1 - r0 <= ST_RES_ROWS) {
+                const float *rs = op.res + out_row(op, 0) * op.ldy + r0;
+                for (int t = ctid; t < (int)(r1 - r0); t += ST_CONSUMERS) cp_async4(&s_res[t], rs + t);
+                sres = s_res;
+            }
             if (r1 > r0) {
                 if (!(op.reuse_prev && last == i - 1))
                     stream_prologue(op, xq, xd, reinterpret_cast<float *>(aux), ctid, cw, lane);
@@ -183,17 +198,21 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
             } else {
                 last = -1;
             }
+            if (sres) {
+                cp_async_wait_all();
+                consumer_sync(ST_CONSUMERS);
+            }
 
             bool fast_done = false;
             if (op.wtype == VB_TYPE_Q8_0 && M == 1) {
                 bool ok = true;
                 fast_done = true;
                 switch (K) {
-                    case 1024: ok = q8_m1_op<16, 4>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns); break;
-                    case 2048: ok = q8_m1_op<16, 8>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns); break;
-                    case 4096: ok = q8_m1_op<16, 16>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns); break;
-                    case 6144: ok = q8_m1_op<32, 12>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns); break;
-                    case 8192: ok = q8_m1_op<32, 16>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns); break;
+                    case 1024: ok = q8_m1_op<16, 4>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns, sres); break;
+                    case 2048: ok = q8_m1_op<16, 8>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns, sres); break;
+                    case 4096: ok = q8_m1_op<16, 16>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns, sres); break;
+                    case 6144: ok = q8_m1_op<32, 12>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns, sres); break;
+                    case 8192: ok = q8_m1_op<32, 16>(op, wslot, sslot, xq, xd, full, empty, slot, phase, r0, r1, cw, lane, &s_abort, err, ns, sres); break;
                     default: fast_done = false; break;
                 }
                 if (!ok) bad = true;

@@ -35,6 +35,14 @@ __device__ __forceinline__ float stream_epilogue(const StreamOp &op, int m, int6
     return v;
 }
 
+// The same epilogue with the residual value already at hand.
+__device__ __forceinline__ float stream_epilogue_res(const StreamOp &op, int64_t n, float v, float res) {
+    if (op.bias) v = __fadd_rn(v, op.bias[n]);
+    if (op.flags & VB_OUT_BF16) v = bf16r(v);
+    if (op.res_scale != 1.0f) v = __fmul_rn(v, op.res_scale);
+    return bf16r(__fadd_rn(res, v));
+}
+
 __device__ __forceinline__ void stream_store(const StreamOp &op, int m, int64_t n, float v) {
     op.y[out_row(op, m) * op.ldy + n] = stream_epilogue(op, m, n, v);
 }
@@ -199,12 +207,13 @@ __device__ __forceinline__ void f16_chunk(const StreamOp &op, const uint8_t *__r
 // slice of the quantized activation (IT half-blocks) and its scales stay in
 // registers for the whole op, so shared memory carries only the weights.
 // Each half-block contributes float(isum_16) * (d_w * d_x); a row is reduced
-// over its LPR lanes.  Returns false on a timeout or an abort.
+// over its LPR lanes.  sres (optional) holds the residual rows r0 .. r1 of an
+// EPI_RESIDUAL op, fetched ahead.  Returns false on a timeout or an abort.
 template <int LPR, int IT>
 __device__ __forceinline__ bool q8_m1_op(const StreamOp &op, const uint8_t *wslot, const uint8_t *sslot,
                                          const int8_t *xq, const float *xd, uint64_t *full, uint64_t *empty,
                                          int &slot, uint32_t &phase, int64_t r0, int64_t r1, int cw, int lane,
-                                         volatile int *abort_flag, int *err, int ns) {
+                                         volatile int *abort_flag, int *err, int ns, const float *sres = nullptr) {
     constexpr int RPW = 32 / LPR;                       // rows per warp per pass
     constexpr int RPP = RPW * ST_CONSUMER_WARPS;        // rows per pass of all warps
     const int K = op.K, nb = K >> 5;
@@ -257,7 +266,7 @@ __device__ __forceinline__ bool q8_m1_op(const StreamOp &op, const uint8_t *wslo
             } else if (valid && ls == 0) {
                 const int64_t n = r + j;
                 if (residual) {
-                    y[n] = stream_epilogue(op, 0, n, acc);
+                    y[n] = sres ? stream_epilogue_res(op, n, acc, sres[n - r0]) : stream_epilogue(op, 0, n, acc);
                 } else {
                     float v = acc;
                     if (bias) v = __fadd_rn(v, bias[n]);
@@ -441,6 +450,20 @@ __device__ __noinline__ bool f16_m1_split_op(const StreamOp &op, const uint8_t *
 namespace vb {
 
 
+__device__ __forceinline__ float4 ldcg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
+
+// Decode attention geometry (see stream_attn): rows per pass, and the
+// spans per (sequence, head) and passes per span for L visible rows.
+constexpr int ATT_PASS = 64;
+
+__device__ __forceinline__ void attn_split(int L, int M, int NH, int G, int &nsp, int &ppi) {
+    const int passes = (L + ATT_PASS - 1) / ATT_PASS;
+    const int cap = max(1, G / (M * NH));
+    ppi = (passes + cap - 1) / cap;
+    nsp = (passes + ppi - 1) / ppi;
+}
+
+
 // Row scales 1/sqrtf(mean(x^2)+eps) of M rows (the ggml_rms_norm statistic:
 // fp32 squares summed in double), left in aux[0..M).  All consumer threads.
 __device__ __forceinline__ void stream_row_scales(const float *x, int64_t ldx, int M, int K, float eps, float *aux,
@@ -527,7 +550,6 @@ __device__ __forceinline__ void q8_store8(const float v[8], bool valid, int qrul
     }
 }
 
-__device__ __forceinline__ float4 ldcg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
 
 // R rounds (items r0*256 + ctid, (r0+1)*256 + ctid, ...) of the Q8_0
 // prologue with every global load issued before any arithmetic, so a round
@@ -668,213 +690,276 @@ __device__ __forceinline__ void rope_pair(float x0, float x1, const float *cs, i
 // Decode attention inside the persistent kernel (vcpm_attention for one new
 // token per sequence, src/minicpm4.c:250-428): for query head h of KV group
 // g = h / (n_heads / n_kv), s_l = (q . k_l) / sqrt(head_dim) and
-// o = softmax(s) . V over the sequence's visible rows.  Work items
-// (sequence, head, 32-row chunk) are dealt round-robin over the CTAs, so a
-// short step still spreads over many SMs.  An item rotates its query head
-// (RoPE table at the sequence's position) and copies the chunk's bf16 K/V
-// rows to shared memory asynchronously; the new token's row comes from this
-// step's k/v (rotated, bf16) and the group's first head appends it to the
-// cache.  Scores: a warp per row (lanes split the dimensions); softmax: one
-// row per lane, computed redundantly by every warp; values: a thread per
-// (V word, row subset), summed over the subsets in shared memory.  The item
-// writes (max, sum) and its partial output; the item that finishes a
-// (sequence, head) last (a device-wide count, no waiting) merges the chunks
-// into y.  op.eps carries the score scale 1/sqrt(head_dim); st holds the
-// step's [M][4] row parameters (shared memory).  head_dim % 64 == 0.
-__device__ __noinline__ void stream_attn(const StreamOp &op, const int *st, uint8_t *aux, int cta, int G, int ctid,
-                                         int cw, int lane) {
+// o = softmax(s) . V over the sequence's visible rows.
+//
+// Work items are (sequence, head, row span); the spans are as long as it
+// takes for every item to fit in one wave of the grid (attn_split), so no
+// CTA runs two items.  An item walks its span in passes of ATT_PASS rows
+// with an online softmax (running max and sum, the partial output rescaled
+// when the max grows).  A pass loads its K and V words straight into
+// registers -- K as four threads per row (a quarter of the dimensions
+// each), V as four consecutive words per thread over a subset of the rows
+// -- all issued before any arithmetic, so a pass costs one memory latency.
+// The new token's row comes from this step's k/v (rotated, bf16), and the
+// group's first head appends it to the cache.  A head with one span writes
+// its output directly; otherwise each item writes its (max, sum) and
+// partial output, and the item that finishes a (sequence, head) last (a
+// device-wide count, no waiting) merges the spans into y.  op.eps carries
+// the score scale 1/sqrt(head_dim); st holds the step's [M][4] row
+// parameters (shared memory).  head_dim is 64, 128 or 256.
+template <int HW>
+__device__ __forceinline__ void stream_attn_hw(const StreamOp &op, const int *st, uint8_t *aux, int cta, int G,
+                                               int ctid, int cw, int lane) {
     __shared__ int s_last;
     __shared__ float s_l;
-    const int HD = op.head_dim, HW = HD >> 1, HALF = HD >> 1, rw = HW + 1;
+    constexpr int HD = 2 * HW, HALF = HW;
+    constexpr int KW = HW / 4;                  // K words per thread (four threads per row)
+    constexpr int VG = HW / 4;                  // V word groups of 4
+    constexpr int VR = ST_CONSUMERS / VG;       // V row subsets
+    constexpr int VJ = ATT_PASS / VR;           // V rows per thread
+    static_assert(ST_CONSUMERS == 4 * ATT_PASS, "one K quarter-row per thread");
     const int NH = op.n_heads, qpk = NH / op.n_kv;
     const int QD = NH * HD, KD = op.n_kv * HD;
-    const int Q = ST_CONSUMERS / HW;                       // row subsets of the value pass
-    uint32_t *ks = reinterpret_cast<uint32_t *>(aux);     // [32][rw]
-    uint32_t *vs = ks + ST_ATT_ROWS * rw;                  // [32][rw]
-    float *qs = reinterpret_cast<float *>(vs + ST_ATT_ROWS * rw);   // [HD]
-    float *scs = qs + HD;                                   // [32] scores
-    float2 *vred = reinterpret_cast<float2 *>(scs + ST_ATT_ROWS);  // [Q][HW]
+    float *qs = reinterpret_cast<float *>(aux);                     // [HD] rotated query
+    uint32_t *fk = reinterpret_cast<uint32_t *>(qs + HD);          // [HW] new row, K words
+    uint32_t *fv = fk + HW;                                         // [HW] new row, V words
+    float *scs = reinterpret_cast<float *>(fv + HW);                // [ATT_PASS] scores
+    float2 *vred = reinterpret_cast<float2 *>(scs + ATT_PASS);     // [warps][HW] partial outputs
     const uint32_t *kc32 = reinterpret_cast<const uint32_t *>(op.kc);
     const uint32_t *vc32 = reinterpret_cast<const uint32_t *>(op.vc);
+    // thread roles: K row kr, quarter kq; V word group vg, row subset vq
+    const int kr = ctid >> 2, kq = ctid & 3;
+    const int vg = ctid % VG, vq = ctid / VG;
     int base = 0;   // first item index of sequence m
     for (int m = 0; m < op.M; m++) {
         const int rope_pos = st[4 * m], wrow = st[4 * m + 1], rstart = st[4 * m + 2], L = st[4 * m + 3];
-        const int nch = (L + ST_ATT_ROWS - 1) / ST_ATT_ROWS;
+        int nsp, ppi;
+        attn_split(L, op.M, NH, G, nsp, ppi);
         const float *qrow = op.qkv + (int64_t)m * op.ldqkv;
         const float *cs = op.rope_cs + (int64_t)rope_pos * HD;
         const int fresh = wrow - rstart;
-        const int items = NH * nch;
-        // this CTA's items: global index cta, cta + G, ... (CTA-uniform)
+        const int items = NH * nsp;
         for (int idx = base + (cta - base % G + G) % G; idx < base + items; idx += G) {
-            const int h = (idx - base) / nch, c = (idx - base) - h * nch, g = h / qpk;
-            {
-                consumer_sync(ST_CONSUMERS);             // previous item's readers are done
-                for (int p = ctid; p < HALF; p += ST_CONSUMERS) {
-                    const float x0 = __ldcg(qrow + h * HD + p), x1 = __ldcg(qrow + h * HD + p + HALF);
-                    float r0 = x0, r1 = x1;
-                    if (op.use_rope) rope_pair(x0, x1, cs, p, r0, r1);
-                    qs[p] = r0;
-                    qs[p + HALF] = r1;
+            const int h = (idx - base) / nsp, sp = (idx - base) - h * nsp, g = h / qpk;
+            const int row0 = sp * ppi * ATT_PASS, row1 = min(L, row0 + ppi * ATT_PASS);
+            const uint32_t *kg32 = kc32 + ((int64_t)g * op.n_rows + rstart) * HW;
+            const uint32_t *vg32 = vc32 + ((int64_t)g * op.n_rows + rstart) * HW;
+            consumer_sync(ST_CONSUMERS);   // the previous item's readers of qs / fk / vred are done
+            float mrun = -INFINITY, lrun = 0.0f;
+            float ox[4] = {0.f, 0.f, 0.f, 0.f}, oy[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int p0 = row0; p0 < row1; p0 += ATT_PASS) {
+                const int n = min(ATT_PASS, row1 - p0);
+                // ---- loads of the pass (cache rows; the new row is patched below)
+                uint4 kw[KW / 4];
+                uint4 vw[VJ];
+#pragma unroll
+                for (int t = 0; t < KW / 4; t++) {
+                    kw[t] = make_uint4(0u, 0u, 0u, 0u);
+                    if (kr < n)
+                        kw[t] = __ldcg(reinterpret_cast<const uint4 *>(kg32 + (int64_t)(p0 + kr) * HW + kq * KW) + t);
                 }
-                const int p0 = c * ST_ATT_ROWS;
-                const int n = min(ST_ATT_ROWS, L - p0);
-                const int64_t base = ((int64_t)g * op.n_rows + rstart + p0) * HW;
-                for (int i = ctid; i < n * HW; i += ST_CONSUMERS) {
-                    const int r = i / HW, w = i - r * HW;
-                    if (p0 + r == fresh) continue;
-                    cp_async4(ks + r * rw + w, kc32 + base + i);
-                    cp_async4(vs + r * rw + w, vc32 + base + i);
+#pragma unroll
+                for (int j = 0; j < VJ; j++) {
+                    const int r = vq + j * VR;
+                    vw[j] = make_uint4(0u, 0u, 0u, 0u);
+                    if (r < n) vw[j] = __ldcg(reinterpret_cast<const uint4 *>(vg32 + (int64_t)(p0 + r) * HW) + vg);
+                }
+                if (p0 == row0) {
+                    // rotated query, and the new row if it is in this span
+                    for (int p = ctid; p < HALF; p += ST_CONSUMERS) {
+                        const float x0 = __ldcg(qrow + h * HD + p), x1 = __ldcg(qrow + h * HD + p + HALF);
+                        float r0 = x0, r1 = x1;
+                        if (op.use_rope) rope_pair(x0, x1, cs, p, r0, r1);
+                        qs[p] = r0;
+                        qs[p + HALF] = r1;
+                    }
+                    if (fresh >= row0 && fresh < row1) {
+                        uint16_t *k16 = reinterpret_cast<uint16_t *>(fk);
+                        uint16_t *v16 = reinterpret_cast<uint16_t *>(fv);
+                        const bool owner = (h % qpk) == 0;   // appends the row to the cache
+                        uint16_t *kgw = op.kc + ((int64_t)g * op.n_rows + wrow) * HD;
+                        uint16_t *vgw = op.vc + ((int64_t)g * op.n_rows + wrow) * HD;
+                        for (int p = ctid; p < HALF; p += ST_CONSUMERS) {
+                            const float k0 = __ldcg(qrow + QD + g * HD + p), k1 = __ldcg(qrow + QD + g * HD + p + HALF);
+                            float r0 = bf16r(k0), r1 = bf16r(k1);
+                            if (op.use_rope) rope_pair(k0, k1, cs, p, r0, r1);
+                            const uint16_t b0 = bf16_bits(r0), b1 = bf16_bits(r1);
+                            const uint16_t c0 = bf16_bits(__ldcg(qrow + QD + KD + g * HD + p));
+                            const uint16_t c1 = bf16_bits(__ldcg(qrow + QD + KD + g * HD + p + HALF));
+                            k16[p] = b0;
+                            k16[p + HALF] = b1;
+                            v16[p] = c0;
+                            v16[p + HALF] = c1;
+                            if (owner) {
+                                kgw[p] = b0;
+                                kgw[p + HALF] = b1;
+                                vgw[p] = c0;
+                                vgw[p + HALF] = c1;
+                            }
+                        }
+                    }
+                    consumer_sync(ST_CONSUMERS);
                 }
                 if (fresh >= p0 && fresh < p0 + n) {
-                    uint16_t *k16 = reinterpret_cast<uint16_t *>(ks + (fresh - p0) * rw);
-                    uint16_t *v16 = reinterpret_cast<uint16_t *>(vs + (fresh - p0) * rw);
-                    const bool owner = (h % qpk) == 0;   // appends the row to the cache
-                    uint16_t *kg = op.kc + ((int64_t)g * op.n_rows + wrow) * HD;
-                    uint16_t *vg = op.vc + ((int64_t)g * op.n_rows + wrow) * HD;
-                    for (int p = ctid; p < HALF; p += ST_CONSUMERS) {
-                        const float k0 = __ldcg(qrow + QD + g * HD + p), k1 = __ldcg(qrow + QD + g * HD + p + HALF);
-                        float r0 = bf16r(k0), r1 = bf16r(k1);
-                        if (op.use_rope) rope_pair(k0, k1, cs, p, r0, r1);
-                        const uint16_t b0 = bf16_bits(r0), b1 = bf16_bits(r1);
-                        const uint16_t c0 = bf16_bits(__ldcg(qrow + QD + KD + g * HD + p));
-                        const uint16_t c1 = bf16_bits(__ldcg(qrow + QD + KD + g * HD + p + HALF));
-                        k16[p] = b0;
-                        k16[p + HALF] = b1;
-                        v16[p] = c0;
-                        v16[p + HALF] = c1;
-                        if (owner) {
-                            kg[p] = b0;
-                            kg[p + HALF] = b1;
-                            vg[p] = c0;
-                            vg[p + HALF] = c1;
-                        }
+                    if (kr == fresh - p0) {
+#pragma unroll
+                        for (int t = 0; t < KW / 4; t++)
+                            kw[t] = reinterpret_cast<const uint4 *>(fk + kq * KW)[t];
                     }
+#pragma unroll
+                    for (int j = 0; j < VJ; j++)
+                        if (vq + j * VR == fresh - p0) vw[j] = reinterpret_cast<const uint4 *>(fv)[vg];
                 }
-                cp_async_wait_all();
-                consumer_sync(ST_CONSUMERS);
-                // scores: warp cw takes rows cw, cw + 8, ...; lanes split the words
-                const float2 *qv = reinterpret_cast<const float2 *>(qs);
-                for (int r = cw; r < ST_ATT_ROWS; r += ST_CONSUMER_WARPS) {
+                // ---- scores: four threads per row, two shuffles
+                {
+                    const float2 *qv = reinterpret_cast<const float2 *>(qs) + kq * KW;
                     float a = 0.0f;
-                    if (r < n) {
-                        for (int w = lane; w < HW; w += 32) {
-                            const uint32_t kk = ks[r * rw + w];
-                            const float2 q = qv[w];
-                            a = fmaf(__uint_as_float(kk << 16), q.x, a);
-                            a = fmaf(__uint_as_float(kk & 0xffff0000u), q.y, a);
-                        }
-                    }
-                    a = warp_sum(a);
-                    if (lane == 0) scs[r] = (r < n) ? __fmul_rn(a, op.eps) : -INFINITY;
-                }
-                consumer_sync(ST_CONSUMERS);
-                // softmax (row = lane), identical in every warp
-                const float sv = scs[lane];
-                const float mx = warp_max(sv);
-                const float e = (lane < n) ? expf(sv - mx) : 0.0f;
-                const float l = warp_sum(e);
-                // values: word w, rows q0, q0 + Q, ... (q0 is warp-uniform)
-                const int w = ctid % HW, q0 = ctid / HW;
-                float ox = 0.0f, oy = 0.0f;
-                for (int p = q0; p < n; p += Q) {
-                    const float ep = __shfl_sync(0xffffffffu, e, p);
-                    const uint32_t vv = vs[p * rw + w];
-                    ox = fmaf(ep, __uint_as_float(vv << 16), ox);
-                    oy = fmaf(ep, __uint_as_float(vv & 0xffff0000u), oy);
-                }
-                vred[q0 * HW + w] = make_float2(ox, oy);
-                consumer_sync(ST_CONSUMERS);
-                const int64_t pi = ((int64_t)m * NH + h) * op.max_chunks + c;
-                if (ctid < HW) {
-                    float2 o = vred[ctid];
-                    for (int q = 1; q < Q; q++) {
-                        const float2 t = vred[q * HW + ctid];
-                        o.x = __fadd_rn(o.x, t.x);
-                        o.y = __fadd_rn(o.y, t.y);
-                    }
-                    *reinterpret_cast<float2 *>(op.part + pi * HD + 2 * ctid) = o;
-                }
-                if (ctid == 0) *reinterpret_cast<float2 *>(op.part_ml + pi * 2) = make_float2(mx, l);
-                // Count the item once the CTA's partials are released
-                // (barrier, then a cumulative fence); the last item of the
-                // (sequence, head) acquires everyone's and merges the chunks.
-                consumer_sync(ST_CONSUMERS);
-                if (ctid == 0) {
-                    fence_acq_rel_gpu();
-                    s_last = atomicAdd(op.cnt + m * NH + h, 1u) == (unsigned)(nch - 1);
-                    if (s_last) fence_acq_rel_gpu();
-                }
-                consumer_sync(ST_CONSUMERS);
-                if (s_last) {
-                    // Merge: every thread loads its chunks' partial outputs
-                    // (4 dims, chunks sl, sl + S, ...) together with the
-                    // chunk statistics, then rescales once the maximum is known.
-                    const int D4 = HD >> 2, S = ST_CONSUMERS / D4, d4 = ctid % D4, sl = ctid / D4;
-                    const float *po = op.part + ((int64_t)m * NH + h) * op.max_chunks * HD + 4 * d4;
-                    const float *pml = op.part_ml + ((int64_t)m * NH + h) * op.max_chunks * 2;
-                    const int mc4 = (op.max_chunks + 3) & ~3;
-                    float *cm = reinterpret_cast<float *>(aux);            // [max_chunks] max -> factor
-                    float *cl = cm + mc4;                                   // [max_chunks] sum
-                    float4 *sred = reinterpret_cast<float4 *>(cl + mc4);   // [S][D4]
-                    float4 ov[4];
 #pragma unroll
-                    for (int k = 0; k < 4; k++) {
-                        const int c2 = sl + k * S;
-                        ov[k] = c2 < nch ? ldcg4(po + (int64_t)c2 * HD) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    }
-                    for (int t = ctid; t < nch; t += ST_CONSUMERS) {
-                        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pml) + t);
-                        cm[t] = ml.x;
-                        cl[t] = ml.y;
-                    }
-                    consumer_sync(ST_CONSUMERS);
-                    if (cw == 0) {
-                        float gm = -INFINITY;
-                        for (int c2 = lane; c2 < nch; c2 += 32) gm = fmaxf(gm, cm[c2]);
-                        gm = warp_max(gm);
-                        float gl = 0.0f;
-                        for (int c2 = lane; c2 < nch; c2 += 32) {
-                            const float f = expf(cm[c2] - gm);
-                            gl = fmaf(cl[c2], f, gl);
-                            cm[c2] = f;
-                        }
-                        gl = warp_sum(gl);
-                        if (lane == 0) s_l = gl;
-                    }
-                    consumer_sync(ST_CONSUMERS);
-                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (int cb = 0; cb < nch; cb += 4 * S) {
-                        if (cb > 0) {   // more than 4 chunks per thread: next batch
+                    for (int t = 0; t < KW / 4; t++) {
+                        const uint32_t wds[4] = {kw[t].x, kw[t].y, kw[t].z, kw[t].w};
 #pragma unroll
-                            for (int k = 0; k < 4; k++) {
-                                const int c2 = cb + sl + k * S;
-                                ov[k] = c2 < nch ? ldcg4(po + (int64_t)c2 * HD) : make_float4(0.f, 0.f, 0.f, 0.f);
-                            }
+                        for (int e = 0; e < 4; e++) {
+                            const float2 q = qv[4 * t + e];
+                            a = fmaf(__uint_as_float(wds[e] << 16), q.x, a);
+                            a = fmaf(__uint_as_float(wds[e] & 0xffff0000u), q.y, a);
                         }
+                    }
+                    a += __shfl_xor_sync(0xffffffffu, a, 1);
+                    a += __shfl_xor_sync(0xffffffffu, a, 2);
+                    if (kq == 0) scs[kr] = (kr < n) ? __fmul_rn(a, op.eps) : -INFINITY;
+                }
+                consumer_sync(ST_CONSUMERS);
+                // ---- online softmax, identical in every warp (rows lane, lane + 32)
+                const float s0 = scs[lane], s1 = scs[lane + 32];
+                const float pmax = warp_max(fmaxf(s0, s1));
+                const float mnew = fmaxf(mrun, pmax);
+                const float fac = mrun == -INFINITY ? 0.0f : expf(mrun - mnew);
+                const float e0 = lane < n ? expf(s0 - mnew) : 0.0f;
+                const float e1 = lane + 32 < n ? expf(s1 - mnew) : 0.0f;
+                lrun = fmaf(lrun, fac, warp_sum(e0 + e1));
+                mrun = mnew;
+                // ---- values: rows vq + j * VR, words 4 vg .. 4 vg + 3
 #pragma unroll
-                        for (int k = 0; k < 4; k++) {
-                            const int c2 = cb + sl + k * S;
-                            if (c2 < nch) {
-                                const float f = cm[c2];
-                                acc.x = fmaf(ov[k].x, f, acc.x);
-                                acc.y = fmaf(ov[k].y, f, acc.y);
-                                acc.z = fmaf(ov[k].z, f, acc.z);
-                                acc.w = fmaf(ov[k].w, f, acc.w);
-                            }
-                        }
+                for (int e = 0; e < 4; e++) {
+                    ox[e] *= fac;
+                    oy[e] *= fac;
+                }
+#pragma unroll
+                for (int j = 0; j < VJ; j++) {
+                    const int r = vq + j * VR;
+                    const float ea = __shfl_sync(0xffffffffu, e0, r & 31);
+                    const float eb = __shfl_sync(0xffffffffu, e1, r & 31);
+                    const float ep = r < 32 ? ea : eb;
+                    const uint32_t wds[4] = {vw[j].x, vw[j].y, vw[j].z, vw[j].w};
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        ox[e] = fmaf(ep, __uint_as_float(wds[e] << 16), ox[e]);
+                        oy[e] = fmaf(ep, __uint_as_float(wds[e] & 0xffff0000u), oy[e]);
                     }
-                    sred[sl * D4 + d4] = acc;
-                    consumer_sync(ST_CONSUMERS);
-                    if (ctid < HD) {
-                        const float *sr = reinterpret_cast<const float *>(sred);
-                        float o = 0.0f;
-                        for (int s2 = 0; s2 < S; s2++) o = __fadd_rn(o, sr[s2 * HD + ctid]);
-                        op.y[(int64_t)m * op.ldy + h * HD + ctid] = __fdiv_rn(o, s_l);
+                }
+                consumer_sync(ST_CONSUMERS);   // scs is rewritten by the next pass
+            }
+            // ---- partial output of the span: sum the row subsets
+#pragma unroll
+            for (int sh = VG; sh < 32; sh <<= 1) {
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    ox[e] += __shfl_xor_sync(0xffffffffu, ox[e], sh);
+                    oy[e] += __shfl_xor_sync(0xffffffffu, oy[e], sh);
+                }
+            }
+            if (lane < VG) {
+#pragma unroll
+                for (int e = 0; e < 4; e++) vred[cw * HW + 4 * vg + e] = make_float2(ox[e], oy[e]);
+            }
+            consumer_sync(ST_CONSUMERS);
+            float2 o = make_float2(0.f, 0.f);
+            if (ctid < HW) {
+                o = vred[ctid];
+                for (int w2 = 1; w2 < ST_CONSUMER_WARPS; w2++) {
+                    const float2 t = vred[w2 * HW + ctid];
+                    o.x = __fadd_rn(o.x, t.x);
+                    o.y = __fadd_rn(o.y, t.y);
+                }
+            }
+            if (nsp == 1) {
+                // one span: the item's output is the head's
+                if (ctid < HW)
+                    *reinterpret_cast<float2 *>(op.y + (int64_t)m * op.ldy + h * HD + 2 * ctid) =
+                        make_float2(__fdiv_rn(o.x, lrun), __fdiv_rn(o.y, lrun));
+                continue;
+            }
+            const int64_t pi = ((int64_t)m * NH + h) * op.max_chunks + sp;
+            if (ctid < HW) *reinterpret_cast<float2 *>(op.part + pi * HD + 2 * ctid) = o;
+            if (ctid == 0) *reinterpret_cast<float2 *>(op.part_ml + pi * 2) = make_float2(mrun, lrun);
+            // Count the item once the CTA's partials are released (barrier,
+            // then a cumulative fence); the last item of the (sequence,
+            // head) acquires everyone's and merges the spans.
+            consumer_sync(ST_CONSUMERS);
+            if (ctid == 0) {
+                fence_acq_rel_gpu();
+                s_last = atomicAdd(op.cnt + m * NH + h, 1u) == (unsigned)(nsp - 1);
+                if (s_last) fence_acq_rel_gpu();
+            }
+            consumer_sync(ST_CONSUMERS);
+            if (s_last) {
+                // thread (d4, sl): 4 dims of spans sl, sl + S, ...
+                const int D4 = HD >> 2, S = ST_CONSUMERS / D4, d4 = ctid % D4, sl = ctid / D4;
+                const float *po = op.part + ((int64_t)m * NH + h) * op.max_chunks * HD + 4 * d4;
+                const float *pml = op.part_ml + ((int64_t)m * NH + h) * op.max_chunks * 2;
+                const int mc4 = (op.max_chunks + 3) & ~3;
+                float *cm = reinterpret_cast<float *>(aux);            // [max_chunks] max -> factor
+                float *cl = cm + mc4;                                   // [max_chunks] sum
+                float4 *sred = reinterpret_cast<float4 *>(cl + mc4);   // [S][D4]
+                for (int t = ctid; t < nsp; t += ST_CONSUMERS) {
+                    const float2 ml = __ldcg(reinterpret_cast<const float2 *>(pml) + t);
+                    cm[t] = ml.x;
+                    cl[t] = ml.y;
+                }
+                consumer_sync(ST_CONSUMERS);
+                if (cw == 0) {
+                    float gm = -INFINITY;
+                    for (int c2 = lane; c2 < nsp; c2 += 32) gm = fmaxf(gm, cm[c2]);
+                    gm = warp_max(gm);
+                    float gl = 0.0f;
+                    for (int c2 = lane; c2 < nsp; c2 += 32) {
+                        const float f = expf(cm[c2] - gm);
+                        gl = fmaf(cl[c2], f, gl);
+                        cm[c2] = f;
                     }
+                    gl = warp_sum(gl);
+                    if (lane == 0) s_l = gl;
+                }
+                consumer_sync(ST_CONSUMERS);
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int c2 = sl; c2 < nsp; c2 += S) {
+                    const float4 ov = ldcg4(po + (int64_t)c2 * HD);
+                    const float f = cm[c2];
+                    acc.x = fmaf(ov.x, f, acc.x);
+                    acc.y = fmaf(ov.y, f, acc.y);
+                    acc.z = fmaf(ov.z, f, acc.z);
+                    acc.w = fmaf(ov.w, f, acc.w);
+                }
+                sred[sl * D4 + d4] = acc;
+                consumer_sync(ST_CONSUMERS);
+                if (ctid < HD) {
+                    const float *sr = reinterpret_cast<const float *>(sred);
+                    float o2 = 0.0f;
+                    for (int s2 = 0; s2 < S; s2++) o2 = __fadd_rn(o2, sr[s2 * HD + ctid]);
+                    op.y[(int64_t)m * op.ldy + h * HD + ctid] = __fdiv_rn(o2, s_l);
                 }
             }
         }
         base += items;
+    }
+}
+
+__device__ __noinline__ void stream_attn(const StreamOp &op, const int *st, uint8_t *aux, int cta, int G, int ctid,
+                                         int cw, int lane) {
+    switch (op.head_dim) {
+        case 64: stream_attn_hw<32>(op, st, aux, cta, G, ctid, cw, lane); break;
+        case 128: stream_attn_hw<64>(op, st, aux, cta, G, ctid, cw, lane); break;
+        default: stream_attn_hw<128>(op, st, aux, cta, G, ctid, cw, lane); break;
     }
 }
 
@@ -887,16 +972,16 @@ __device__ __forceinline__ void attn_prefetch(const StreamOp &op, const int *st,
     int base = 0;
     for (int m = 0; m < op.M; m++) {
         const int rope_pos = st[4 * m], rstart = st[4 * m + 2], L = st[4 * m + 3];
-        const int nch = (L + ST_ATT_ROWS - 1) / ST_ATT_ROWS, items = NH * nch;
+        int nsp, ppi;
+        attn_split(L, op.M, NH, G, nsp, ppi);
+        const int items = NH * nsp;
         for (int idx = base + (cta - base % G + G) % G; idx < base + items; idx += G) {
-            const int h = (idx - base) / nch, c = (idx - base) - h * nch;
-            {
-                const int p0 = c * ST_ATT_ROWS, n = min(ST_ATT_ROWS, L - p0);
-                const int64_t row = (int64_t)(h / qpk) * op.n_rows + rstart + p0;
-                prefetch_l2(op.kc + row * HD, (uint32_t)(n * HD * 2));
-                prefetch_l2(op.vc + row * HD, (uint32_t)(n * HD * 2));
-                if (op.use_rope) prefetch_l2(op.rope_cs + (int64_t)rope_pos * HD, (uint32_t)(HD * 4));
-            }
+            const int h = (idx - base) / nsp, sp = (idx - base) - h * nsp;
+            const int row0 = sp * ppi * ATT_PASS, n = min(L, row0 + ppi * ATT_PASS) - row0;
+            const int64_t row = (int64_t)(h / qpk) * op.n_rows + rstart + row0;
+            prefetch_l2(op.kc + row * HD, (uint32_t)(n * HD * 2));
+            prefetch_l2(op.vc + row * HD, (uint32_t)(n * HD * 2));
+            if (op.use_rope) prefetch_l2(op.rope_cs + (int64_t)rope_pos * HD, (uint32_t)(HD * 4));
         }
         base += items;
     }

@@ -76,10 +76,13 @@ constexpr int ST_THREADS = ST_CONSUMERS + 32;
 constexpr int ST_XBYTES = 16384;                // activation operand (int8 or fp16)
 constexpr int ST_MMAX = 8;
 constexpr int ST_MAX_OPS = 384;                 // ops per program (row table in shared memory)
+constexpr int ST_RES_ROWS = 256;                // residual rows fetched ahead (M = 1 ops) ...
+constexpr int ST_RES_OFF = 2048;                // ... at this offset in the aux scratch
 
 // Scratch of the non-GEMV ops (attention chunk staging, row statistics).
 constexpr int ST_ATT_ROWS = 32;                  // K/V rows per attention item
 constexpr int ST_AUX_BYTES = 26624;
+static_assert(ST_RES_OFF + 4 * ST_RES_ROWS <= ST_AUX_BYTES, "residual rows in the aux scratch");
 
 // Dynamic shared memory of a launch with `ns` ring stages: weight slots,
 // scale slots, the activation operand, the mbarriers, then (if the program
@@ -100,12 +103,11 @@ struct StreamStep {
     int v[ST_MMAX][4];
 };
 
-// Shared-memory bytes the attention op needs: one item's K/V tiles, query,
-// scores and value partials, or the chunk merge's statistics and partials.
+// Shared-memory bytes the attention op needs: one item's query, new row,
+// scores and value partials, or the span merge's statistics and partials.
 inline size_t stream_attn_aux_bytes(int head_dim, int max_chunks) {
-    const int hw = head_dim / 2, rw = hw + 1;
-    const size_t item = (size_t)2 * ST_ATT_ROWS * rw * 4 + (size_t)head_dim * 4 + ST_ATT_ROWS * 4 +
-                        (size_t)ST_CONSUMERS * 8;
+    const int hw = head_dim / 2;
+    const size_t item = (size_t)head_dim * 4 + (size_t)2 * hw * 4 + 64 * 4 + (size_t)ST_CONSUMER_WARPS * hw * 8;
     const size_t merge = (size_t)2 * ((max_chunks + 3) & ~3) * 4 + (size_t)ST_CONSUMERS * 16;
     return item > merge ? item : merge;
 }
