@@ -66,7 +66,29 @@ def build(verbose: bool = False, jobs: int = 8) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    build_host()
     return LIB
+
+
+HOST_SRC = os.path.join(HERE, "host", "vcpm_gen_run.c")
+HOST_BIN = os.path.join(HERE, "host", "vcpm_gen_run")
+
+
+def build_host() -> str:
+    """The C11 host driver (host/vcpm_gen_run.c): compiled as plain C with
+    warnings as errors against include/vcpm_b200.h alone and linked to the
+    library above (rpath: the library's directory)."""
+    hdr = os.path.join(ROOT, "include", "vcpm_b200.h")
+    if os.path.exists(HOST_BIN) and all(os.path.getmtime(HOST_BIN) >= os.path.getmtime(d)
+                                        for d in (HOST_SRC, hdr, LIB)):
+        return HOST_BIN
+    cc = shutil.which("gcc", path="/usr/bin") or "gcc"
+    cmd = [cc, "-std=c11", "-O2", "-Wall", "-Wextra", "-Werror", "-pedantic", "-I", os.path.join(ROOT, "include"),
+           HOST_SRC, "-o", HOST_BIN, "-L", HERE, "-lvcpm_b200", "-Wl,-rpath," + HERE, "-lm"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"host driver build failed:\n{r.stdout}\n{r.stderr}")
+    return HOST_BIN
 
 
 if __name__ == "__main__":
