@@ -1047,6 +1047,8 @@ def e2e_bench(ctx, host_layers, args, rank, world, gpu_index=0, wtype=None):
     ctx.sync()
     vae_ms = ctx.elapsed_ms(vev[0], vev[1]) / 10
     vae_tflops = vae_flops(B * PATCH) / (vae_ms * 1e-3) / 1e12
+    stop_run = None if (args.no_e2e_stop or f16) else e2e_stop_run(ctx, vb, parts, vst, embed, ids, ids_h, emb, patches, audio,
+                                                          audio_h, stops, T, NP, B, rank, world)
     vst.close()
     vae.close()
     tt = max_over_ranks([pre_ms + steps_ms, pre_ms, steps_ms], world)
@@ -1079,7 +1081,70 @@ def e2e_bench(ctx, host_layers, args, rank, world, gpu_index=0, wtype=None):
                     "tflops": vae_tflops, "fp32_simt_nominal_tflops": FP32_SIMT_NOMINAL_TFLOPS,
                     "frac_of_nominal": vae_tflops / FP32_SIMT_NOMINAL_TFLOPS},
             "excluded": "none of the synthetic pipeline (tokenizer and WAV writing are host I/O)",
+            "with_stop": stop_run,
             "cpu_baseline": base}
+
+
+def e2e_stop_run(ctx, vb, parts, vst, embed, ids, ids_h, emb, patches, audio, audio_h, stops, T, NP, B, rank, world):
+    """The same pipeline with the reference's per-utterance termination
+    (src/gen_run.c:166-215): every patch step returns the stop flags
+    (stop predictor + min-length gate, min_len = NP / 2, at most NP
+    patches), the host reads them, and finished utterances leave both the
+    generator (vb_gen_retire) and the VAE streams (vb_vae_stream_retire),
+    so later steps run at the smaller batch.  RTF = max-over-ranks time /
+    the audio actually generated (all ranks)."""
+    import torch
+    gen = vb.Gen(ctx, parts, B, T + NP + 8)
+    gen.set_min_len(NP // 2)
+    vst.reset()
+    flags = torch.zeros(B, dtype=torch.int32, device="cuda")
+    flags_h = torch.zeros(B, dtype=torch.int32).pin_memory()
+    torch.cuda.synchronize()
+    ctx.sync()
+    if world > 1:
+        torch.distributed.barrier()
+    ev = [ctx.event() for _ in range(2)]
+    ctx.record(ev[0])
+    ctx.memcpy_h2d(ids, ids_h, ids_h.numel() * 4)
+    ctx.get_rows(embed, ids, B * T, emb)
+    gen.prefill(T, emb)
+    active = list(range(B))
+    n_patches = [0] * B
+    steps = 0
+    for s in range(NP):
+        n = len(active)
+        gen.step(1000 + rank * B, patches[s][:n], stops[s][:n], flags[:n])
+        vst.decode(patches[s][:n], PATCH, audio[s][:n])
+        ctx.memcpy_d2h(flags_h, flags, n * 4)
+        ctx.sync()
+        steps += 1
+        fl = flags_h[:n].tolist()
+        for u in active:
+            n_patches[u] += 1
+        done = [active[j] for j in range(n) if fl[j]]
+        if done:
+            gen.retire(done)
+            vst.retire(done)
+            active = [u for u in active if u not in done]
+        if not active:
+            break
+    ctx.memcpy_d2h(audio_h, audio, audio.numel() * 4)
+    ctx.record(ev[1])
+    ctx.sync()
+    ms = ctx.elapsed_ms(ev[0], ev[1])
+    rc, derr = ctx.device_status()
+    gen.close()
+    tmax = max_over_ranks([ms], world)[0]
+    tot = torch.tensor([float(sum(n_patches))], dtype=torch.float64, device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(tot)
+    audio_s = float(tot.item()) * SAMPLES_PER_PATCH / SAMPLE_RATE
+    return {"rtf": tmax * 1e-3 / audio_s, "wall_ms_max_over_ranks": tmax, "audio_s": audio_s,
+            "min_len": NP // 2, "max_len": NP, "steps_rank0": steps,
+            "patches_per_utterance_rank0": {"min": min(n_patches), "mean": sum(n_patches) / B, "max": max(n_patches)},
+            "device_error": derr,
+            "note": "host reads the stop flags every patch (one synchronisation per step, as the reference's "
+                    "loop); finished utterances are compacted out of the generator and the VAE streams"}
 
 
 def cpu_e2e_baseline(w, prompt=32, patches=2):
@@ -1160,6 +1225,8 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-e2e-f16", action="store_true", help="skip the F16-weight variant of the e2e run")
+    ap.add_argument("--no-e2e-stop", action="store_true",
+                    help="skip the e2e run with stop-predictor termination (min_len = patches / 2)")
     ap.add_argument("--e2e-utts", type=int, default=64)
     ap.add_argument("--e2e-patches", type=int, default=100)
     ap.add_argument("--e2e-clock-ms", type=int, default=500, help="nvidia-smi sampling period during the e2e run")

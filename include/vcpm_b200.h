@@ -519,6 +519,17 @@ int vb_vae_stream_reset(vb_ctx *ctx, vb_vae_stream s);
  * with more timesteps than the stream has seen, (re)allocates the stream's
  * activation buffers (waiting for the stream first). */
 int vb_vae_stream_decode(vb_ctx *ctx, vb_vae_stream s, const float *latent, int n_timesteps, float *audio);
+/* Ends the listed streams (utterance indices 0..n_streams-1 of the
+ * creation; ended or unknown indices are ignored): the VAE side of the
+ * per-utterance break of src/gen_run.c:208-213.  The remaining streams'
+ * histories are compacted, in utterance order, so later decodes take
+ * latent/audio rows of the remaining streams only -- the row order of
+ * vb_gen_active after the same vb_gen_retire.  Synchronises the context
+ * stream.  vb_vae_stream_reset brings back every stream. */
+int vb_vae_stream_retire(vb_ctx *ctx, vb_vae_stream s, int n, const int32_t *utterances);
+/* Number of current streams; their utterance indices in row order into
+ * `utterances` (host int32 [n_streams]) when not NULL.  -1 for a NULL s. */
+int vb_vae_stream_active(vb_vae_stream s, int32_t *utterances);
 void vb_vae_stream_destroy(vb_ctx *ctx, vb_vae_stream s);
 int vb_vae_stream_conv_cache_count(vb_vae_stream s);     /* 20 */
 int vb_vae_stream_upconv_cache_count(vb_vae_stream s);   /* 6  */

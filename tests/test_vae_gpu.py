@@ -31,7 +31,11 @@ def ctx():
 
 
 def dev(a):
-    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()
+    """Device copy, complete before returning: the library's stream does not
+    wait for torch's."""
+    t = torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()
+    torch.cuda.synchronize()
+    return t
 
 
 def oracle_stream(cfg, t, latent, chunks, f32=False):
@@ -61,8 +65,8 @@ def device_stream(ctx, vae, latent, chunks, up):
     outs = []
     at = 0
     for c in chunks:
-        lat = dev(latent[:, at:at + c])
         audio = torch.full((n, c * up), float("nan"), device="cuda")
+        lat = dev(latent[:, at:at + c])     # synchronises, so the fill above has landed
         st.decode(lat, c, audio)
         ctx.sync()
         outs.append(audio.cpu().numpy())
@@ -186,5 +190,39 @@ def test_vae_rejects_bad_arguments(ctx):
     with pytest.raises(vb.VBError) as e:
         st.decode(lat, 2, audio.data_ptr() + 4)                         # misaligned output
     assert e.value.code == vb.VB_ERR_INVALID_ARG
+    st.close()
+    vae.close()
+
+
+def test_vae_stream_retire_continues_remaining_streams(ctx):
+    """Retiring streams compacts the histories of the rest: after two patches
+    of four utterances, utterances 1 and 3 end and the third patch of 0 and 2
+    (now rows 0 and 1) matches the oracle's uninterrupted streams."""
+    cfg = O.VAEConfig(**SMALL)
+    t = S.vae_tensors(cfg)
+    vae = vb.VAE(ctx, vb_cfg(cfg), t)
+    latent = S.normal((4, 12, cfg.latent_dim))
+    up = cfg.upsample()
+    st = vae.stream(4, 4)
+    for c0 in (0, 4):
+        audio = torch.zeros((4, 4 * up), device="cuda")
+        lat = dev(latent[:, c0:c0 + 4])
+        st.decode(lat, 4, audio)
+        ctx.sync()
+    st.retire([3, 1, 7])            # 7: unknown, ignored
+    assert st.active() == [0, 2]
+    audio = torch.full((2, 4 * up), float("nan"), device="cuda")
+    lat3 = dev(latent[[0, 2], 8:12])
+    st.decode(lat3, 4, audio)
+    ctx.sync()
+    got = audio.cpu().numpy()
+    keep = latent[[0, 2]]
+    ref = oracle_stream(cfg, t, keep, [4, 4, 4])[:, 8 * up:]
+    ref32 = oracle_stream(cfg, t, keep, [4, 4, 4], f32=True)[:, 8 * up:]
+    assert_pcm_close(got, ref, ref32)
+    st.retire([0, 2])
+    assert st.active() == []
+    st.reset()
+    assert st.active() == [0, 1, 2, 3]
     st.close()
     vae.close()

@@ -377,6 +377,10 @@ struct vb_vae_s {
 struct vb_vae_stream_s {
     vb_vae vae = nullptr;
     int n = 0;                    // streams (utterances) decoded in lockstep
+    int n0 = 0;                   // streams at creation (the caches' row capacity)
+    std::vector<int32_t> utt;     // utterance index of each current row
+    int32_t *map_dev = nullptr;   // [n0] row map of a retire
+    float *tmp = nullptr;         // gather scratch of a retire (largest cache)
     int patch_size = 0;
     int parity = 0;               // which half of each double-buffered history is current
     float *cache_in[2] = {};      // [n][6][latent]
@@ -629,7 +633,7 @@ extern "C" int vb_vae_stream_create(vb_ctx *ctx, vb_vae v, int n_streams, int pa
     if (fault_injected("alloc")) return set_error(ctx, VB_ERR_OOM, "vb_vae_stream_create: injected allocation fault");
     vb_vae_stream s = new vb_vae_stream_s();
     s->vae = v;
-    s->n = n_streams;
+    s->n = s->n0 = n_streams;
     s->patch_size = patch_size;
     const vb_vae_config &c = v->cfg;
     const int D = c.decoder_dim;
@@ -650,6 +654,19 @@ extern "C" int vb_vae_stream_create(vb_ctx *ctx, vb_vae v, int n_streams, int pa
                 ok = alloc((size_t)n_streams * 6 * VAE_DIL[u] * (D >> (b + 1)), &s->cache_res[b][u][h]);
     }
     for (int h = 0; h < 2 && ok; h++) ok = alloc((size_t)n_streams * 6 * (D >> 6), &s->cache_out[h]);
+    if (ok) {
+        // retire scratch: the row map and one gather buffer of the largest cache
+        size_t big = (size_t)6 * c.latent_dim;
+        for (int b = 0; b < 6; b++) big = std::max(big, (size_t)6 * VAE_DIL[2] * (D >> (b + 1)));
+        big = std::max(big, (size_t)D);
+        void *m = nullptr, *t = nullptr;
+        ok = cudaMalloc(&m, (size_t)n_streams * 4) == cudaSuccess;
+        if (ok) s->allocs.push_back(m);
+        ok = ok && cudaMalloc(&t, big * n_streams * sizeof(float)) == cudaSuccess;
+        if (ok) s->allocs.push_back(t);
+        s->map_dev = static_cast<int32_t *>(m);
+        s->tmp = static_cast<float *>(t);
+    }
     if (!ok) {
         vb_vae_stream_destroy(ctx, s);
         return set_error(ctx, VB_ERR_OOM, "vb_vae_stream_create: history allocation failed");
@@ -665,6 +682,10 @@ extern "C" int vb_vae_stream_create(vb_ctx *ctx, vb_vae v, int n_streams, int pa
 
 extern "C" int vb_vae_stream_reset(vb_ctx *ctx, vb_vae_stream s) {
     if (!ctx || !s) return VB_ERR_INVALID_ARG;
+    // every stream of the creation, in utterance order, from zero history
+    s->n = s->n0;
+    s->utt.resize(s->n0);
+    for (int i = 0; i < s->n0; i++) s->utt[i] = i;
     const vb_vae_config &c = s->vae->cfg;
     const int D = c.decoder_dim, n = s->n;
     for (int h = 0; h < 2; h++) {
@@ -680,6 +701,69 @@ extern "C" int vb_vae_stream_reset(vb_ctx *ctx, vb_vae_stream s) {
     }
     s->parity = 0;
     return VB_OK;
+}
+
+namespace vb {
+__global__ void vae_gather_rows_kernel(const float *src, float *dst, const int32_t *map, int rows, int64_t width) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)rows * width) return;
+    const int64_t r = i / width, c = i % width;
+    dst[i] = src[(int64_t)map[r] * width + c];
+}
+}  // namespace vb
+
+extern "C" int vb_vae_stream_retire(vb_ctx *ctx, vb_vae_stream s, int n, const int32_t *utterances) {
+    if (!ctx || !s || n < 0 || (n > 0 && !utterances)) return VB_ERR_INVALID_ARG;
+    std::vector<char> drop(s->n, 0);
+    bool any = false;
+    for (int i = 0; i < n; i++)
+        for (int r = 0; r < s->n; r++)
+            if (s->utt[r] == utterances[i] && !drop[r]) {
+                drop[r] = 1;
+                any = true;
+            }
+    if (!any) return VB_OK;
+    std::vector<int32_t> map, utt;
+    for (int r = 0; r < s->n; r++)
+        if (!drop[r]) {
+            map.push_back(r);
+            utt.push_back(s->utt[r]);
+        }
+    const int nk = (int)map.size();
+    if (nk > 0) {
+        const vb_vae_config &c = s->vae->cfg;
+        const int D = c.decoder_dim;
+        std::vector<std::pair<float *, int64_t>> bufs;   // cache, floats per stream
+        for (int h = 0; h < 2; h++) {
+            bufs.push_back({s->cache_in[h], (int64_t)6 * c.latent_dim});
+            bufs.push_back({s->cache_out[h], (int64_t)6 * (D >> 6)});
+        }
+        for (int b = 0; b < 6; b++) {
+            bufs.push_back({s->cache_up[b], (int64_t)(D >> b)});
+            for (int u = 0; u < 3; u++)
+                for (int h = 0; h < 2; h++) bufs.push_back({s->cache_res[b][u][h], (int64_t)6 * VAE_DIL[u] * (D >> (b + 1))});
+        }
+        VB_CHECK(ctx, cudaMemcpyAsync(s->map_dev, map.data(), (size_t)nk * 4, cudaMemcpyHostToDevice, ctx->stream));
+        for (auto &bw : bufs) {
+            const int64_t total = (int64_t)nk * bw.second;
+            vae_gather_rows_kernel<<<(unsigned)((total + 255) / 256), 256, 0, ctx->stream>>>(bw.first, s->tmp, s->map_dev,
+                                                                                           nk, bw.second);
+            VB_LAUNCH_CHECK(ctx, "vae_gather_rows");
+            VB_CHECK(ctx, cudaMemcpyAsync(bw.first, s->tmp, (size_t)total * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+        }
+    }
+    // the host row map must outlive the copy that reads it
+    VB_CHECK(ctx, cudaStreamSynchronize(ctx->stream));
+    s->n = nk;
+    s->utt = utt;
+    return VB_OK;
+}
+
+extern "C" int vb_vae_stream_active(vb_vae_stream s, int32_t *utterances) {
+    if (!s) return -1;
+    if (utterances)
+        for (int r = 0; r < s->n; r++) utterances[r] = s->utt[r];
+    return s->n;
 }
 
 extern "C" void vb_vae_stream_destroy(vb_ctx *ctx, vb_vae_stream s) {

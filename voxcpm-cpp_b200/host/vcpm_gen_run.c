@@ -7,7 +7,8 @@
  * TSLM -> FSQ -> RALM -> stop predictor with the min-length gate), the
  * latent patch of every utterance through the streaming AudioVAE decoder,
  * and the reference's per-utterance break (:195-213): utterances whose stop
- * flag is set are retired (vb_gen_retire compacts the batch), the rest go
+ * flag is set are retired from the generator and the VAE streams alike
+ * (vb_gen_retire / vb_vae_stream_retire compact both batches), the rest go
  * on until max_len patches.
  *
  *   vcpm_gen_run layout
@@ -317,13 +318,11 @@ static int run(int B, int max_len, int min_len, uint64_t seed) {
     check(vb_gen_set_min_len(g, min_len), "vb_gen_set_min_len");
     float *emb = dev_vec((int64_t)B * PROMPT * H, 0.0f, 0.5f);
     check(vb_gen_prefill(ctx, g, PROMPT, emb), "vb_gen_prefill");
-    void *patches = NULL, *lat = NULL, *audio = NULL, *stop_d = NULL;
+    void *patches = NULL, *audio = NULL, *stop_d = NULL;
     const size_t prow = (size_t)PATCH * FEAT * 4;
     check(vb_malloc(ctx, (size_t)B * prow, &patches), "vb_malloc");
-    check(vb_malloc(ctx, (size_t)B * prow, &lat), "vb_malloc");
     check(vb_malloc(ctx, (size_t)B * spp * 4, &audio), "vb_malloc");
     check(vb_malloc(ctx, (size_t)B * 4, &stop_d), "vb_malloc");
-    check(vb_memset(ctx, lat, 0, (size_t)B * prow), "vb_memset");
     int32_t *active = (int32_t *)keep(calloc((size_t)B, 4)), *stop = (int32_t *)keep(calloc((size_t)B, 4));
     int32_t *done = (int32_t *)keep(calloc((size_t)B, 4));
     int *n_patches = (int *)keep(calloc((size_t)B, sizeof(int)));
@@ -334,22 +333,23 @@ static int run(int B, int max_len, int min_len, uint64_t seed) {
         const int n = vb_gen_active(g, active);
         if (n <= 0) break;
         check(vb_gen_step_stop(ctx, g, seed, (float *)patches, NULL, (int32_t *)stop_d), "vb_gen_step_stop");
-        /* the active rows' patches into their utterances' VAE streams */
-        for (int j = 0; j < n; j++)
-            check(vb_memcpy_d2d(ctx, (char *)lat + (size_t)active[j] * prow, (char *)patches + (size_t)j * prow, prow),
-                  "vb_memcpy_d2d");
-        check(vb_vae_stream_decode(ctx, vst, (const float *)lat, PATCH, (float *)audio), "vb_vae_stream_decode");
-        check(vb_memcpy_d2h(ctx, pcm, audio, (size_t)B * spp * 4), "vb_memcpy_d2h");
+        /* the VAE streams are retired with the generator's rows, so the
+         * patches' row order is the streams' */
+        check(vb_vae_stream_decode(ctx, vst, (const float *)patches, PATCH, (float *)audio), "vb_vae_stream_decode");
+        check(vb_memcpy_d2h(ctx, pcm, audio, (size_t)n * spp * 4), "vb_memcpy_d2h");
         check(vb_memcpy_d2h(ctx, stop, stop_d, (size_t)n * 4), "vb_memcpy_d2h");
         check(vb_sync(ctx), "vb_sync");
         int n_done = 0;
         for (int j = 0; j < n; j++) {
             const int u = active[j];
             n_patches[u]++;
-            for (int s = 0; s < spp; s++) checksum += fabs((double)pcm[(size_t)u * spp + s]);
+            for (int s = 0; s < spp; s++) checksum += fabs((double)pcm[(size_t)j * spp + s]);
             if (stop[j]) done[n_done++] = u;
         }
-        if (n_done) check(vb_gen_retire(ctx, g, n_done, done), "vb_gen_retire");
+        if (n_done) {
+            check(vb_gen_retire(ctx, g, n_done, done), "vb_gen_retire");
+            check(vb_vae_stream_retire(ctx, vst, n_done, done), "vb_vae_stream_retire");
+        }
         steps++;
     }
     int derr = 0;

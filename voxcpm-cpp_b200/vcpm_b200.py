@@ -154,6 +154,8 @@ SIGNATURES = {
     "vb_vae_stream_reset": (_I, [_P, _P]),
     "vb_vae_stream_decode": (_I, [_P, _P, _P, _I, _P]),
     "vb_vae_stream_destroy": (None, [_P, _P]),
+    "vb_vae_stream_retire": (_I, [_P, _P, _I, C.POINTER(C.c_int32)]),
+    "vb_vae_stream_active": (_I, [_P, C.POINTER(C.c_int32)]),
     "vb_vae_stream_conv_cache_count": (_I, [_P]),
     "vb_vae_stream_upconv_cache_count": (_I, [_P]),
     "vb_vae_stream_patch_samples": (_I, [_P]),
@@ -574,6 +576,19 @@ class VAEStream:
 
     def reset(self):
         self.ctx.check(self.ctx.L.vb_vae_stream_reset(self.ctx.h, self.h))
+
+    def retire(self, utterances):
+        """Ends the listed streams (utterance indices); the rest are compacted."""
+        u = list(utterances)
+        arr = (C.c_int32 * max(1, len(u)))(*u)
+        self.ctx.check(self.ctx.L.vb_vae_stream_retire(self.ctx.h, self.h, len(u), arr))
+
+    def active(self):
+        """Utterance indices of the current streams, in row order."""
+        n = self.ctx.L.vb_vae_stream_active(self.h, None)
+        buf = (C.c_int32 * max(1, n))()
+        self.ctx.L.vb_vae_stream_active(self.h, buf)
+        return list(buf[:n])
 
     def info(self):
         L = self.ctx.L
