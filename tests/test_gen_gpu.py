@@ -293,3 +293,41 @@ def test_retired_rows_compact(ctx):
         S.assert_envelope(p, rp[s, u], rp32[s, u])
     assert (3, 1) not in got and (3, 0) in got and (3, 2) in got
     m.close()
+
+
+def test_generation_step_replays_from_a_graph(ctx):
+    """A vb_gen step (B = 2: both LM steps on the single-launch decoder)
+    issues no allocation, synchronisation or pageable host copy once a step
+    of the same shape has run, so it can be captured in a vb_graph.  Two
+    generators start from the same prompt; after one eager step on each, the
+    second step runs eagerly on the first and is captured on the second:
+    one replay of the graph gives the same patches, stop logits and
+    last_lm_hidden bit for bit."""
+    m = Model(ctx, O.TYPE_Q8_0)
+    parts = m.device_parts()
+    B, T, seed = 2, 6, 2024
+    embeds = dev(O.bf16_round(S.normal((B, T, H), 0.5)))
+    ga = vb.Gen(ctx, parts, B, 32)
+    gb = vb.Gen(ctx, parts, B, 32)
+    ga.prefill(T, embeds)
+    gb.prefill(T, embeds)
+    for g in (ga, gb):
+        g.step(seed, zeros((B, PATCH, FEAT)), zeros((B, 2)))
+    pa, sa, ha = zeros((B, PATCH, FEAT)), zeros((B, 2)), zeros((B, H))
+    ga.step(seed, pa, sa)
+    ga.state(vb.GEN_LAST_LM_HIDDEN, ha)
+    pb, sb, hb = zeros((B, PATCH, FEAT)), zeros((B, 2)), zeros((B, H))
+    ctx.sync()
+    ctx.graph_begin()
+    gb.step(seed, pb, sb)
+    graph = ctx.graph_end()
+    ctx.graph_launch(graph)
+    gb.state(vb.GEN_LAST_LM_HIDDEN, hb)
+    ctx.sync()
+    assert np.array_equal(pa.cpu().numpy(), pb.cpu().numpy())
+    assert np.array_equal(sa.cpu().numpy(), sb.cpu().numpy())
+    assert np.array_equal(ha.cpu().numpy(), hb.cpu().numpy())
+    ctx.graph_destroy(graph)
+    ga.close()
+    gb.close()
+    m.close()

@@ -177,6 +177,10 @@ struct vb_lm {
     std::vector<LayerDev> layers;
     float *final_norm = nullptr;
     size_t weight_bytes = 0;
+    // token tables of vb_lm_forward_noncausal per (segments, segment length):
+    // they depend on the shape only, so they are uploaded once (outside
+    // stream capture) and later calls of that shape copy nothing from the host
+    std::map<std::pair<int, int>, int32_t *> nc_tables;
 };
 
 struct vb_kv {
@@ -220,6 +224,7 @@ static void lm_free(vb_ctx *ctx, vb_lm *lm) {
         cudaFree(L.ffn_norm);
     }
     cudaFree(lm->final_norm);
+    for (auto &t : lm->nc_tables) cudaFree(t.second);
     delete lm;
 }
 
@@ -501,19 +506,41 @@ extern "C" int vb_lm_forward_noncausal(vb_ctx *ctx, vb_lm *lm, int n, int T, flo
     if (!ctx || !lm || n <= 0 || T <= 0 || !h) return VB_ERR_INVALID_ARG;
     const vb_lm_config &c = lm->cfg;
     const int M = n * T;
-    std::vector<int32_t> tab((size_t)4 * M);
-    for (int m = 0; m < M; m++) {
-        tab[m] = m % T;
-        tab[M + m] = m;
-        tab[2 * M + m] = (m / T) * T;
-        tab[3 * M + m] = T;
+    int32_t *d = nullptr;
+    auto it = lm->nc_tables.find(std::make_pair(n, T));
+    if (it != lm->nc_tables.end()) {
+        d = it->second;
+    } else {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        cudaStreamIsCapturing(ctx->stream, &cs);
+        if (cs != cudaStreamCaptureStatusNone)
+            return set_error(ctx, VB_ERR_BACKEND,
+                             "vb_lm_forward_noncausal: the first call of shape (%d, %d) must be made outside stream capture",
+                             n, T);
+        std::vector<int32_t> tab((size_t)4 * M);
+        for (int m = 0; m < M; m++) {
+            tab[m] = m % T;
+            tab[M + m] = m;
+            tab[2 * M + m] = (m / T) * T;
+            tab[3 * M + m] = T;
+        }
+        VB_CHECK(ctx, cudaMalloc(&d, tab.size() * 4));
+        const cudaError_t e = cudaMemcpy(d, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            cudaFree(d);
+            return check_cuda(ctx, e, "vb_lm_forward_noncausal: token tables");
+        }
+        lm->nc_tables[std::make_pair(n, T)] = d;
     }
     const size_t kv_elems = (size_t)c.n_kv_heads * M * c.head_dim;
     int rc = ws_reserve(ctx, layer_ws_bytes(c, M) + 2 * align256(kv_elems * 2) + align256((size_t)16 * M) + 4096);
     if (rc) return rc;
     Carve cv(ctx->ws.ptr);
     TokenTables tt;
-    if ((rc = upload_tables(ctx, cv, M, tab, tt))) return rc;
+    tt.pos = d;
+    tt.dst = d + M;
+    tt.start = d + 2 * M;
+    tt.len = d + 3 * M;
     tt.max_len = T;
     tt.seg_T = T;
     uint16_t *kc = cv.take<uint16_t>(kv_elems);
