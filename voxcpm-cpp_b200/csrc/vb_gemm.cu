@@ -769,6 +769,7 @@ __global__ void __launch_bounds__(ACT_NORM_THREADS) gemm_act_norm_kernel(const f
 // 32*(w%4).. and columns [CW * g, CW * (g+1)) with g = (w-2)/4.  A stage is
 // refilled once its MMAs have completed AND the epilogue has read its scales.
 constexpr int GI_BK = 128;
+constexpr int GI_MIN_M = 3;     // fewest activation rows routed to the int8 kernel (gemm_small_m)
 // NG column groups of CW columns: BN = NG * CW, 4 * NG epilogue warps
 constexpr int gi_threads(int ng) { return 64 + 128 * ng; }
 constexpr int GI_DBUF = 4;
@@ -1433,6 +1434,17 @@ static bool gemm_i8_faster(int64_t M, int64_t K, int64_t N) {
     return M <= 256 || (M <= 512 && N <= 2560) || (M <= 768 && K >= 3 * N);
 }
 
+// Q8_0 with 3 <= M < 16 activation rows (decode steps of a few utterances):
+// the int8 kernel with its narrowest tile (32 activation rows, the absent
+// ones zero-filled by TMA and never stored).  It streams each weight once
+// at the tensor cores' pace, where the M <= 8 weight-streaming op and the
+// GEMV kernels pay per activation row (B200, 28-layer decode step: M = 8
+// 9.0 ms per token on those, 4.2 ms at M = 16 on this kernel).
+bool gemm_small_m(const vb_ctx *ctx, vb_weight w, int64_t M) {
+    return ctx->gemm_i8 != 0 && w->type == VB_TYPE_Q8_0 && M >= GI_MIN_M && M < 16 && w->K % GI_BK == 0 &&
+           encode_fn() != nullptr;
+}
+
 bool gemm_supported(vb_weight w, int64_t M) {
     if (M < 16 || !encode_fn()) return false;
     if (w->type == VB_TYPE_Q8_0) return w->K % GM_BK == 0;
@@ -1443,7 +1455,7 @@ bool gemm_supported(vb_weight w, int64_t M) {
 int launch_gemm(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx, int64_t x_mod,
                 const MatmulOut &out, const GemmPro *pro) {
     if (w->type == VB_TYPE_Q8_0 && w->K % GI_BK == 0 &&
-        (ctx->gemm_i8 == 2 || (ctx->gemm_i8 == 1 && gemm_i8_faster(M, w->K, w->N))))
+        (gemm_small_m(ctx, w, M) || ctx->gemm_i8 == 2 || (ctx->gemm_i8 == 1 && gemm_i8_faster(M, w->K, w->N))))
         return launch_gemm_i8(ctx, w, x, M, ldx, x_mod, out, pro);
     GemmState *gs = gemm_state(ctx);
     if (!gs) return set_error(ctx, VB_ERR_OOM, "gemm: state allocation failed");

@@ -267,7 +267,9 @@ int init_gemv(vb_ctx *ctx) {
 
 static size_t q8_smem(int mc, int64_t K) { return (size_t)((mc * K + 15) & ~15) + (size_t)mc * (K / QK) * 4; }
 
-bool matmul_uses_gemm(vb_ctx *ctx, vb_weight w, int64_t M) { return ctx->use_gemm && gemm_supported(w, M); }
+bool matmul_uses_gemm(vb_ctx *ctx, vb_weight w, int64_t M) {
+    return ctx->use_gemm && (gemm_supported(w, M) || gemm_small_m(ctx, w, M));
+}
 
 int launch_matmul_pro(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t ldx, const GemmPro &pro,
                       const MatmulOut &out_in) {
@@ -287,7 +289,7 @@ int launch_matmul(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t l
     MatmulOut out = out_in;
     if (out.ldy == 0) out.ldy = w->N;
     if (out.seg == 0) { out.seg = M; out.seg_stride = 0; out.seg_off = 0; }
-    if (ctx->use_gemm && gemm_supported(w, M)) return launch_gemm(ctx, w, x, M, ldx, x_mod, out);
+    if (matmul_uses_gemm(ctx, w, M)) return launch_gemm(ctx, w, x, M, ldx, x_mod, out);
     {
         // small M on Q8_0 / F16: the weight-streaming kernel as a single op
         const int rc = launch_stream1(ctx, w, x, M, ldx ? ldx : w->K, x_mod > 0 ? x_mod : M, out);

@@ -37,6 +37,7 @@ int launch_matmul(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, int64_t l
 
 // Tensor-core path for M >= 16 (vb_gemm.cu); launch_matmul dispatches to it.
 bool gemm_supported(vb_weight w, int64_t M);
+bool gemm_small_m(const vb_ctx *ctx, vb_weight w, int64_t M);
 // Prologue fused into the tensor-core path's activation operand: norm_w set
 // -> the operand is vcpm_rms_norm(x) with weight norm_w and bf16 rounding;
 // swiglu_f > 0 -> x rows are [gate (F) | up (F)] (ldx 0 means 2F) and the
