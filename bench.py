@@ -735,6 +735,51 @@ def run_launches_case(args, local_rank):
     return 0 if rc == 0 else 1
 
 
+def run_kernels_case(args, local_rank):
+    """Profiling case: per-kernel device time of one end-to-end patch step
+    (CUPTI activity records through torch.profiler).  The end-to-end section
+    runs twice, with args.e2e_patches and with args.e2e_patches + 8 patches;
+    the difference of the two kernel totals divided by 8 is one patch step
+    (prompt, warm-up and setup cancel).  Kernels launched as programmatic
+    dependents start before their predecessor ends, so their records include
+    that wait: compare shares, and the step's event time for the total."""
+    import argparse
+    import torch
+    import vcpm_b200 as vb
+    from torch.profiler import profile, ProfilerActivity
+    torch.cuda.set_device(local_rank)
+    ctx = vb.Context(local_rank)
+    rng = np.random.default_rng(1234)
+    host_layers = [{name: synth_q8_0(rng, N, K) for name, K, N, _ in SHAPES} for _ in range(LAYERS)]
+    totals, step_ms = [], None
+    for np_ in (args.e2e_patches, args.e2e_patches + 8):
+        a = argparse.Namespace(e2e_utts=args.e2e_utts, e2e_patches=np_, e2e_clock_ms=args.e2e_clock_ms,
+                               no_e2e_stop=True, no_cpu=True, steps=1, warmup=args.warmup)
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            r = e2e_bench(ctx, host_layers, a, 0, 1, local_rank)
+        step_ms = r["per_patch_ms"]
+        tot = {}
+        for e in prof.events():
+            if e.device_type.name == "CUDA":
+                t = tot.setdefault(e.name, [0, 0.0])
+                t[0] += 1
+                t[1] += e.device_time_total
+        totals.append(tot)
+    a, b = totals
+    per = {k: ((b[k][0] - a.get(k, [0, 0])[0]) / 8.0, (b[k][1] - a.get(k, [0, 0])[1]) / 8.0 / 1e3) for k in b}
+    # kernels only (the copies that differ between the runs are the larger
+    # run's setup: its KV caches hold 8 more positions)
+    per = {k: v for k, v in per.items() if v[1] > 0 and not k.startswith("Mem")}
+    tot_ms = sum(v[1] for v in per.values())
+    rows = [{"kernel": k.replace("(anonymous namespace)::", "").split("(")[0], "launches": round(v[0], 1), "ms": round(v[1], 3), "share": round(v[1] / tot_ms, 4)}
+            for k, v in sorted(per.items(), key=lambda kv: -kv[1][1])]
+    rc, derr = ctx.device_status()
+    print(json.dumps({"mode": "kernels", "utterances": args.e2e_utts, "step_ms": step_ms, "kernel_ms_sum": tot_ms,
+                      "kernels": rows[:24], "device_error": derr}), flush=True)
+    ctx.close()
+    return 0 if rc == 0 else 1
+
+
 def run_decode_case(args, local_rank):
     """Profiling case: the 28-layer decode step (vb_decoder_step, one
     persistent launch per token) after a 256-token prefill; warmup + steps
@@ -1230,7 +1275,7 @@ def main():
     ap.add_argument("--e2e-utts", type=int, default=64)
     ap.add_argument("--e2e-patches", type=int, default=100)
     ap.add_argument("--e2e-clock-ms", type=int, default=500, help="nvidia-smi sampling period during the e2e run")
-    ap.add_argument("--mode", default="full", choices=["full", "config1", "gemm", "decode", "vae", "launches"],
+    ap.add_argument("--mode", default="full", choices=["full", "config1", "gemm", "decode", "vae", "launches", "kernels"],
                     help="config1 / gemm / decode: small profiling cases (config-1 streaming program, one "
                          "tensor-core mat-mul shape, the single-launch decode step)")
     ap.add_argument("--gemm-shape", default="1408,1024,8192")
@@ -1256,6 +1301,8 @@ def main():
         return run_decode_case(args, local_rank)
     if args.mode == "launches":
         return run_launches_case(args, local_rank)
+    if args.mode == "kernels":
+        return run_kernels_case(args, local_rank)
     if world > 1:
         import datetime
         import torch
