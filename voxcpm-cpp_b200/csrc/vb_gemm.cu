@@ -1258,6 +1258,8 @@ int init_gemm(vb_ctx *ctx) {
                                        GM_SMEM_BUDGET + 1024));
     VB_CHECK(ctx, cudaFuncSetAttribute(gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        GM_SMEM_BUDGET + 1024));
+    VB_CHECK(ctx, cudaFuncSetAttribute(gemm_i8_kernel<8, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       GM_SMEM_BUDGET + 1024));
     VB_CHECK(ctx, cudaFuncSetAttribute(gemm_i8_kernel<8, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        GM_SMEM_BUDGET + 1024));
     VB_CHECK(ctx, cudaFuncSetAttribute(gemm_i8_kernel<16, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1305,7 +1307,10 @@ static int launch_gemm_i8(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, i
     double best = 1e300;
     // (BN = 96: three column groups of 32, twelve epilogue warps -- with 4
     // groups of 32 the register budget of 16 epilogue warps spills)
-    for (int cand : {96, 64, 32}) {
+    // (BN = 16, two column groups of 8, for M <= 16 only: the narrowest
+    // MMA, half the epilogue warps of BN = 32 and no fold of absent rows)
+    for (int cand : {96, 64, 32, 16}) {
+        if (cand == 16 && mr > 16) continue;
         if (cand > 32 && cand > mr && (cand == 96 ? 64 : cand >> 1) >= mr) continue;
         const int64_t tiles = (int64_t)tiles_n * ((M + cand - 1) / cand);
         for (int sp = 1; sp <= std::max(1, kt_total / 2); sp++) {
@@ -1419,8 +1424,9 @@ static int launch_gemm_i8(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, i
     const int n_work = tiles * splits;
     const CUtensorMap &twm = *reinterpret_cast<const CUtensorMap *>(w->tmap_i8);
     void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmArgs) =
-        BN == 96 ? gemm_i8_kernel<32, 3> : BN == 64 ? gemm_i8_kernel<16, 4> : gemm_i8_kernel<8, 4>;
-    const int threads = gi_threads(BN == 96 ? 3 : 4);
+        BN == 96 ? gemm_i8_kernel<32, 3>
+                 : BN == 64 ? gemm_i8_kernel<16, 4> : BN == 32 ? gemm_i8_kernel<8, 4> : gemm_i8_kernel<8, 2>;
+    const int threads = gi_threads(BN == 96 ? 3 : BN == 16 ? 2 : 4);
     VB_CHECK(ctx, pdl_launch(ctx, kern, dim3((unsigned)std::min(n_work, ctx->sm_count)), dim3(threads), smem, twm,
                              am->th, am->tl, g));
     VB_LAUNCH_CHECK(ctx, "gemm_i8");
