@@ -178,6 +178,51 @@ int launch_kv_write(vb_ctx *ctx, const float *k, const float *v, int64_t ldkv, u
     return VB_OK;
 }
 
+// RoPE of the q and k heads of a fused qkv row and the bf16 K/V append, as
+// one launch: item (t, head, pair p) of the n_heads query heads rotates
+// the pair in place; of the n_kv key heads it rotates the pair in place and
+// stores it with the matching value pair into the caches.  The same
+// rounding as rope_kernel followed by kv_write_kernel (bf16 rotated values,
+// then their bf16 bits).
+__global__ void rope_kv_kernel(float *qkv, int64_t ld, int64_t kd, int head_dim, int n_heads, int n_kv, int T,
+                               const int32_t *pos, const float *cs, uint16_t *kc, uint16_t *vc, int n_rows,
+                               const int32_t *dst_row) {
+    const int half = head_dim >> 1;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t total = (int64_t)T * (n_heads + n_kv) * half;
+    if (i >= total) return;
+    const int p = (int)(i % half);
+    const int hh = (int)((i / half) % (n_heads + n_kv));
+    const int t = (int)(i / ((int64_t)half * (n_heads + n_kv)));
+    float *row = qkv + (int64_t)t * ld;
+    float *v = row + (int64_t)hh * head_dim;   // q heads, then k heads (k follows q in the row)
+    const float *c = cs + (int64_t)pos[t] * head_dim + 2 * p;
+    const float cv = c[0], sv = c[1];
+    const float x0 = v[p], x1 = v[p + half];
+    const float r0 = bf16r(__fsub_rn(__fmul_rn(x0, cv), __fmul_rn(x1, sv)));
+    const float r1 = bf16r(__fadd_rn(__fmul_rn(x0, sv), __fmul_rn(x1, cv)));
+    v[p] = r0;
+    v[p + half] = r1;
+    if (hh < n_heads) return;
+    const int g = hh - n_heads;
+    const float *vv = row + (int64_t)n_heads * head_dim + kd + (int64_t)g * head_dim;
+    const int64_t dst = ((int64_t)g * n_rows + dst_row[t]) * head_dim;
+    kc[dst + p] = bf16_bits(r0);
+    kc[dst + p + half] = bf16_bits(r1);
+    vc[dst + p] = bf16_bits(vv[p]);
+    vc[dst + p + half] = bf16_bits(vv[p + half]);
+}
+
+int launch_rope_kv(vb_ctx *ctx, float *qkv, int64_t ld, int64_t kd, int head_dim, int n_heads, int n_kv, int T,
+                   const int32_t *pos, const float *cs, uint16_t *kc, uint16_t *vc, int n_rows, const int32_t *dst_row) {
+    const int64_t total = (int64_t)T * (n_heads + n_kv) * (head_dim / 2);
+    if (total == 0) return VB_OK;
+    rope_kv_kernel<<<(unsigned)((total + 255) / 256), 256, 0, ctx->stream>>>(qkv, ld, kd, head_dim, n_heads, n_kv, T,
+                                                                             pos, cs, kc, vc, n_rows, dst_row);
+    VB_LAUNCH_CHECK(ctx, "rope_kv");
+    return VB_OK;
+}
+
 __global__ void fill_kernel(float *x, float v, int64_t n) {
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) x[i] = v;

@@ -104,6 +104,10 @@ int launch_fsq(vb_ctx *ctx, float *x, int64_t n, float s);
 // positions pos[t]; table cs [max_pos][head_dim].
 int launch_rope(vb_ctx *ctx, float *x, int64_t ldx, int head_dim, int n_heads, int T, const int32_t *pos,
                 const float *cs, unsigned flags);
+// RoPE of q and k (bf16) and the bf16 K/V append in one launch; kd = the
+// k block's width (v starts kd after k in a row).
+int launch_rope_kv(vb_ctx *ctx, float *qkv, int64_t ld, int64_t kd, int head_dim, int n_heads, int n_kv, int T,
+                   const int32_t *pos, const float *cs, uint16_t *kc, uint16_t *vc, int n_rows, const int32_t *dst_row);
 int launch_kv_write(vb_ctx *ctx, const float *k, const float *v, int64_t ldkv, uint16_t *kc, uint16_t *vc,
                     int n_rows, int T, int n_kv, int head_dim, const int32_t *dst_row);
 int launch_fill(vb_ctx *ctx, float *x, float v, int64_t n);

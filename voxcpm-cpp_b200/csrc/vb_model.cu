@@ -363,13 +363,16 @@ static int run_layers(vb_ctx *ctx, vb_lm *lm, int M, float *h, const TokenTables
         }
         dumpf(ctx, qkv, QKV, M, "L%d.qkv", l);
         if (!c.no_rope) {
-            if ((rc = launch_rope(ctx, qkv, QKV, c.head_dim, c.n_heads, M, tt.pos, cs, VB_OUT_BF16))) return rc;
-            if ((rc = launch_rope(ctx, qkv + QD, QKV, c.head_dim, c.n_kv_heads, M, tt.pos, cs, VB_OUT_BF16))) return rc;
+            if ((rc = launch_rope_kv(ctx, qkv, QKV, KD, c.head_dim, c.n_heads, c.n_kv_heads, M, tt.pos, cs, kc, vc,
+                                     kv_rows, tt.dst)))
+                return rc;
+            dumpf(ctx, qkv, QKV, M, "L%d.qkv_rope", l);
+        } else {
+            dumpf(ctx, qkv, QKV, M, "L%d.qkv_rope", l);
+            if ((rc = launch_kv_write(ctx, qkv + QD, qkv + QD + KD, QKV, kc, vc, kv_rows, M, c.n_kv_heads,
+                                      c.head_dim, tt.dst)))
+                return rc;
         }
-        dumpf(ctx, qkv, QKV, M, "L%d.qkv_rope", l);
-        if ((rc = launch_kv_write(ctx, qkv + QD, qkv + QD + KD, QKV, kc, vc, kv_rows, M, c.n_kv_heads, c.head_dim,
-                                  tt.dst)))
-            return rc;
         if (tt.seg_T > 0 && tt.seg_T <= 32 && c.head_dim % 32 == 0) {
             if ((rc = launch_attention_segments(ctx, qkv, QKV, kc, vc, kv_rows, M / tt.seg_T, tt.seg_T, c.n_heads,
                                                 c.n_kv_heads, c.head_dim, att, QD)))
