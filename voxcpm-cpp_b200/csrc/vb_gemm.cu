@@ -1317,7 +1317,10 @@ static int launch_gemm_i8(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, i
             const int kps = (kt_total + sp - 1) / sp;
             const int64_t units = tiles * ((kt_total + kps - 1) / kps);
             const int64_t waves = (units + ctx->sm_count - 1) / ctx->sm_count;
-            const double t = (double)waves * ((double)cand * kps + 256.0) + (sp > 1 ? 8.0 * sp * cand : 0.0);
+            // split price: the last CTA of a tile adds every split's partials
+            // (measured on B200 for M = 8 .. 704: 1 x splits x BN picks the
+            // fastest tile and split of every swept shape)
+            const double t = (double)waves * ((double)cand * kps + 256.0) + (sp > 1 ? 1.0 * sp * cand : 0.0);
             if (t < best * 0.999) { best = t; BN = cand; splits = sp; }
             if (units >= 4 * ctx->sm_count) break;
         }
