@@ -1437,10 +1437,11 @@ static int launch_gemm_i8(vb_ctx *ctx, vb_weight w, const float *x, int64_t M, i
 }
 
 // Where the int8 kernel beats the fp16 split kernel (B200 sweep of the
-// MiniCPM4 projection shapes, M = 64 .. 4096): its epilogue work grows with
-// M x N x K/32 while the split kernel's fixed per-call cost falls away.
+// MiniCPM4 and LocDiT projection shapes, M = 128 .. 1408): its epilogue work
+// grows with M x N x K/32 while the split kernel's fixed per-call cost falls
+// away, and the split kernel is weakest on long-K, narrow-N shapes.
 static bool gemm_i8_faster(int64_t M, int64_t K, int64_t N) {
-    return M <= 256 || (M <= 512 && N <= 2560) || (M <= 768 && K >= 3 * N);
+    return M <= 256 || (K >= 3 * N && M <= 1536) || (double)M * (double)N * (double)K <= 3.3e9;
 }
 
 // Q8_0 with 3 <= M < 16 activation rows (decode steps of a few utterances):
