@@ -168,7 +168,8 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) attn_segment_kernel(AttnArgs a
         vs[i] = bf16_to_f(a.v[base + i]);
     }
     __syncthreads();
-    for (int pr = warp; pr < T * qpk; pr += ATT_WARPS) {
+    // blockIdx.z picks this CTA's ATT_WARPS (token, head) rows of the segment
+    for (int pr = blockIdx.z * ATT_WARPS + warp; pr < T * qpk; pr += ATT_WARPS * gridDim.z) {
         const int t = pr / qpk, h = g * qpk + pr % qpk;
         const int64_t tok = (int64_t)sgi * T + t;
         const float *qr = a.q + tok * a.ldq + (int64_t)h * HD;
@@ -269,7 +270,12 @@ int launch_attention_segments(vb_ctx *ctx, const float *q, int64_t ldq, const ui
     a.out = out;
     a.ldo = ldo ? ldo : (int64_t)n_heads * head_dim;
     a.kq_scale = 1.0f / sqrtf((float)head_dim);
-    const dim3 grid((unsigned)n_kv, (unsigned)n_seg);
+    // one warp per (token, query head) row: the rows of a segment and KV
+    // group are spread over ceil(T * heads-per-group / ATT_WARPS) CTAs, each
+    // staging the group's K/V rows itself (a few KB from L2), so a small
+    // batch still fills the GPU
+    const int rows = T * (n_heads / n_kv);
+    const dim3 grid((unsigned)n_kv, (unsigned)n_seg, (unsigned)((rows + ATT_WARPS - 1) / ATT_WARPS));
     switch (head_dim / 32) {
         case 1: attn_segment_kernel<1><<<grid, ATT_WARPS * 32, sm, ctx->stream>>>(a, T); break;
         case 2: attn_segment_kernel<2><<<grid, ATT_WARPS * 32, sm, ctx->stream>>>(a, T); break;
