@@ -24,6 +24,7 @@ namespace vb {
 constexpr int ATT_CH = 64;         // K/V rows per CTA
 constexpr int ATT_WARPS = 8;
 constexpr int ATT_HD_MAX = 256;
+constexpr int ATT_LD = 4;           // 16-byte K and V loads per thread in flight while staging a chunk
 
 struct AttnArgs {
     const float *q;
@@ -63,10 +64,38 @@ __global__ void __launch_bounds__(ATT_WARPS * 32) attn_chunk_kernel(AttnArgs a) 
     const int64_t base = ((int64_t)g * a.n_rows + a.row_start[t] + p0) * HW;
     const uint32_t *kg = reinterpret_cast<const uint32_t *>(a.k) + base;
     const uint32_t *vg = reinterpret_cast<const uint32_t *>(a.v) + base;
-    for (int i = threadIdx.x; i < n * HW; i += blockDim.x) {
-        const int r = i / HW, w = i % HW;
-        ks[r * rw + w] = __ldg(kg + i);
-        vs[r * rw + w] = __ldg(vg + i);
+    if ((HW & 3) == 0) {
+        // 16-byte loads, a batch of ATT_LD per thread in flight before any
+        // store (rows are 16-byte aligned in global memory, padded in shared)
+        const uint4 *kg4 = reinterpret_cast<const uint4 *>(kg), *vg4 = reinterpret_cast<const uint4 *>(vg);
+        const int w4 = (n * HW) >> 2;
+        for (int i0 = threadIdx.x; i0 < w4; i0 += ATT_LD * blockDim.x) {
+            uint4 kk[ATT_LD], vv[ATT_LD];
+#pragma unroll
+            for (int u = 0; u < ATT_LD; u++) {
+                const int i = i0 + u * blockDim.x;
+                if (i < w4) {
+                    kk[u] = __ldg(kg4 + i);
+                    vv[u] = __ldg(vg4 + i);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < ATT_LD; u++) {
+                const int i = i0 + u * blockDim.x;
+                if (i < w4) {
+                    const int r = (4 * i) / HW, w = (4 * i) % HW;
+                    uint32_t *kd = ks + r * rw + w, *vd = vs + r * rw + w;
+                    kd[0] = kk[u].x; kd[1] = kk[u].y; kd[2] = kk[u].z; kd[3] = kk[u].w;
+                    vd[0] = vv[u].x; vd[1] = vv[u].y; vd[2] = vv[u].z; vd[3] = vv[u].w;
+                }
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < n * HW; i += blockDim.x) {
+            const int r = i / HW, w = i % HW;
+            ks[r * rw + w] = __ldg(kg + i);
+            vs[r * rw + w] = __ldg(vg + i);
+        }
     }
     for (int i = threadIdx.x; i < qpk * HD; i += blockDim.x) {
         const int j = i / HD, d = i % HD;
