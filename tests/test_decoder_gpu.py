@@ -138,14 +138,17 @@ def test_decoder_batched_slots_match_oracle(ctx):
     lm.close()
 
 
-@pytest.mark.parametrize("wtype,n", [(O.TYPE_Q8_0, 1), (O.TYPE_Q8_0, 2), (O.TYPE_F16, 1)])
+@pytest.mark.parametrize("wtype,n", [(O.TYPE_Q8_0, 1), (O.TYPE_Q8_0, 2), (O.TYPE_Q8_0, 4), (O.TYPE_Q8_0, 8),
+                                     (O.TYPE_F16, 1), (O.TYPE_F16, 2)])
 def test_decoder_full_width_agrees_with_per_op_path(ctx, wtype, n):
     """Projection shapes of the MiniCPM4 decode benchmark (hidden 2048, 16q/2kv,
     head_dim 128, FFN 6144) on two blocks: 40 steps through the decoder and,
     on a second cache, through vb_lm_forward(T = 1); the 40 steps cross the
-    32- and 64-row attention chunk boundaries.  F16 (n = 1: two rows of an
-    F16 K = 6144 operand exceed the streaming kernel's 16 KiB) runs the FFN
-    down projection (residual epilogue) with several warps per row."""
+    32- and 64-row attention chunk boundaries.  F16 at n = 1 runs the FFN
+    down projection (residual epilogue) with several warps per row; operands
+    wider than 16 KiB (Q8_0 n = 4 and 8, F16 n = 2: several rows of the
+    K = 6144 down projection) take a larger operand buffer in place of ring
+    stages."""
     c, lm, _, _, _ = build_lm(ctx, wtype, oracle=False, hidden=2048, n_heads=16, n_kv=2, head_dim=128,
                               ffn=6144, n_layers=2)
     H, T = c["hidden"], 5

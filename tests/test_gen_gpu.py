@@ -177,9 +177,9 @@ class Model:
         return patches, stops
 
 
-@pytest.mark.parametrize("B", [3, 2])
+@pytest.mark.parametrize("B", [5, 2])
 def test_generation_loop_matches_oracle(ctx, B):
-    """B=3 runs the TSLM/RALM steps through the per-op path, B=2 through the
+    """B=5 runs the TSLM/RALM steps through the per-op path, B=2 through the
     single-launch decoder."""
     m = Model(ctx, O.TYPE_Q8_0)
     parts = m.device_parts()
@@ -208,7 +208,7 @@ def test_generation_loop_matches_oracle(ctx, B):
     m.close()
 
 
-@pytest.mark.parametrize("B", [3, 2])
+@pytest.mark.parametrize("B", [5, 2])
 def test_stop_predictor_and_termination(ctx, B):
     """The gen_run loop on the device: every step the stop logits, class and
     flag are those of the oracle's gen_predict_stop on the device's own

@@ -36,15 +36,15 @@ namespace vb {
 __global__ void __launch_bounds__(ST_THREADS, 1)
     stream_gemv_kernel(const StreamOp *__restrict__ ops, const int2 *__restrict__ rows,
                        const uint16_t *__restrict__ idx, const int *__restrict__ counts, int n_ops, unsigned *bars,
-                       int *err, const StreamStep step, const int ns, const long long dep_limit) {
+                       int *err, const StreamStep step, const int ns, const long long dep_limit, const int xbytes) {
     extern __shared__ __align__(128) uint8_t sm[];
     uint8_t *wslot = sm;
     uint8_t *sslot = wslot + (size_t)ns * ST_SLOT;
     int8_t *xq = reinterpret_cast<int8_t *>(sslot + (size_t)ns * ST_SC_SLOT);
-    float *xd = reinterpret_cast<float *>(xq + ST_XBYTES);
-    uint64_t *full = reinterpret_cast<uint64_t *>(xd + ST_XBYTES / 32);
+    float *xd = reinterpret_cast<float *>(xq + xbytes);
+    uint64_t *full = reinterpret_cast<uint64_t *>(xd + xbytes / 32);
     uint64_t *empty = full + ST_STAGES_MAX;
-    uint8_t *aux = sm + st_smem(ns, false);          // non-GEMV op scratch (aux programs only)
+    uint8_t *aux = sm + st_smem(ns, false, xbytes);  // non-GEMV op scratch (aux programs only)
     __shared__ volatile int s_abort;
     __shared__ int s_step[ST_MMAX * 4];
     __shared__ StreamOp s_ops[2];
@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(ST_THREADS, 1)
     // scratch, past what the prologues use; programs without aux skip it)
     uint32_t dyn_smem;
     asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn_smem));
-    float *s_res = dyn_smem >= st_smem(ns, true) ? reinterpret_cast<float *>(aux + ST_RES_OFF) : nullptr;
+    float *s_res = dyn_smem >= st_smem(ns, true, xbytes) ? reinterpret_cast<float *>(aux + ST_RES_OFF) : nullptr;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x, cta = blockIdx.x;
@@ -454,8 +454,8 @@ int stream_gemv_geometry(vb_ctx *ctx, StreamOp &s, int i) {
     if (s.rows_per_chunk < 1 || s.row_bytes % 16)
         return set_error(ctx, VB_ERR_INVALID_ARG, "program op %d: K=%d not supported by the streaming kernel", i, s.K);
     const int xbytes = (s.wtype == VB_TYPE_Q8_0 ? 1 : 2) * s.K * s.M;
-    if (xbytes > ST_XBYTES)
-        return set_error(ctx, VB_ERR_INVALID_ARG, "program op %d: M*K operand exceeds %d bytes", i, ST_XBYTES);
+    if (xbytes > ST_XBYTES_MAX)
+        return set_error(ctx, VB_ERR_INVALID_ARG, "program op %d: M*K operand exceeds %d bytes", i, ST_XBYTES_MAX);
     if (s.wtype == VB_TYPE_Q8_0 && (s.K % QK))
         return set_error(ctx, VB_ERR_INVALID_ARG, "program op %d: Q8_0 K=%d is not a multiple of 32", i, s.K);
     return VB_OK;
@@ -471,6 +471,7 @@ struct vb_program_s {
     int *d_err = nullptr;
     int n_ops = 0, n_groups = 0, n_counters = 0, grid = 0;
     int stages = 0;               // ring depth of this program's launches
+    int xbytes = 0;               // activation operand buffer bytes
     size_t smem = 0;              // dynamic shared memory per CTA
     size_t weight_bytes = 0;
 };
@@ -485,8 +486,27 @@ static size_t st1_smem(int xq_bytes) {
            2 * ST_STAGES_MAX * 8 + 64;
 }
 
+// Dynamic shared memory a streaming launch may use: the device's opt-in
+// maximum per block less the kernel's static shared memory (the same on
+// every B200).
+static int stream_smem_limit() {
+    static int limit = 0;
+    if (limit == 0) {
+        int optin = 0, dev = 0;
+        cudaFuncAttributes fa{};
+        if (cudaGetDevice(&dev) == cudaSuccess &&
+            cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) == cudaSuccess &&
+            cudaFuncGetAttributes(&fa, stream_gemv_kernel) == cudaSuccess && optin > (int)fa.sharedSizeBytes)
+            limit = optin - (int)fa.sharedSizeBytes;
+        else
+            limit = (int)ST_SMEM_ALL;
+    }
+    return limit;
+}
+
 int init_stream(vb_ctx *ctx) {
-    VB_CHECK(ctx, cudaFuncSetAttribute(stream_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ST_SMEM_ALL));
+    VB_CHECK(ctx, cudaFuncSetAttribute(stream_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       stream_smem_limit()));
     VB_CHECK(ctx, cudaFuncSetAttribute(stream_gemv1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)st1_smem(ST_XBYTES)));
     // all of the SM's unified memory as shared memory, so two CTAs fit (one of
@@ -617,8 +637,20 @@ int stream_program_build(vb_ctx *ctx, std::vector<StreamOp> ops, int n_groups, i
     // prologue) need no aux scratch and run a deeper ring.
     bool aux = false;
     for (const StreamOp &op : ops) aux = aux || op.kind != OPK_GEMV || op.pro == PRO_RMSNORM;
-    const int stages = aux ? ST_STAGES_AUX : ST_STAGES_MAX;
-    const size_t smem = st_smem(stages, aux);
+    // The activation operand buffer: 16 KB, or the widest op's M * K
+    // bytes (decode steps of several sequences through a K = 6144 down
+    // projection), paid for with ring stages when shared memory runs short.
+    int xbytes = ST_XBYTES;
+    for (const StreamOp &op : ops)
+        if (op.kind == OPK_GEMV) {
+            const int xb = (((op.wtype == VB_TYPE_Q8_0 ? 1 : 2) * op.K * op.M) + 127) & ~127;
+            xbytes = xb > xbytes ? xb : xbytes;
+        }
+    int stages = aux ? ST_STAGES_AUX : ST_STAGES_MAX;
+    while (stages > 2 && st_smem(stages, aux, xbytes) > (size_t)stream_smem_limit()) stages--;
+    const size_t smem = st_smem(stages, aux, xbytes);
+    if (smem > (size_t)stream_smem_limit())
+        return set_error(ctx, VB_ERR_INVALID_ARG, "stream program: a %d-byte activation operand does not fit", xbytes);
     int per_sm = 0;
     VB_CHECK(ctx, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stream_gemv_kernel, ST_THREADS, smem));
     if (per_sm < 1) return set_error(ctx, VB_ERR_BACKEND, "streaming kernel does not fit on an SM");
@@ -628,6 +660,7 @@ int stream_program_build(vb_ctx *ctx, std::vector<StreamOp> ops, int n_groups, i
     p->n_counters = n_counters;
     p->grid = ctx->sm_count;
     p->stages = stages;
+    p->xbytes = xbytes;
     p->smem = smem;
     p->weight_bytes = weight_bytes;
     cudaError_t e = cudaMalloc(&p->d_ops, sizeof(StreamOp) * ops.size());
@@ -666,7 +699,7 @@ int stream_program_launch(vb_ctx *ctx, vb_program p, const StreamStep &step) {
     VB_CHECK(ctx, cudaLaunchKernelEx(&cfg, stream_gemv_kernel, (const StreamOp *)p->d_ops, (const int2 *)p->d_rows,
                                      (const uint16_t *)p->d_idx, (const int *)p->d_counts, p->n_ops, p->d_bars,
                                      p->d_err, step, p->stages,
-                                     ctx->dep_wait_limit > 0 ? ctx->dep_wait_limit : WAIT_LIMIT_CYCLES));
+                                     ctx->dep_wait_limit > 0 ? ctx->dep_wait_limit : WAIT_LIMIT_CYCLES, p->xbytes));
     VB_LAUNCH_CHECK(ctx, "stream_gemv");
     return VB_OK;
 }

@@ -73,7 +73,8 @@ constexpr int ST_SC_SLOT = ST_SLOT / 16;        // Q8_0 scale bytes per stage
 constexpr int ST_CONSUMER_WARPS = 8;
 constexpr int ST_CONSUMERS = ST_CONSUMER_WARPS * 32;
 constexpr int ST_THREADS = ST_CONSUMERS + 32;
-constexpr int ST_XBYTES = 16384;                // activation operand (int8 or fp16)
+constexpr int ST_XBYTES = 16384;                // activation operand (int8 or fp16) of most programs
+constexpr int ST_XBYTES_MAX = 65536;            // widest operand a program may size its buffer to (M * K * bytes)
 constexpr int ST_MMAX = 8;
 constexpr int ST_MAX_OPS = 384;                 // ops per program (row table in shared memory)
 constexpr int ST_RES_ROWS = 256;                // residual rows fetched ahead (M = 1 ops) ...
@@ -88,8 +89,8 @@ static_assert(ST_RES_OFF + 4 * ST_RES_ROWS <= ST_AUX_BYTES, "residual rows in th
 // scale slots, the activation operand, the mbarriers, then (if the program
 // has attention / norm ops or RMSNorm prologues) the aux scratch.  Programs
 // without aux use the freed bytes for a sixth stage (more bytes in flight).
-constexpr size_t st_smem(int ns, bool aux) {
-    return (size_t)ns * ST_SLOT + (size_t)ns * ST_SC_SLOT + ST_XBYTES + (ST_XBYTES / 32) * 4 +
+constexpr size_t st_smem(int ns, bool aux, int xbytes = ST_XBYTES) {
+    return (size_t)ns * ST_SLOT + (size_t)ns * ST_SC_SLOT + (size_t)xbytes + (size_t)(xbytes / 32) * 4 +
            2 * ST_STAGES_MAX * 8 + 64 + (aux ? ST_AUX_BYTES : 0);
 }
 constexpr size_t ST_SMEM_ALL = st_smem(ST_STAGES_MAX, false) > st_smem(ST_STAGES_AUX, true)
