@@ -142,7 +142,8 @@ int vb_matmul_bias(vb_ctx *ctx, vb_weight w, const float *x, int64_t M,
  * one group run concurrently; an op with wait_group >= 0 reads its x only
  * after every op of that earlier group has finished on all SMs.  Groups are
  * numbered 0, 1, 2, ... in op order.  Weights are Q8_0 or F16, 1 <= M <= 8,
- * M*K*(1 or 2 bytes) <= 16384, x rows 16-byte aligned.  Semantics per op
+ * M*K*(1 or 2 bytes) <= 65536 (above 16384 the program trades weight-ring
+ * stages for the wider operand buffer), x rows 16-byte aligned.  Semantics per op
  * are those of vb_matmul_bias. */
 typedef struct {
     vb_weight w;
@@ -315,7 +316,7 @@ int vb_lm_forward_noncausal(vb_ctx *ctx, vb_lm *lm, int n, int T, float *h);
  * reference makes per generated token for the TSLM and the RALM
  * (src/gen_step.c:763, :894).  The decoder binds n KV slots `seq` of `kv`
  * (1 <= n <= 8; n * K bytes of every projection's quantized activation must
- * fit 16 KiB) and owns its buffers, RoPE table (positions below the next
+ * fit 64 KiB) and owns its buffers, RoPE table (positions below the next
  * power of two >= capacity + 1, at least 512) and launch program.  Q8_0 and
  * F16 stacks.  Each step appends one token per slot exactly as
  * vb_lm_forward(n, seq, pos, T = 1) does; results agree with it within the
