@@ -67,12 +67,14 @@ def test_gemm_vs_oracle(ctx, wtype, K, N, M):
     assert S.rel_l2(out, ref) < 2e-5
 
 
+@pytest.mark.parametrize("wtype", [O.TYPE_Q8_0, O.TYPE_F16])
 @pytest.mark.parametrize("K,N,M", [(2048, 2560, 3), (6144, 2048, 8), (2048, 12288, 5), (1024, 200, 15)])
-def test_small_m_int8_vs_oracle(ctx, K, N, M):
-    """Q8_0 with 3 <= M < 16 rows takes the int8 tensor-core kernel (one
-    32-row activation tile, the absent rows zero-filled): ggml's exact block
-    sums, within the mat-mul tolerance of the oracle."""
-    out, ref, _ = run_matmul(ctx, O.TYPE_Q8_0, K, N, M)
+def test_small_m_vs_oracle(ctx, wtype, K, N, M):
+    """3 <= M < 16 rows take the tensor-core kernels with a 16-row tile (the
+    absent rows zero-filled): Q8_0 on the int8 kernel (ggml's exact block
+    sums), F16 on the kind::f16 kernel, within the mat-mul tolerance of the
+    oracle."""
+    out, ref, _ = run_matmul(ctx, wtype, K, N, M)
     S.assert_matmul_close(out, ref, 1e-3)
     assert S.rel_l2(out, ref) < 2e-5
 

@@ -1444,15 +1444,17 @@ static bool gemm_i8_faster(int64_t M, int64_t K, int64_t N) {
     return M <= 256 || (K >= 3 * N && M <= 1536) || (double)M * (double)N * (double)K <= 3.3e9;
 }
 
-// Q8_0 with 3 <= M < 16 activation rows (decode steps of a few utterances):
-// the int8 kernel with its narrowest tile (32 activation rows, the absent
-// ones zero-filled by TMA and never stored).  It streams each weight once
-// at the tensor cores' pace, where the M <= 8 weight-streaming op and the
-// GEMV kernels pay per activation row (B200, 28-layer decode step: M = 8
-// 9.0 ms per token on those, 4.2 ms at M = 16 on this kernel).
+// 3 <= M < 16 activation rows (decode steps of a few utterances) on the
+// tensor cores with a 16-row tile (the absent rows zero-filled by TMA and
+// never stored): Q8_0 on the int8 kernel, F16 on the kind::f16 kernel.
+// Each streams every weight once at the tensor cores' pace, where the
+// M <= 8 weight-streaming op and the GEMV kernels pay per activation row
+// (B200, 28-layer Q8_0 decode step: M = 8 9.0 ms per token on those,
+// 2.8 ms on the int8 kernel).
 bool gemm_small_m(const vb_ctx *ctx, vb_weight w, int64_t M) {
-    return ctx->gemm_i8 != 0 && w->type == VB_TYPE_Q8_0 && M >= GI_MIN_M && M < 16 && w->K % GI_BK == 0 &&
-           encode_fn() != nullptr;
+    if (M < GI_MIN_M || M >= 16 || encode_fn() == nullptr) return false;
+    if (w->type == VB_TYPE_Q8_0) return ctx->gemm_i8 != 0 && w->K % GI_BK == 0;
+    return w->type == VB_TYPE_F16 && w->K % GM_BK == 0;
 }
 
 bool gemm_supported(vb_weight w, int64_t M) {
